@@ -1,0 +1,163 @@
+/*
+ * h3_b200.h -- C-ABI of the B200 (sm_100a) MiniMax-H3 DiT-block hot path.
+ *
+ * Every entry point takes plain descriptors (pointer + shape + element strides),
+ * launches on the caller's CUDA stream and returns an h3_status.  Callers own
+ * every buffer; no entry point allocates device memory.  Validation mirrors the
+ * reference op wrappers (shape/dtype checks that throw std::invalid_argument
+ * there return H3_ERR_BAD_SHAPE / H3_ERR_BAD_DTYPE here), except that widths
+ * are parameters instead of the reference's hard-coded 128/5376.
+ *
+ * Reference interfaces replaced (file:line inside the reference tree):
+ *   h3_rms_norm                    InfiniCore.patch:160 (h3_numerics.hpp), checks :891-900
+ *   h3_swiglu                      InfiniCore.patch:161, checks :909-917
+ *   h3_rms_modulate                InfiniCore.patch:162, checks :928-939
+ *   h3_rope                        InfiniCore.patch:164, checks :948-958
+ *   h3_gated_residual              InfiniCore.patch:165, checks :963-979
+ *   h3_gated_residual_rms_modulate InfiniCore.patch:179-181, checks :992-1004
+ *   h3_qk_norm_rope                InfiniCore.patch:169-170 (h3_qk_norm_rope_), checks :1015-1024
+ *   h3_rope_cache                  InfiniCore.patch:173, checks :1033-1041
+ *   h3_mha                         InfiniCore.patch:1333-1426 (mha_ninetoothed.cc plan/run)
+ *   h3_timestep_embedding          InfiniCore.patch:223-252 (infiniopTimestepEmbedding C API)
+ *   h3_linear*                     InfiniCore.patch:1231-1292 (linear.cc) + the fused
+ *                                  epilogues of InfiniLM.patch:1172-1179, 1377-1394
+ */
+#ifndef H3_B200_H
+#define H3_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define H3_ABI_VERSION 1
+#define H3_MAX_DIMS 4
+
+typedef enum h3_dtype {
+    H3_BF16 = 0,
+    H3_F32 = 1,
+    H3_F64 = 2,
+    H3_I64 = 3
+} h3_dtype;
+
+typedef enum h3_status {
+    H3_OK = 0,
+    H3_ERR_NULL = 1,          /* a required descriptor or data pointer is null   */
+    H3_ERR_BAD_SHAPE = 2,     /* shapes do not match the op's contract           */
+    H3_ERR_BAD_DTYPE = 3,     /* unsupported element type                        */
+    H3_ERR_BAD_LAYOUT = 4,    /* strides/alignment the op cannot address         */
+    H3_ERR_UNSUPPORTED = 5,   /* valid request outside what this build supports  */
+    H3_ERR_LAUNCH = 6,        /* the CUDA launch reported an error               */
+    H3_ERR_DRIVER = 7,        /* a driver entry point could not be resolved      */
+    H3_ERR_TIMEOUT = 8        /* a bounded device-side wait gave up              */
+} h3_status;
+
+/* A strided view.  strides are in ELEMENTS (not bytes); stride 0 broadcasts.
+ * Dimensions past ndim are ignored. */
+typedef struct h3_tensor {
+    void *data;
+    int64_t shape[H3_MAX_DIMS];
+    int64_t strides[H3_MAX_DIMS];
+    int32_t ndim;
+    int32_t dtype; /* h3_dtype */
+} h3_tensor;
+
+int h3_abi_version(void);
+const char *h3_status_string(int status);
+
+/* Synchronises the current device and reports (then clears) whether any bounded
+ * device-side wait gave up since the last call: H3_ERR_TIMEOUT in that case,
+ * H3_ERR_LAUNCH if the device reports an error, else H3_OK.  No reference
+ * counterpart (the reference's waits are unbounded). */
+int h3_device_error(void);
+
+/* ---------------- fused pointwise ops (BF16, reference rounding) ---------------- */
+
+/* y = staged-BF16 RMSNorm(x) * weight over the last axis.  x, y [S,C] or [B,S,C]; weight [C]. */
+int h3_rms_norm(const h3_tensor *y, const h3_tensor *x, const h3_tensor *weight, float eps,
+                void *stream);
+
+/* y = bf16(up * bf16(gate / (1 + exp(-gate)))).  up, gate, y same shape, 2-D or 3-D. */
+int h3_swiglu(const h3_tensor *y, const h3_tensor *up, const h3_tensor *gate, void *stream);
+
+/* y = bf16(bf16(rms_norm(x, weight) * bf16(1 + scale)) + shift).  scale/shift have
+ * x's shape (stride 0 broadcasts a modulation row over tokens). */
+int h3_rms_modulate(const h3_tensor *y, const h3_tensor *x, const h3_tensor *weight,
+                    const h3_tensor *scale, const h3_tensor *shift, float eps, void *stream);
+
+/* LayerNorm (mean-subtracted, no affine, fp32 statistics, one BF16 rounding)
+ * followed by the same modulate.  Builder extension, no reference counterpart. */
+int h3_ln_modulate(const h3_tensor *y, const h3_tensor *x, const h3_tensor *scale,
+                   const h3_tensor *shift, float eps, void *stream);
+
+/* out = bf16(x + bf16(gate * y)); gate may broadcast (stride 0). */
+int h3_gated_residual(const h3_tensor *out, const h3_tensor *x, const h3_tensor *gate,
+                      const h3_tensor *y, void *stream);
+
+/* residual = bf16(x + bf16(gate * y)); out = h3_rms_modulate(residual, ...). */
+int h3_gated_residual_rms_modulate(const h3_tensor *residual, const h3_tensor *out,
+                                   const h3_tensor *x, const h3_tensor *gate, const h3_tensor *y,
+                                   const h3_tensor *weight, const h3_tensor *scale,
+                                   const h3_tensor *shift, float eps, void *stream);
+
+/* NeoX RoPE of x [S,H,128] with token-ordered angles cos/sin [S,half] (half = 48 in
+ * the reference layout, 64 for the full-D 44/42/42 layout): pairs (i, i+half) for
+ * i < half rotate, channels [2*half, 128) pass through. */
+int h3_rope(const h3_tensor *y, const h3_tensor *x, const h3_tensor *cos, const h3_tensor *sin,
+            void *stream);
+
+/* Per-head staged RMSNorm (weight [128]) then RoPE of x [T,P,Hs,128] (any strides)
+ * written to out [T,P,Hs,128] (any strides -- e.g. the permuted view of an
+ * all-to-all send buffer [P,T,Hs,128]).  cos/sin [T,half]. */
+int h3_qk_norm_rope(const h3_tensor *out, const h3_tensor *x, const h3_tensor *weight,
+                    const h3_tensor *cos, const h3_tensor *sin, float eps, void *stream);
+
+/* RoPE table: out [T,96] BF16 = cat(cos, sin) of angle[t, 16a+k] =
+ * f32(position[t,a]) * (1 / power[k]); position [T,3] F64, power [16] F32. */
+int h3_rope_cache(const h3_tensor *out, const h3_tensor *position, const h3_tensor *power,
+                  void *stream);
+
+/* Sectioned generalisation: sections (f0,f1,f2) frequencies per axis, power
+ * [f0+f1+f2] F32 (axis-major), out [T, 2*(f0+f1+f2)].  (16,16,16) with the 16
+ * powers repeated reproduces h3_rope_cache. */
+int h3_rope_cache_sectioned(const h3_tensor *out, const h3_tensor *position,
+                            const h3_tensor *power, int32_t f0, int32_t f1, int32_t f2,
+                            void *stream);
+
+/* out [N,dim] F32: cos(t*f_k) for k < dim/2 then sin(t*f_k), f_k = exp(-ln(max_period)*k/(dim/2)).
+ * t [N] F32. */
+int h3_timestep_embedding(const h3_tensor *out, const h3_tensor *t, float max_period, void *stream);
+
+/* ---------------- attention ---------------- */
+
+/* Non-causal softmax(q k^T * scale) v.  q, out [B,Sq,H,128]; k, v [B,Sk,H,128]
+ * (Sk may be shorter than Sq: sequence-parallel padding).  Strides arbitrary
+ * with innermost stride 1 and 16-byte aligned rows.  fp32 softmax/accumulate. */
+int h3_mha(const h3_tensor *out, const h3_tensor *q, const h3_tensor *k, const h3_tensor *v,
+           float scale, void *stream);
+
+/* ---------------- projections (BF16 in/out, fp32 accumulate) ---------------- */
+
+/* y [M,N] = x [M,K] * w[N,K]^T.  Rows of x, w, y contiguous (inner stride 1),
+ * row strides multiples of 8 elements, K a multiple of 64. */
+int h3_linear(const h3_tensor *y, const h3_tensor *x, const h3_tensor *w, void *stream);
+
+/* y [M,F] = swiglu(up, gate) with [up|gate] = x * w_packed^T, where w_packed is
+ * h3_pack_gate_up() of the [up; gate] weight [2F,K].  F a multiple of 128. */
+int h3_linear_swiglu(const h3_tensor *y, const h3_tensor *x, const h3_tensor *w_packed,
+                     void *stream);
+
+/* out [M,N] = bf16(residual + bf16(gate * bf16(x * w^T))); gate [M,N] (stride 0 ok). */
+int h3_linear_gated_residual(const h3_tensor *out, const h3_tensor *x, const h3_tensor *w,
+                             const h3_tensor *residual, const h3_tensor *gate, void *stream);
+
+/* Reorder the [up; gate] rows of a gate_up weight [2F,K] into 128-row blocks
+ * [up_0 | gate_0 | up_1 | gate_1 ...] consumed by h3_linear_swiglu. */
+int h3_pack_gate_up(const h3_tensor *dst, const h3_tensor *src, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* H3_B200_H */

@@ -1,0 +1,404 @@
+// BF16 projections of the H3 DiT block on tcgen05 / TMEM, fed by TMA (sm_100a),
+// with the block's pointwise ops fused into the epilogue.
+//
+//   y = x W^T                                       (QKV, out-proj; reference linear,
+//                                                     patches/InfiniCore.patch:1231-1292)
+//   y = swiglu(x Wup^T, x Wgate^T)                   (gate_up + h3_swiglu,
+//                                                     patches/InfiniLM.patch:1172-1179)
+//   y = bf16(res + bf16(gate * bf16(x W^T)))         (down-proj + h3_gated_residual,
+//                                                     patches/InfiniLM.patch:1391-1394)
+// The epilogues round the accumulator to BF16 first, exactly where the unfused
+// reference materialises the linear's BF16 output, then apply the pointwise op
+// with its staged rounding, so fused == unfused bit for bit.
+//
+// Persistent kernel, one CTA per SM, 128x256 output tiles, K in steps of 64
+// (one 128-byte swizzle span) through a 4-slot TMA ring.  Warp 0 loads (TMA, no
+// multicast), warp 1 issues tcgen05.mma (M=128, N=256, K=16) into one of two
+// TMEM accumulators (2 x 256 columns), warps 4..7 drain the other accumulator
+// (tcgen05.ld, one output row per thread) while the next tile accumulates.
+// Tiles are rasterised in column groups of 16 so the CTAs in flight share A rows
+// and a ~40 MB slab of W in L2.
+#include <math.h>
+#include <stdint.h>
+
+#include "h3_abi_util.h"
+#include "h3_common.cuh"
+#include "sm100_ptx.cuh"
+#include "tma_host.h"
+
+namespace h3 {
+namespace gemm {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;  // 16 KB
+constexpr int B_BYTES = BN * BK * 2;  // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int THREADS = 256;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr int GROUP_N = 16;
+constexpr int OFF_BAR = STAGES * STAGE_BYTES;
+constexpr int NUM_BARS = 2 * STAGES + 4;
+constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 16 + 1024;
+
+enum Epi { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_GATED_RES = 2 };
+
+struct Params {
+    int M, N, K;            // N: accumulator columns (weight rows)
+    int num_m, num_n, num_tiles;
+    __nv_bfloat16 *out;
+    int64_t ldo;
+    const __nv_bfloat16 *res;
+    int64_t ldr;
+    const __nv_bfloat16 *gate;
+    int64_t ldg;            // 0 broadcasts one gate row
+};
+
+__device__ __forceinline__ void tile_coords(const Params &p, int tile, int &m, int &n) {
+    const int span = GROUP_N * p.num_m;
+    const int g = tile / span;
+    const int r = tile - g * span;
+    const int n0 = g * GROUP_N;
+    const int gw = min(GROUP_N, p.num_n - n0);
+    m = r / gw;
+    n = n0 + (r - m * gw);
+}
+
+__device__ __forceinline__ void st_global_v4(void *ptr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(ptr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&v);
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
+    uint64_t *full = bars;
+    uint64_t *empty = bars + STAGES;
+    uint64_t *acc_full = bars + 2 * STAGES;
+    uint64_t *acc_empty = acc_full + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + NUM_BARS);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kblocks = p.K / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&acc_full[a], 1);
+            mbar_init(&acc_empty[a], 128);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            tma_prefetch_desc(&ta);
+            tma_prefetch_desc(&tb);
+            uint32_t it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+                int m, n;
+                tile_coords(p, tile, m, n);
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const uint32_t slot = it % STAGES, use = it / STAGES;
+                    ok = mbar_wait(&empty[slot], (use & 1) ^ 1, abort_flag);
+                    if (!ok) break;
+                    uint8_t *sa = smem + slot * STAGE_BYTES;
+                    mbar_expect_tx(&full[slot], STAGE_BYTES);
+                    tma_load_2d(sa, &ta, &full[slot], kb * BK, m * BM);
+                    tma_load_2d(sa + A_BYTES, &tb, &full[slot], kb * BK, n * BN);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN, false);
+            const uint32_t base = smem_u32(smem);
+            uint32_t it = 0, lt = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++lt) {
+                const uint32_t acc = lt & 1, use = lt >> 1;
+                ok = mbar_wait(&acc_empty[acc], (use & 1) ^ 1, abort_flag);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t d = tmem + acc * BN;
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const uint32_t slot = it % STAGES;
+                    ok = mbar_wait(&full[slot], (it / STAGES) & 1, abort_flag);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t sa = base + slot * STAGE_BYTES, sb = sa + A_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk)
+                        umma_ss(d, smem_desc_sw128(sa + kk * 32, 16, 1024), smem_desc_sw128(sb + kk * 32, 16, 1024),
+                                IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+                    umma_commit(&empty[slot]);
+                }
+                if (!ok) break;
+                umma_commit(&acc_full[acc]);
+            }
+            if (!ok) drain_in_flight();
+        }
+    } else if (warp >= 4) {
+        const int wq = warp & 3;
+        const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
+        uint32_t lt = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++lt) {
+            int m, n;
+            tile_coords(p, tile, m, n);
+            const uint32_t acc = lt & 1;
+            ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[acc], (lt >> 1) & 1, abort_flag));
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t tbase = tmem + acc * BN + lane_off;
+            const int row = m * BM + wq * 32 + lane;
+            const bool row_ok = row < p.M;
+            if (EPI == EPI_SWIGLU) {
+                // accumulator columns [0,128) = up, [128,256) = gate of features n*128 + c
+#pragma unroll 1
+                for (int cc = 0; cc < 4; ++cc) {
+                    uint32_t u[32], g[32];
+                    tmem_ld32(tbase + cc * 32, u);
+                    tmem_ld32(tbase + 128 + cc * 32, g);
+                    tmem_ld_wait();
+                    const int col = n * 128 + cc * 32;
+                    if (row_ok) {
+                        uint32_t w[16];
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            float o2[2];
+#pragma unroll
+                            for (int e = 0; e < 2; ++e) {
+                                const float up = bf(__uint_as_float(u[2 * i + e]));
+                                const float gt = bf(__uint_as_float(g[2 * i + e]));
+                                const float act = bf(__fdiv_rn(gt, add_rn(1.0f, expf(-gt))));
+                                o2[e] = mul_rn(up, act);
+                            }
+                            w[i] = pack2(o2[0], o2[1]);
+                        }
+                        __nv_bfloat16 *dst = p.out + (int64_t)row * p.ldo + col;
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) st_global_v4(dst + 8 * q, w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+                    }
+                }
+            } else {
+#pragma unroll 1
+                for (int cc = 0; cc < BN / 32; ++cc) {
+                    uint32_t v[32];
+                    tmem_ld32(tbase + cc * 32, v);
+                    tmem_ld_wait();
+                    const int col = n * BN + cc * 32;
+                    if (row_ok && col < p.N) {
+                        uint32_t w[16];
+                        if (EPI == EPI_STORE) {
+#pragma unroll
+                            for (int i = 0; i < 16; ++i)
+                                w[i] = pack2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+                        } else {  // EPI_GATED_RES
+                            const __nv_bfloat16 *rp = p.res + (int64_t)row * p.ldr + col;
+                            const __nv_bfloat16 *gp = p.gate + (int64_t)row * p.ldg + col;
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) {
+                                float rf[8], gf[8];
+                                unpack8(*reinterpret_cast<const uint4 *>(rp + 8 * q), rf);
+                                unpack8(*reinterpret_cast<const uint4 *>(gp + 8 * q), gf);
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) {
+                                    float o2[2];
+#pragma unroll
+                                    for (int k = 0; k < 2; ++k) {
+                                        const int idx = 8 * q + 2 * e + k;
+                                        const float yv = bf(__uint_as_float(v[idx]));
+                                        o2[k] = add_rn(rf[2 * e + k], bf(mul_rn(gf[2 * e + k], yv)));
+                                    }
+                                    w[4 * q + e] = pack2(o2[0], o2[1]);
+                                }
+                            }
+                        }
+                        __nv_bfloat16 *dst = p.out + (int64_t)row * p.ldo + col;
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) st_global_v4(dst + 8 * q, w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&acc_empty[acc]);
+        }
+        if (!ok) drain_in_flight();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+// dst rows = 128-row blocks [up_0 | gate_0 | up_1 | gate_1 | ...] of src = [up; gate]
+__global__ void pack_gate_up_kernel(__nv_bfloat16 *dst, int64_t lddst, const __nv_bfloat16 *src, int64_t ldsrc,
+                                    int64_t F, int64_t K) {
+    const int64_t vpr = K / 8;
+    const int64_t total = 2 * F * vpr;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = idx / vpr, c = (idx - r * vpr) * 8;
+        const int64_t blk = r / 256, within = r - blk * 256;
+        const int64_t s = within < 128 ? blk * 128 + within : F + blk * 128 + (within - 128);
+        *reinterpret_cast<uint4 *>(dst + r * lddst + c) = *reinterpret_cast<const uint4 *>(src + s * ldsrc + c);
+    }
+}
+
+}  // namespace gemm
+}  // namespace h3
+
+using namespace h3;
+
+namespace {
+
+int check_matrix(const h3_tensor *t) {
+    H3_CHECK(check_bf16(t));
+    if (t->ndim != 2) return H3_ERR_BAD_SHAPE;
+    if (t->strides[1] != 1 || !aligned16(t->data)) return H3_ERR_BAD_LAYOUT;
+    if (t->shape[0] > 1 && (t->strides[0] % 8 != 0 || t->strides[0] < t->shape[1])) return H3_ERR_BAD_LAYOUT;
+    return H3_OK;
+}
+
+int mat_tmap(CUtensorMap *map, const h3_tensor *t, uint32_t box_rows) {
+    const cuuint64_t dims[2] = {(cuuint64_t)t->shape[1], (cuuint64_t)t->shape[0]};
+    const int64_t ld = t->shape[0] > 1 ? t->strides[0] : ((t->shape[1] + 7) / 8) * 8;
+    const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    const cuuint32_t box[2] = {gemm::BK, box_rows};
+    return make_tmap_bf16(map, t->data, 2, dims, strides, box);
+}
+
+template <int EPI>
+int launch_gemm(const h3_tensor *x, const h3_tensor *w, gemm::Params &p, cudaStream_t stream) {
+    CUtensorMap ta, tb;
+    H3_CHECK(mat_tmap(&ta, x, gemm::BM));
+    H3_CHECK(mat_tmap(&tb, w, gemm::BN));
+    p.num_m = (p.M + gemm::BM - 1) / gemm::BM;
+    p.num_n = (p.N + gemm::BN - 1) / gemm::BN;
+    p.num_tiles = p.num_m * p.num_n;
+    if (p.num_tiles == 0) return H3_OK;
+    static std::atomic<bool> attr_set[3][64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return H3_ERR_UNSUPPORTED;
+    if (!attr_set[EPI][dev].load()) {
+        if (cudaFuncSetAttribute(gemm::gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 gemm::SMEM_BYTES) != cudaSuccess)
+            return H3_ERR_LAUNCH;
+        attr_set[EPI][dev].store(true);
+    }
+    const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
+    gemm::gemm_kernel<EPI><<<grid, gemm::THREADS, gemm::SMEM_BYTES, stream>>>(ta, tb, p);
+    return launch_status();
+}
+
+int check_gemm_operands(const h3_tensor *y, const h3_tensor *x, const h3_tensor *w) {
+    H3_CHECK(check_matrix(y));
+    H3_CHECK(check_matrix(x));
+    H3_CHECK(check_matrix(w));
+    if (x->shape[1] != w->shape[1]) return H3_ERR_BAD_SHAPE;
+    if (x->shape[1] % gemm::BK != 0 || x->shape[1] == 0) return H3_ERR_UNSUPPORTED;
+    if (x->shape[0] > 0x7fffffffLL || w->shape[0] > 0x7fffffffLL) return H3_ERR_UNSUPPORTED;
+    return H3_OK;
+}
+
+}  // namespace
+
+extern "C" int h3_linear(const h3_tensor *y, const h3_tensor *x, const h3_tensor *w, void *stream) {
+    H3_CHECK(check_gemm_operands(y, x, w));
+    if (y->shape[0] != x->shape[0] || y->shape[1] != w->shape[0]) return H3_ERR_BAD_SHAPE;
+    if (y->shape[1] % 32 != 0) return H3_ERR_UNSUPPORTED;
+    gemm::Params p{};
+    p.M = (int)x->shape[0];
+    p.N = (int)w->shape[0];
+    p.K = (int)x->shape[1];
+    p.out = static_cast<__nv_bfloat16 *>(y->data);
+    p.ldo = y->strides[0];
+    return launch_gemm<gemm::EPI_STORE>(x, w, p, (cudaStream_t)stream);
+}
+
+extern "C" int h3_linear_swiglu(const h3_tensor *y, const h3_tensor *x, const h3_tensor *w_packed, void *stream) {
+    H3_CHECK(check_gemm_operands(y, x, w_packed));
+    const int64_t F = w_packed->shape[0] / 2;
+    if (w_packed->shape[0] % 256 != 0) return H3_ERR_BAD_SHAPE;
+    if (y->shape[0] != x->shape[0] || y->shape[1] != F) return H3_ERR_BAD_SHAPE;
+    gemm::Params p{};
+    p.M = (int)x->shape[0];
+    p.N = (int)w_packed->shape[0];
+    p.K = (int)x->shape[1];
+    p.out = static_cast<__nv_bfloat16 *>(y->data);
+    p.ldo = y->strides[0];
+    return launch_gemm<gemm::EPI_SWIGLU>(x, w_packed, p, (cudaStream_t)stream);
+}
+
+extern "C" int h3_linear_gated_residual(const h3_tensor *out, const h3_tensor *x, const h3_tensor *w,
+                                        const h3_tensor *residual, const h3_tensor *gate, void *stream) {
+    H3_CHECK(check_gemm_operands(out, x, w));
+    H3_CHECK(check_bf16(residual));
+    H3_CHECK(check_bf16(gate));
+    if (out->shape[0] != x->shape[0] || out->shape[1] != w->shape[0]) return H3_ERR_BAD_SHAPE;
+    H3_CHECK(check_same_shape(residual, out));
+    H3_CHECK(check_same_shape(gate, out));
+    if (out->shape[1] % 32 != 0) return H3_ERR_UNSUPPORTED;
+    if (residual->strides[1] != 1 || gate->strides[1] != 1 || !aligned16(residual->data) || !aligned16(gate->data) ||
+        residual->strides[0] % 8 != 0 || gate->strides[0] % 8 != 0)
+        return H3_ERR_BAD_LAYOUT;
+    gemm::Params p{};
+    p.M = (int)x->shape[0];
+    p.N = (int)w->shape[0];
+    p.K = (int)x->shape[1];
+    p.out = static_cast<__nv_bfloat16 *>(out->data);
+    p.ldo = out->strides[0];
+    p.res = static_cast<const __nv_bfloat16 *>(residual->data);
+    p.ldr = residual->strides[0];
+    p.gate = static_cast<const __nv_bfloat16 *>(gate->data);
+    p.ldg = gate->strides[0];
+    return launch_gemm<gemm::EPI_GATED_RES>(x, w, p, (cudaStream_t)stream);
+}
+
+extern "C" int h3_pack_gate_up(const h3_tensor *dst, const h3_tensor *src, void *stream) {
+    H3_CHECK(check_matrix(dst));
+    H3_CHECK(check_matrix(src));
+    H3_CHECK(check_same_shape(dst, src));
+    if (src->shape[0] % 256 != 0 || src->shape[1] % 8 != 0) return H3_ERR_BAD_SHAPE;
+    const int64_t F = src->shape[0] / 2, K = src->shape[1];
+    if (F == 0 || K == 0) return H3_OK;
+    const int64_t work = 2 * F * (K / 8);
+    int blocks = (int)((work + 255) / 256);
+    if (blocks > num_sms() * 16) blocks = num_sms() * 16;
+    gemm::pack_gate_up_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(
+        static_cast<__nv_bfloat16 *>(dst->data), dst->strides[0], static_cast<const __nv_bfloat16 *>(src->data),
+        src->strides[0], F, K);
+    return launch_status();
+}
+
+extern "C" unsigned int h3_gemm_device_error_read_and_clear(void) {
+    unsigned int v = 0, zero = 0;
+    cudaMemcpyFromSymbol(&v, h3::g_h3_device_error, sizeof(v));
+    cudaMemcpyToSymbol(h3::g_h3_device_error, &zero, sizeof(zero));
+    return v;
+}

@@ -1,0 +1,706 @@
+// Fused pointwise kernels of the H3 DiT block (sm_100a), with the reference's
+// BF16 rounding at every step (tools/h3_pointwise.py; torch compositions in
+// tools/bench_h3_ops.py:81-258), plus their C-ABI entry points.
+//
+// Design: HBM-bound.  Row ops (RMSNorm/AdaLN family) run one 128-thread CTA per
+// row with the row held in registers (one HBM read, one write); the reduction
+// order is fixed by the thread/vector assignment (per-thread serial sum over its
+// 8-wide vectors in column order, xor-shuffle tree, then warps 0..3 in order), so
+// a row's result never depends on which CTA or rank computes it.  Per-head ops
+// (q/k norm + RoPE) run one warp per 128-wide head row, lanes exchanging RoPE
+// partners by shuffle.  Each kernel has a vectorised path (16-byte / 8-byte
+// accesses, inner stride 1, aligned rows) and a strided path with the same
+// arithmetic and the same summation order, so both give identical bits.
+#include <math.h>
+
+#include "h3_abi_util.h"
+#include "h3_common.cuh"
+
+namespace h3 {
+
+// ===========================================================================
+// element-wise ops: gated residual, SwiGLU
+// ===========================================================================
+struct EwArgs {
+    RowView a, b, c;     // gated residual: a=x, b=gate, c=y ; swiglu: a=up, b=gate
+    RowViewMut o;
+    int64_t rows, n1, C;
+};
+
+enum { EW_GATED_RESIDUAL = 0, EW_SWIGLU = 1 };
+
+template <int OP>
+__device__ __forceinline__ float ew_apply(float a, float b, float c) {
+    if (OP == EW_GATED_RESIDUAL) {
+        return add_rn(a, bf(mul_rn(b, c)));  // bf16(x + bf16(gate * y)), rounded by the store
+    } else {
+        const float act = bf(__fdiv_rn(b, add_rn(1.0f, expf(-b))));  // bf16(g / (1 + exp(-g)))
+        return mul_rn(a, act);
+    }
+}
+
+template <int OP>
+__global__ void __launch_bounds__(256) ew_vec_kernel(EwArgs args) {
+    const int64_t vpr = args.C >> 3;
+    const int64_t total = args.rows * vpr;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = idx / vpr;
+        const int64_t col = (idx - row * vpr) << 3;
+        const uint4 va = *reinterpret_cast<const uint4 *>(
+            args.a.p + row_offset(args.a.s0, args.a.s1, row, args.n1) + col);
+        const uint4 vb = *reinterpret_cast<const uint4 *>(
+            args.b.p + row_offset(args.b.s0, args.b.s1, row, args.n1) + col);
+        uint4 vc = make_uint4(0, 0, 0, 0);
+        if (OP == EW_GATED_RESIDUAL)
+            vc = *reinterpret_cast<const uint4 *>(args.c.p + row_offset(args.c.s0, args.c.s1, row, args.n1) + col);
+        float fa[8], fb[8], fc[8], fo[8];
+        unpack8(va, fa);
+        unpack8(vb, fb);
+        unpack8(vc, fc);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) fo[i] = ew_apply<OP>(fa[i], fb[i], fc[i]);
+        *reinterpret_cast<uint4 *>(args.o.p + row_offset(args.o.s0, args.o.s1, row, args.n1) + col) = pack8(fo);
+    }
+}
+
+template <int OP>
+__global__ void __launch_bounds__(256) ew_strided_kernel(EwArgs args) {
+    const int64_t total = args.rows * args.C;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = idx / args.C;
+        const int64_t col = idx - row * args.C;
+        const float a = __bfloat162float(args.a.p[row_offset(args.a.s0, args.a.s1, row, args.n1) + col * args.a.sc]);
+        const float b = __bfloat162float(args.b.p[row_offset(args.b.s0, args.b.s1, row, args.n1) + col * args.b.sc]);
+        float c = 0.f;
+        if (OP == EW_GATED_RESIDUAL)
+            c = __bfloat162float(args.c.p[row_offset(args.c.s0, args.c.s1, row, args.n1) + col * args.c.sc]);
+        args.o.p[row_offset(args.o.s0, args.o.s1, row, args.n1) + col * args.o.sc] =
+            __float2bfloat16_rn(ew_apply<OP>(a, b, c));
+    }
+}
+
+// ===========================================================================
+// row ops: RMSNorm, RMSNorm+AdaLN, gated residual + RMSNorm+AdaLN, LN+AdaLN
+// ===========================================================================
+enum { ROW_RMS = 0, ROW_RMS_MOD = 1, ROW_RES_RMS_MOD = 2, ROW_LN_MOD = 3 };
+
+struct RowArgs {
+    RowView x, gate, y, scale, shift;   // gate/y only for ROW_RES_RMS_MOD
+    const __nv_bfloat16 *weight;        // [C], stride wsc
+    int64_t wsc;
+    RowViewMut out, residual;           // residual only for ROW_RES_RMS_MOD
+    int64_t rows, n1, C;
+    float eps;
+};
+
+constexpr int ROW_THREADS = 128;
+
+template <bool VEC>
+__device__ __forceinline__ void row_load8(const __nv_bfloat16 *base, int64_t sc, int64_t col, int64_t C,
+                                          float f[8]) {
+    if (VEC) {
+        unpack8(*reinterpret_cast<const uint4 *>(base + col), f);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[i] = (col + i < C) ? __bfloat162float(base[(col + i) * sc]) : 0.f;
+    }
+}
+template <bool VEC>
+__device__ __forceinline__ void row_store8(__nv_bfloat16 *base, int64_t sc, int64_t col, int64_t C,
+                                           const float f[8]) {
+    if (VEC) {
+        *reinterpret_cast<uint4 *>(base + col) = pack8(f);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (col + i < C) base[(col + i) * sc] = __float2bfloat16_rn(f[i]);
+    }
+}
+
+// Sum over the CTA in a fixed order: xor tree inside each warp, then warps in order.
+__device__ __forceinline__ float cta_sum(float v, float *red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = add_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();  // red[] may still be read from a previous reduction
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float s = red[0];
+#pragma unroll
+    for (int w = 1; w < ROW_THREADS / 32; ++w) s = add_rn(s, red[w]);
+    return s;
+}
+
+template <int MODE, bool VEC, int VPT>
+__global__ void __launch_bounds__(ROW_THREADS) row_kernel(RowArgs args) {
+    __shared__ float red[ROW_THREADS / 32];
+    const int64_t row = blockIdx.x;
+    const int64_t C = args.C;
+    const int64_t nvec = (C + 7) >> 3;
+    const __nv_bfloat16 *xrow = args.x.p + row_offset(args.x.s0, args.x.s1, row, args.n1);
+
+    float v[VPT][8];
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+        const int64_t vi = threadIdx.x + (int64_t)k * ROW_THREADS;
+        if (vi < nvec) {
+            row_load8<VEC>(xrow, args.x.sc, vi * 8, C, v[k]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[k][i] = 0.f;
+        }
+    }
+    if (MODE == ROW_RES_RMS_MOD) {
+        const __nv_bfloat16 *grow = args.gate.p + row_offset(args.gate.s0, args.gate.s1, row, args.n1);
+        const __nv_bfloat16 *yrow = args.y.p + row_offset(args.y.s0, args.y.s1, row, args.n1);
+        __nv_bfloat16 *rrow = args.residual.p + row_offset(args.residual.s0, args.residual.s1, row, args.n1);
+#pragma unroll
+        for (int k = 0; k < VPT; ++k) {
+            const int64_t vi = threadIdx.x + (int64_t)k * ROW_THREADS;
+            if (vi < nvec) {
+                float g[8], y[8];
+                row_load8<VEC>(grow, args.gate.sc, vi * 8, C, g);
+                row_load8<VEC>(yrow, args.y.sc, vi * 8, C, y);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[k][i] = bf(add_rn(v[k][i], bf(mul_rn(g[i], y[i]))));
+                row_store8<VEC>(rrow, args.residual.sc, vi * 8, C, v[k]);
+            }
+        }
+    }
+
+    // ---- statistics ----
+    float r = 0.f, shift_ln = 0.f;
+    if (MODE == ROW_LN_MOD) {
+        float s = 0.f;
+#pragma unroll
+        for (int k = 0; k < VPT; ++k)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) s = add_rn(s, v[k][i]);
+        const float mean = __fdiv_rn(cta_sum(s, red), (float)C);
+        float q = 0.f;
+#pragma unroll
+        for (int k = 0; k < VPT; ++k) {
+            const int64_t vi = threadIdx.x + (int64_t)k * ROW_THREADS;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                if (vi * 8 + i < C) {
+                    const float d = __fsub_rn(v[k][i], mean);
+                    q = __fmaf_rn(d, d, q);
+                }
+            }
+        }
+        const float var = __fdiv_rn(cta_sum(q, red), (float)C);
+        r = rsqrt_torch(add_rn(var, args.eps));
+        shift_ln = -mul_rn(r, mean);  // y = x * rstd + (-rstd * mean), fused
+    } else {
+        float s = 0.f;
+#pragma unroll
+        for (int k = 0; k < VPT; ++k)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) s = add_rn(s, bf(mul_rn(v[k][i], v[k][i])));  // bf16(x^2)
+        const float mean = bf(__fdiv_rn(cta_sum(s, red), (float)C));
+        const float var = bf(add_rn(mean, args.eps));
+        r = bf(rsqrt_torch(var));
+    }
+
+    // ---- normalise, weight, modulate, store ----
+    const __nv_bfloat16 *srow = nullptr, *hrow = nullptr;
+    if (MODE != ROW_RMS) {
+        srow = args.scale.p + row_offset(args.scale.s0, args.scale.s1, row, args.n1);
+        hrow = args.shift.p + row_offset(args.shift.s0, args.shift.s1, row, args.n1);
+    }
+    __nv_bfloat16 *orow = args.out.p + row_offset(args.out.s0, args.out.s1, row, args.n1);
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+        const int64_t vi = threadIdx.x + (int64_t)k * ROW_THREADS;
+        if (vi >= nvec) continue;
+        float o[8];
+        if (MODE == ROW_LN_MOD) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] = bf(__fmaf_rn(v[k][i], r, shift_ln));
+        } else {
+            float w[8];
+            if (VEC && args.wsc == 1) {
+                unpack8(*reinterpret_cast<const uint4 *>(args.weight + vi * 8), w);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    w[i] = (vi * 8 + i < C) ? __bfloat162float(args.weight[(vi * 8 + i) * args.wsc]) : 0.f;
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] = bf(mul_rn(bf(mul_rn(v[k][i], r)), w[i]));
+        }
+        if (MODE != ROW_RMS) {
+            float sc[8], sh[8];
+            row_load8<VEC>(srow, args.scale.sc, vi * 8, C, sc);
+            row_load8<VEC>(hrow, args.shift.sc, vi * 8, C, sh);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float factor = bf(add_rn(sc[i], 1.0f));
+                o[i] = add_rn(bf(mul_rn(o[i], factor)), sh[i]);
+            }
+        }
+        row_store8<VEC>(orow, args.out.sc, vi * 8, C, o);
+    }
+}
+
+// ===========================================================================
+// per-head q/k RMSNorm + RoPE (one warp per 128-wide head row)
+// ===========================================================================
+struct HeadArgs {
+    const __nv_bfloat16 *x;
+    int64_t xs[4];                 // [T, P, Hs, D] strides
+    __nv_bfloat16 *out;
+    int64_t os[4];
+    const __nv_bfloat16 *weight;   // [128] (norm only)
+    int64_t wsc;
+    const __nv_bfloat16 *cos, *sin;
+    int64_t cs0, cs1, ss0, ss1;
+    int64_t T, P, Hs;
+    int half;                      // rotated pairs (48 or 64); 0 = no rotation
+    float eps;
+};
+
+template <bool NORM, bool VEC>
+__global__ void __launch_bounds__(256) head_kernel(HeadArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int64_t rows = a.T * a.P * a.Hs;
+    const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    const int d = a.half >> 2;  // lanes per rotated half
+    for (int64_t rix = warp0; rix < rows; rix += nwarps) {
+        const int64_t h = rix % a.Hs;
+        const int64_t tp = rix / a.Hs;
+        const int64_t p = tp % a.P;
+        const int64_t t = tp / a.P;
+        const __nv_bfloat16 *xr = a.x + t * a.xs[0] + p * a.xs[1] + h * a.xs[2];
+        __nv_bfloat16 *orow = a.out + t * a.os[0] + p * a.os[1] + h * a.os[2];
+        float v[4];
+        if (VEC) {
+            unpack4(*reinterpret_cast<const uint2 *>(xr + 4 * lane), v);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[i] = __bfloat162float(xr[(4 * lane + i) * a.xs[3]]);
+        }
+        if (NORM) {
+            float s = 0.f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) s = add_rn(s, bf(mul_rn(v[i], v[i])));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) s = add_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+            const float mean = bf(__fdiv_rn(s, 128.0f));
+            const float var = bf(add_rn(mean, a.eps));
+            const float r = bf(rsqrt_torch(var));
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float w = __bfloat162float(a.weight[(4 * lane + i) * a.wsc]);
+                v[i] = bf(mul_rn(bf(mul_rn(v[i], r)), w));
+            }
+        }
+        float o[4];
+        if (a.half > 0) {
+            // exchange with the RoPE partner lane (values are exact BF16, packed losslessly)
+            const uint2 mine = pack4(v);
+            const int partner = lane < d ? lane + d : (lane < 2 * d ? lane - d : lane);
+            uint2 theirs;
+            theirs.x = __shfl_sync(0xffffffffu, mine.x, partner);
+            theirs.y = __shfl_sync(0xffffffffu, mine.y, partner);
+            float pv[4];
+            unpack4(theirs, pv);
+            if (lane < 2 * d) {
+                const int j = 4 * (lane < d ? lane : lane - d);
+                float c[4], s[4];
+                if (VEC) {
+                    unpack4(*reinterpret_cast<const uint2 *>(a.cos + t * a.cs0 + j), c);
+                    unpack4(*reinterpret_cast<const uint2 *>(a.sin + t * a.ss0 + j), s);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        c[i] = __bfloat162float(a.cos[t * a.cs0 + (j + i) * a.cs1]);
+                        s[i] = __bfloat162float(a.sin[t * a.ss0 + (j + i) * a.ss1]);
+                    }
+                }
+                if (lane < d) {  // first half: y0 = bf(bf(a*c) + bf(-b*s))
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) o[i] = add_rn(bf(mul_rn(v[i], c[i])), bf(mul_rn(-pv[i], s[i])));
+                } else {         // second half: y1 = bf(bf(b*c) + bf(a*s))
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) o[i] = add_rn(bf(mul_rn(v[i], c[i])), bf(mul_rn(pv[i], s[i])));
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) o[i] = v[i];
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) o[i] = v[i];
+        }
+        if (VEC) {
+            *reinterpret_cast<uint2 *>(orow + 4 * lane) = pack4(o);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) orow[(4 * lane + i) * a.os[3]] = __float2bfloat16_rn(o[i]);
+        }
+    }
+}
+
+// ===========================================================================
+// RoPE table and timestep embedding
+// ===========================================================================
+struct RopeCacheArgs {
+    const double *pos;
+    int64_t ps0, ps1;
+    const float *power[3];  // per-axis power arrays (all equal for the reference table)
+    int64_t pws;            // power element stride
+    __nv_bfloat16 *out;
+    int64_t os0, os1;
+    int64_t T;
+    int f[3];
+    int ftot;
+};
+
+__global__ void __launch_bounds__(256) rope_cache_kernel(RopeCacheArgs a) {
+    const int64_t total = a.T * a.ftot;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t t = idx / a.ftot;
+        const int j = (int)(idx - t * a.ftot);
+        const int axis = j < a.f[0] ? 0 : (j < a.f[0] + a.f[1] ? 1 : 2);
+        const int k = j - (axis > 0 ? a.f[0] : 0) - (axis > 1 ? a.f[1] : 0);
+        const float position = __double2float_rn(a.pos[t * a.ps0 + axis * a.ps1]);
+        const float inverse = __fdiv_rn(1.0f, a.power[axis][k * a.pws]);
+        const float angle = __fmul_rn(position, inverse);
+        // cos/sin evaluated in double and rounded once to fp32: the correctly
+        // rounded fp32 value, which the CPU reference's fp32 cos/sin match to 1 ulp.
+        const float c = (float)cos((double)angle);
+        const float s = (float)sin((double)angle);
+        a.out[t * a.os0 + j * a.os1] = __float2bfloat16_rn(c);
+        a.out[t * a.os0 + (a.ftot + j) * a.os1] = __float2bfloat16_rn(s);
+    }
+}
+
+__global__ void __launch_bounds__(256) timestep_embedding_kernel(float *out, int64_t os0, int64_t os1,
+                                                                 const float *t, int64_t ts, int64_t n,
+                                                                 int64_t dim, float log_max_period) {
+    const int64_t total = n * dim;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = idx / dim, c = idx - i * dim;
+        const int64_t half = dim / 2;
+        const int64_t k = c < half ? c : c - half;
+        const float freq = expf(__fdiv_rn(__fmul_rn(-log_max_period, (float)k), (float)half));
+        const float angle = __fmul_rn(t[i * ts], freq);
+        out[i * os0 + c * os1] = c < half ? cosf(angle) : sinf(angle);
+    }
+}
+
+// ===========================================================================
+// host-side launchers
+// ===========================================================================
+static int grid_for(int64_t work, int threads) {
+    int64_t blocks = (work + threads - 1) / threads;
+    const int64_t cap = (int64_t)num_sms() * 16;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    return (int)blocks;
+}
+
+static RowView rowview(const h3_tensor *t) {
+    RowView r;
+    r.p = static_cast<const __nv_bfloat16 *>(t->data);
+    lead_strides(t, &r.s0, &r.s1);
+    r.sc = t->strides[t->ndim - 1];
+    return r;
+}
+static RowViewMut rowview_mut(const h3_tensor *t) {
+    RowViewMut r;
+    r.p = static_cast<__nv_bfloat16 *>(t->data);
+    lead_strides(t, &r.s0, &r.s1);
+    r.sc = t->strides[t->ndim - 1];
+    return r;
+}
+
+template <int OP>
+static int launch_ew(const h3_tensor *o, const h3_tensor *a, const h3_tensor *b, const h3_tensor *c,
+                     cudaStream_t stream) {
+    EwArgs args;
+    args.a = rowview(a);
+    args.b = rowview(b);
+    args.c = c ? rowview(c) : args.b;
+    args.o = rowview_mut(o);
+    lead_dims(o, &args.rows, &args.n1);
+    args.C = o->shape[o->ndim - 1];
+    if (args.rows == 0 || args.C == 0) return H3_OK;
+    const bool vec = rows_vectorizable(o, 8) && rows_vectorizable(a, 8) && rows_vectorizable(b, 8) &&
+                     (!c || rows_vectorizable(c, 8));
+    if (vec) {
+        const int g = grid_for(args.rows * (args.C / 8), 256);
+        ew_vec_kernel<OP><<<g, 256, 0, stream>>>(args);
+    } else {
+        const int g = grid_for(args.rows * args.C, 256);
+        ew_strided_kernel<OP><<<g, 256, 0, stream>>>(args);
+    }
+    return launch_status();
+}
+
+template <int MODE>
+static int launch_row(RowArgs &args, bool vec, cudaStream_t stream) {
+    if (args.rows == 0 || args.C == 0) return H3_OK;
+    const int64_t nvec = (args.C + 7) / 8;
+    const int vpt = (int)((nvec + ROW_THREADS - 1) / ROW_THREADS);
+    if (args.rows > 0x7fffffffLL) return H3_ERR_UNSUPPORTED;
+    const dim3 grid((unsigned)args.rows);
+#define H3_ROW_CASE(V)                                                                       \
+    case V:                                                                                  \
+        if (vec) row_kernel<MODE, true, V><<<grid, ROW_THREADS, 0, stream>>>(args);         \
+        else row_kernel<MODE, false, V><<<grid, ROW_THREADS, 0, stream>>>(args);            \
+        break;
+    switch (vpt) {
+        H3_ROW_CASE(1)
+        H3_ROW_CASE(2)
+        H3_ROW_CASE(3)
+        H3_ROW_CASE(4)
+        H3_ROW_CASE(5)
+        H3_ROW_CASE(6)
+        H3_ROW_CASE(8)
+        case 7:
+            if (vec) row_kernel<MODE, true, 8><<<grid, ROW_THREADS, 0, stream>>>(args);
+            else row_kernel<MODE, false, 8><<<grid, ROW_THREADS, 0, stream>>>(args);
+            break;
+        default:
+            return H3_ERR_UNSUPPORTED;  // rows wider than 8192 elements
+    }
+#undef H3_ROW_CASE
+    return launch_status();
+}
+
+}  // namespace h3
+
+using namespace h3;
+
+// ===========================================================================
+// C-ABI
+// ===========================================================================
+extern "C" int h3_gated_residual(const h3_tensor *out, const h3_tensor *x, const h3_tensor *gate,
+                                 const h3_tensor *y, void *stream) {
+    H3_CHECK(check_bf16(out) ?: check_bf16(x) ?: check_bf16(gate) ?: check_bf16(y));
+    H3_CHECK(check_rank(out, 2, 3) ?: check_same_shape(out, x) ?: check_same_shape(out, gate) ?:
+             check_same_shape(out, y));
+    return launch_ew<EW_GATED_RESIDUAL>(out, x, gate, y, (cudaStream_t)stream);
+}
+
+extern "C" int h3_swiglu(const h3_tensor *y, const h3_tensor *up, const h3_tensor *gate, void *stream) {
+    H3_CHECK(check_bf16(y) ?: check_bf16(up) ?: check_bf16(gate));
+    H3_CHECK(check_rank(y, 2, 3) ?: check_same_shape(y, up) ?: check_same_shape(y, gate));
+    return launch_ew<EW_SWIGLU>(y, up, gate, nullptr, (cudaStream_t)stream);
+}
+
+static int fill_row_args(RowArgs &a, const h3_tensor *out, const h3_tensor *x, const h3_tensor *weight,
+                         const h3_tensor *scale, const h3_tensor *shift, float eps, bool *vec) {
+    a.x = rowview(x);
+    a.out = rowview_mut(out);
+    a.gate = a.y = a.x;
+    a.residual = a.out;
+    a.scale = scale ? rowview(scale) : a.x;
+    a.shift = shift ? rowview(shift) : a.x;
+    a.weight = weight ? static_cast<const __nv_bfloat16 *>(weight->data) : nullptr;
+    a.wsc = weight ? weight->strides[0] : 1;
+    lead_dims(out, &a.rows, &a.n1);
+    a.C = out->shape[out->ndim - 1];
+    a.eps = eps;
+    *vec = rows_vectorizable(out, 8) && rows_vectorizable(x, 8) && (!scale || rows_vectorizable(scale, 8)) &&
+           (!shift || rows_vectorizable(shift, 8)) &&
+           (!weight || (weight->strides[0] == 1 && aligned16(weight->data)));
+    return H3_OK;
+}
+
+static int check_weight(const h3_tensor *w, int64_t C) {
+    if (!w || !w->data) return H3_ERR_NULL;
+    if (w->dtype != H3_BF16) return H3_ERR_BAD_DTYPE;
+    if (w->ndim != 1 || w->shape[0] != C) return H3_ERR_BAD_SHAPE;
+    return H3_OK;
+}
+
+extern "C" int h3_rms_norm(const h3_tensor *y, const h3_tensor *x, const h3_tensor *weight, float eps,
+                           void *stream) {
+    H3_CHECK(check_bf16(y) ?: check_bf16(x));
+    H3_CHECK(check_rank(x, 2, 3) ?: check_same_shape(y, x));
+    H3_CHECK(check_weight(weight, x->shape[x->ndim - 1]));
+    RowArgs a;
+    bool vec;
+    fill_row_args(a, y, x, weight, nullptr, nullptr, eps, &vec);
+    return launch_row<ROW_RMS>(a, vec, (cudaStream_t)stream);
+}
+
+extern "C" int h3_rms_modulate(const h3_tensor *y, const h3_tensor *x, const h3_tensor *weight,
+                               const h3_tensor *scale, const h3_tensor *shift, float eps, void *stream) {
+    H3_CHECK(check_bf16(y) ?: check_bf16(x) ?: check_bf16(scale) ?: check_bf16(shift));
+    H3_CHECK(check_rank(x, 2, 3) ?: check_same_shape(y, x) ?: check_same_shape(scale, x) ?:
+             check_same_shape(shift, x));
+    H3_CHECK(check_weight(weight, x->shape[x->ndim - 1]));
+    RowArgs a;
+    bool vec;
+    fill_row_args(a, y, x, weight, scale, shift, eps, &vec);
+    return launch_row<ROW_RMS_MOD>(a, vec, (cudaStream_t)stream);
+}
+
+extern "C" int h3_ln_modulate(const h3_tensor *y, const h3_tensor *x, const h3_tensor *scale,
+                              const h3_tensor *shift, float eps, void *stream) {
+    H3_CHECK(check_bf16(y) ?: check_bf16(x) ?: check_bf16(scale) ?: check_bf16(shift));
+    H3_CHECK(check_rank(x, 2, 3) ?: check_same_shape(y, x) ?: check_same_shape(scale, x) ?:
+             check_same_shape(shift, x));
+    RowArgs a;
+    bool vec;
+    fill_row_args(a, y, x, nullptr, scale, shift, eps, &vec);
+    return launch_row<ROW_LN_MOD>(a, vec, (cudaStream_t)stream);
+}
+
+extern "C" int h3_gated_residual_rms_modulate(const h3_tensor *residual, const h3_tensor *out,
+                                              const h3_tensor *x, const h3_tensor *gate, const h3_tensor *y,
+                                              const h3_tensor *weight, const h3_tensor *scale,
+                                              const h3_tensor *shift, float eps, void *stream) {
+    H3_CHECK(check_bf16(residual) ?: check_bf16(out) ?: check_bf16(x) ?: check_bf16(gate) ?: check_bf16(y) ?:
+             check_bf16(scale) ?: check_bf16(shift));
+    H3_CHECK(check_rank(x, 2, 3) ?: check_same_shape(out, x) ?: check_same_shape(residual, x) ?:
+             check_same_shape(gate, x) ?: check_same_shape(y, x) ?: check_same_shape(scale, x) ?:
+             check_same_shape(shift, x));
+    H3_CHECK(check_weight(weight, x->shape[x->ndim - 1]));
+    RowArgs a;
+    bool vec;
+    fill_row_args(a, out, x, weight, scale, shift, eps, &vec);
+    a.gate = rowview(gate);
+    a.y = rowview(y);
+    a.residual = rowview_mut(residual);
+    vec = vec && rows_vectorizable(gate, 8) && rows_vectorizable(y, 8) && rows_vectorizable(residual, 8);
+    return launch_row<ROW_RES_RMS_MOD>(a, vec, (cudaStream_t)stream);
+}
+
+static int head_launch(const h3_tensor *out, const h3_tensor *x, const h3_tensor *weight,
+                       const h3_tensor *cos, const h3_tensor *sin, float eps, bool norm, cudaStream_t stream) {
+    // x/out are [T, P, Hs, 128] (4-D) or [S, H, 128] (3-D, seen as P = 1)
+    HeadArgs a;
+    int64_t shp[4], xs[4], os[4];
+    if (x->ndim == 4) {
+        for (int i = 0; i < 4; ++i) { shp[i] = x->shape[i]; xs[i] = x->strides[i]; os[i] = out->strides[i]; }
+    } else {
+        shp[0] = x->shape[0]; shp[1] = 1; shp[2] = x->shape[1]; shp[3] = x->shape[2];
+        xs[0] = x->strides[0]; xs[1] = 0; xs[2] = x->strides[1]; xs[3] = x->strides[2];
+        os[0] = out->strides[0]; os[1] = 0; os[2] = out->strides[1]; os[3] = out->strides[2];
+    }
+    a.x = static_cast<const __nv_bfloat16 *>(x->data);
+    a.out = static_cast<__nv_bfloat16 *>(out->data);
+    for (int i = 0; i < 4; ++i) { a.xs[i] = xs[i]; a.os[i] = os[i]; }
+    a.weight = weight ? static_cast<const __nv_bfloat16 *>(weight->data) : nullptr;
+    a.wsc = weight ? weight->strides[0] : 1;
+    a.cos = static_cast<const __nv_bfloat16 *>(cos->data);
+    a.sin = static_cast<const __nv_bfloat16 *>(sin->data);
+    a.cs0 = cos->strides[0]; a.cs1 = cos->strides[1];
+    a.ss0 = sin->strides[0]; a.ss1 = sin->strides[1];
+    a.T = shp[0]; a.P = shp[1]; a.Hs = shp[2];
+    a.half = (int)cos->shape[1];
+    a.eps = eps;
+    const int64_t rows = a.T * a.P * a.Hs;
+    if (rows == 0) return H3_OK;
+    bool vec = xs[3] == 1 && os[3] == 1 && a.cs1 == 1 && a.ss1 == 1 && aligned_to(x->data, 8) &&
+               aligned_to(out->data, 8) && aligned_to(cos->data, 8) && aligned_to(sin->data, 8);
+    for (int i = 0; i < 3; ++i) vec = vec && (xs[i] % 4 == 0) && (os[i] % 4 == 0);
+    vec = vec && a.cs0 % 4 == 0 && a.ss0 % 4 == 0;
+    const int g = grid_for(rows * 32, 256);
+    if (norm) {
+        if (vec) head_kernel<true, true><<<g, 256, 0, stream>>>(a);
+        else head_kernel<true, false><<<g, 256, 0, stream>>>(a);
+    } else {
+        if (vec) head_kernel<false, true><<<g, 256, 0, stream>>>(a);
+        else head_kernel<false, false><<<g, 256, 0, stream>>>(a);
+    }
+    return launch_status();
+}
+
+static int check_angles(const h3_tensor *cos, const h3_tensor *sin, int64_t T) {
+    H3_CHECK(check_bf16(cos) ?: check_bf16(sin));
+    if (cos->ndim != 2 || cos->shape[0] != T) return H3_ERR_BAD_SHAPE;
+    H3_CHECK(check_same_shape(cos, sin));
+    const int64_t half = cos->shape[1];
+    if (half <= 0 || half % 4 != 0 || 2 * half > 128) return H3_ERR_BAD_SHAPE;
+    return H3_OK;
+}
+
+extern "C" int h3_rope(const h3_tensor *y, const h3_tensor *x, const h3_tensor *cos, const h3_tensor *sin,
+                       void *stream) {
+    H3_CHECK(check_bf16(y) ?: check_bf16(x));
+    if (x->ndim != 3 || x->shape[2] != 128) return H3_ERR_BAD_SHAPE;
+    H3_CHECK(check_same_shape(y, x));
+    H3_CHECK(check_angles(cos, sin, x->shape[0]));
+    return head_launch(y, x, nullptr, cos, sin, 0.f, false, (cudaStream_t)stream);
+}
+
+extern "C" int h3_qk_norm_rope(const h3_tensor *out, const h3_tensor *x, const h3_tensor *weight,
+                               const h3_tensor *cos, const h3_tensor *sin, float eps, void *stream) {
+    H3_CHECK(check_bf16(out) ?: check_bf16(x));
+    if (x->ndim != 4 || x->shape[3] != 128) return H3_ERR_BAD_SHAPE;
+    H3_CHECK(check_same_shape(out, x));
+    H3_CHECK(check_weight(weight, 128));
+    H3_CHECK(check_angles(cos, sin, x->shape[0]));
+    return head_launch(out, x, weight, cos, sin, eps, true, (cudaStream_t)stream);
+}
+
+static int rope_cache_launch(const h3_tensor *out, const h3_tensor *position, const float *p0, const float *p1,
+                             const float *p2, int64_t pws, int f0, int f1, int f2, cudaStream_t stream) {
+    RopeCacheArgs a;
+    a.pos = static_cast<const double *>(position->data);
+    a.ps0 = position->strides[0];
+    a.ps1 = position->strides[1];
+    a.power[0] = p0; a.power[1] = p1; a.power[2] = p2;
+    a.pws = pws;
+    a.out = static_cast<__nv_bfloat16 *>(out->data);
+    a.os0 = out->strides[0];
+    a.os1 = out->strides[1];
+    a.T = position->shape[0];
+    a.f[0] = f0; a.f[1] = f1; a.f[2] = f2;
+    a.ftot = f0 + f1 + f2;
+    if (a.T == 0) return H3_OK;
+    rope_cache_kernel<<<grid_for(a.T * a.ftot, 256), 256, 0, stream>>>(a);
+    return launch_status();
+}
+
+extern "C" int h3_rope_cache(const h3_tensor *out, const h3_tensor *position, const h3_tensor *power,
+                             void *stream) {
+    if (!out || !position || !power || !out->data || !position->data || !power->data) return H3_ERR_NULL;
+    if (position->dtype != H3_F64 || power->dtype != H3_F32 || out->dtype != H3_BF16) return H3_ERR_BAD_DTYPE;
+    if (position->ndim != 2 || position->shape[1] != 3 || power->ndim != 1 || power->shape[0] != 16)
+        return H3_ERR_BAD_SHAPE;
+    if (out->ndim != 2 || out->shape[0] != position->shape[0] || out->shape[1] != 96) return H3_ERR_BAD_SHAPE;
+    const float *p = static_cast<const float *>(power->data);
+    return rope_cache_launch(out, position, p, p, p, power->strides[0], 16, 16, 16, (cudaStream_t)stream);
+}
+
+extern "C" int h3_rope_cache_sectioned(const h3_tensor *out, const h3_tensor *position, const h3_tensor *power,
+                                       int32_t f0, int32_t f1, int32_t f2, void *stream) {
+    if (!out || !position || !power || !out->data || !position->data || !power->data) return H3_ERR_NULL;
+    if (position->dtype != H3_F64 || power->dtype != H3_F32 || out->dtype != H3_BF16) return H3_ERR_BAD_DTYPE;
+    if (f0 <= 0 || f1 <= 0 || f2 <= 0) return H3_ERR_BAD_SHAPE;
+    const int ftot = f0 + f1 + f2;
+    if (position->ndim != 2 || position->shape[1] != 3 || power->ndim != 1 || power->shape[0] != ftot)
+        return H3_ERR_BAD_SHAPE;
+    if (out->ndim != 2 || out->shape[0] != position->shape[0] || out->shape[1] != 2 * ftot) return H3_ERR_BAD_SHAPE;
+    const float *p = static_cast<const float *>(power->data);
+    const int64_t s = power->strides[0];
+    return rope_cache_launch(out, position, p, p + f0 * s, p + (f0 + f1) * s, s, f0, f1, f2,
+                             (cudaStream_t)stream);
+}
+
+extern "C" int h3_timestep_embedding(const h3_tensor *out, const h3_tensor *t, float max_period, void *stream) {
+    if (!out || !t || !out->data || !t->data) return H3_ERR_NULL;
+    if (out->dtype != H3_F32 || t->dtype != H3_F32) return H3_ERR_BAD_DTYPE;
+    if (t->ndim != 1 || out->ndim != 2 || out->shape[0] != t->shape[0] || out->shape[1] % 2 != 0 ||
+        out->shape[1] <= 0)
+        return H3_ERR_BAD_SHAPE;
+    const int64_t n = t->shape[0], dim = out->shape[1];
+    if (n == 0) return H3_OK;
+    timestep_embedding_kernel<<<grid_for(n * dim, 256), 256, 0, (cudaStream_t)stream>>>(
+        static_cast<float *>(out->data), out->strides[0], out->strides[1], static_cast<const float *>(t->data),
+        t->strides[0], n, dim, logf(max_period));
+    return launch_status();
+}

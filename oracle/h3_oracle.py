@@ -1,0 +1,281 @@
+"""CPU oracle for the MiniMax-H3 DiT-block hot path.  TEST INFRASTRUCTURE ONLY.
+
+This module restates, in eager PyTorch on the CPU, the arithmetic of the
+reference's torch compositions for every op on the path, with each BF16
+rounding step where the reference places it.  It is the checker for the CUDA
+kernels: only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU
+baseline leg use it.  The product path never imports it.
+
+Parity is pinned: ``tests/test_oracle_golden.py`` checks these functions
+bit-for-bit against fixtures generated from the reference's own code
+(``tests/golden/make_golden.py`` imports ``tools/bench_h3_ops.py``).
+
+Reference anchors (file:line inside the reference tree; patches are cited by
+line number inside the patch file):
+
+* RMSNorm, staged BF16:        tools/bench_h3_ops.py:81-88, kernel tools/h3_pointwise.py:46-57
+* AdaLN modulate:              tools/bench_h3_ops.py:91-93, tools/h3_pointwise.py:83-97
+* RoPE (NeoX, 3 axes):         tools/bench_h3_ops.py:96-106, tools/h3_pointwise.py:199-214
+* RoPE table:                  tools/bench_h3_ops.py:109-113, patches/InfiniLM.patch:6605-6634
+* q/k norm + RoPE:             tools/bench_h3_ops.py:129-153, tools/h3_pointwise.py:262-294
+* gated residual:              tools/bench_h3_ops.py:208-218, tools/h3_pointwise.py:121-124
+* gated residual + RMS/AdaLN:  tools/bench_h3_ops.py:221-241, tools/h3_pointwise.py:150-168
+* SwiGLU:                      tools/bench_h3_ops.py:244-258, tools/h3_pointwise.py:18-22
+* attention (fp32 math):       tools/verify_attention.py:60-64, tools/h3_attention.py:25-41
+* block composition:           patches/InfiniLM.patch:1303-1397 (forward, forward_segmented)
+* MLP:                         patches/InfiniLM.patch:1172-1179 ([up; gate] rows, :5775-5784)
+* Ulysses permutations:        patches/InfiniLM.patch:895-1137
+* timestep embedding:          patches/InfiniCore.patch:2115-2137 (kernel), :2834-2845 (test formula)
+"""
+from __future__ import annotations
+
+import math
+from typing import Sequence
+
+import torch
+
+BF16 = torch.bfloat16
+
+
+def _r(t: torch.Tensor) -> torch.Tensor:
+    """Round an fp32 tensor to BF16 (round-to-nearest-even), as ``.to(bf16)``."""
+    return t.to(BF16)
+
+
+# --------------------------------------------------------------------------
+# RMSNorm / AdaLN (tools/bench_h3_ops.py:81-93)
+# --------------------------------------------------------------------------
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    """Staged BF16 RMSNorm over the last axis: sq=bf16(x*x); mean=bf16(sum/D);
+    var=bf16(mean+eps); r=bf16(1/sqrt(var)); out=bf16(bf16(x*r)*w)."""
+    xf = x.float()
+    squared = _r(xf * xf)
+    mean = _r(squared.float().sum(-1, keepdim=True) / x.shape[-1])
+    variance = _r(mean.float() + torch.tensor(eps, dtype=torch.float32))
+    reciprocal = _r(torch.rsqrt(variance.float()))
+    return _r(_r(xf * reciprocal.float()).float() * weight.float())
+
+
+def modulate(normalized: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor) -> torch.Tensor:
+    """bf16(bf16(n * bf16(1 + scale)) + shift)."""
+    factor = _r(scale.float() + 1.0)
+    return _r(_r(normalized.float() * factor.float()).float() + shift.float())
+
+
+def rms_modulate(x, weight, scale, shift, eps):
+    return modulate(rms_norm(x, weight, eps), scale, shift)
+
+
+def ln_modulate(x, scale, shift, eps):
+    """LayerNorm variant of AdaLN (mean-subtracted, no affine), the form the
+    BASELINE configs describe.  Not in the reference; defined here as torch's
+    fp32 layer_norm rounded once to BF16, then the reference's staged modulate."""
+    normalized = _r(torch.nn.functional.layer_norm(x.float(), (x.shape[-1],), eps=eps))
+    return modulate(normalized, scale, shift)
+
+
+# --------------------------------------------------------------------------
+# Residuals and SwiGLU
+# --------------------------------------------------------------------------
+def gated_residual(x, gate, y):
+    """bf16(x + bf16(gate * y)) -- torch.add(x, torch.mul(gate, y)) in BF16."""
+    return _r(x.float() + _r(gate.float() * y.float()).float())
+
+
+def gated_residual_rms_modulate(x, gate, y, weight, scale, shift, eps):
+    residual = gated_residual(x, gate, y)
+    return residual, rms_modulate(residual, weight, scale, shift, eps)
+
+
+def swiglu(up, gate):
+    """bf16(up * bf16(g / (1 + exp(-g))))."""
+    g = gate.float()
+    activated = _r(g / (1.0 + torch.exp(-g)))
+    return _r(up.float() * activated.float())
+
+
+# --------------------------------------------------------------------------
+# RoPE
+# --------------------------------------------------------------------------
+def rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """NeoX half rotation over the first 2*half channels of [T, H, D], angles
+    [T, half] in token order; the rest passes through.  Reference layout
+    half=48, D=128; the 44/42/42 extension uses half=64."""
+    half = cos.shape[-1]
+    a, b, rest = x[..., :half].float(), x[..., half:2 * half].float(), x[..., 2 * half:]
+    c = cos.float().unsqueeze(-2)
+    s = sin.float().unsqueeze(-2)
+    y0 = _r(_r(a * c).float() + _r(-b * s).float())
+    y1 = _r(_r(b * c).float() + _r(a * s).float())
+    return torch.cat([y0, y1, rest], dim=-1)
+
+
+def qk_norm_rope(x, weight, cos, sin, eps):
+    """Per-head staged RMSNorm over D then RoPE.  x [T, ..., D]; cos/sin [T, half]
+    broadcast over every middle axis."""
+    normalized = rms_norm(x, weight, eps)
+    extra = normalized.dim() - 2
+    c, s = cos, sin
+    for _ in range(extra - 1):
+        c, s = c.unsqueeze(1), s.unsqueeze(1)
+    return rope(normalized, c, s)
+
+
+def rope_powers(sections: Sequence[int] = (16, 16, 16), theta: float = 10000.0) -> list[torch.Tensor]:
+    """Per-axis fp32 powers theta ** (2k / (2 f)), k < f (torch float pow), as the
+    pipeline computes them (patches/InfiniLM.patch:7014-7025)."""
+    out = []
+    for f in sections:
+        exponent = torch.arange(0, 2 * f, 2, dtype=torch.float32) / (2 * f)
+        out.append(torch.full_like(exponent, theta) ** exponent)
+    return out
+
+
+def rotary_cache(positions: torch.Tensor, sections: Sequence[int] = (16, 16, 16),
+                 theta: float = 10000.0) -> torch.Tensor:
+    """[T, 3] positions -> [T, 2*half] BF16 = cat(cos, sin), axis-major angles
+    angle[t, off_a + k] = f32(pos[t, a]) * (1 / theta**(2k/(2 f_a))).
+    sections=(16,16,16) is the reference table (bench_h3_ops.py:109-113);
+    (22,21,21) is the full-D 44/42/42 extension."""
+    cols = []
+    for axis, power in enumerate(rope_powers(sections, theta)):
+        inverse = 1.0 / power
+        cols.append(positions[:, axis].float().unsqueeze(-1) * inverse.view(1, -1))
+    angles = torch.cat(cols, dim=-1)
+    return torch.cat((angles.cos(), angles.sin()), dim=-1).to(BF16)
+
+
+def grid_positions(t: int, h: int, w: int) -> torch.Tensor:
+    """Integer (t, h, w) latent grid enumerated t-major, as fp64 [t*h*w, 3]."""
+    tt, hh, ww = torch.meshgrid(torch.arange(t), torch.arange(h), torch.arange(w), indexing="ij")
+    return torch.stack((tt, hh, ww), -1).reshape(-1, 3).double()
+
+
+# --------------------------------------------------------------------------
+# Attention
+# --------------------------------------------------------------------------
+def attention_fp32(q, k, v, scale, chunk: int = 1024) -> torch.Tensor:
+    """softmax(q k^T * scale) v in fp32 for [B, S, H, D] inputs (the mha
+    layout); K/V length may be shorter than Q's.  Returns fp32 [B, Sq, H, D]."""
+    qf = q.float().permute(0, 2, 1, 3)
+    kf = k.float().permute(0, 2, 1, 3)
+    vf = v.float().permute(0, 2, 1, 3)
+    out = torch.empty(qf.shape, dtype=torch.float32)
+    for s in range(0, qf.shape[2], chunk):
+        logits = (qf[:, :, s:s + chunk] @ kf.transpose(-2, -1)) * scale
+        out[:, :, s:s + chunk] = torch.softmax(logits, -1) @ vf
+    return out.permute(0, 2, 1, 3)
+
+
+# --------------------------------------------------------------------------
+# Timestep embedding (patches/InfiniCore.patch:2115-2137, test :2834-2845)
+# --------------------------------------------------------------------------
+def timestep_embedding(t: torch.Tensor, dim: int, max_period: float = 10000.0) -> torch.Tensor:
+    half = dim // 2
+    exponent = -math.log(max_period) * torch.arange(half, dtype=torch.float32) / half
+    angles = t.float().unsqueeze(1) * exponent.exp().unsqueeze(0)
+    return torch.cat((angles.cos(), angles.sin()), dim=1)
+
+
+# --------------------------------------------------------------------------
+# Ulysses permutations (patches/InfiniLM.patch:895-1137), integer layout only
+# --------------------------------------------------------------------------
+def ulysses_send_blocks(local: torch.Tensor, world: int, group_start: int = 0,
+                        group_heads: int | None = None) -> torch.Tensor:
+    """[T, H, D] local tokens -> [W, T, Hs, D]: block p holds heads
+    p*Hl + group_start + j (j < Hs) of the local tokens (gather_sequence :895-910,
+    overlapped send_blocks :926-934)."""
+    tokens, heads, d = local.shape
+    hl = heads // world
+    hs = hl if group_heads is None else group_heads
+    idx = torch.tensor([p * hl + group_start + j for p in range(world) for j in range(hs)])
+    return local[:, idx].view(tokens, world, hs, d).permute(1, 0, 2, 3).contiguous()
+
+
+def ulysses_all_to_all(send: Sequence[torch.Tensor]) -> list[torch.Tensor]:
+    """Equal-split all-to-all over W ranks: recv[r][q] = send[q][r]."""
+    world = len(send)
+    return [torch.stack([send[q][r] for q in range(world)]) for r in range(world)]
+
+
+def ulysses_gather(recv: torch.Tensor) -> torch.Tensor:
+    """[W, T, Hs, D] received blocks -> [W*T, Hs, D], token axis in global order."""
+    w, t, hs, d = recv.shape
+    return recv.reshape(w * t, hs, d)
+
+
+def ulysses_scatter_back(returned: Sequence[torch.Tensor], group_heads: Sequence[int]) -> torch.Tensor:
+    """Per group g: returned[g] [W, T, Hs_g, D] (block q = heads q*Hl + off_g + h
+    of the local tokens) -> output [T, W, Hl, D] (attend_exchanged_groups :1006-1014)."""
+    w, t, _, d = returned[0].shape
+    hl = sum(group_heads)
+    out = torch.empty(t, w, hl, d, dtype=returned[0].dtype)
+    off = 0
+    for r, hs in zip(returned, group_heads):
+        out[:, :, off:off + hs] = r.permute(1, 0, 2, 3)
+        off += hs
+    return out
+
+
+# --------------------------------------------------------------------------
+# DiT block (patches/InfiniLM.patch:1303-1397)
+# --------------------------------------------------------------------------
+def linear(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """y = x W^T, BF16 in/out, fp32 accumulation (no bias on the block linears,
+    patches/InfiniLM.patch:734-741, 1163-1169)."""
+    return _r(x.float() @ weight.float().t())
+
+
+def block_forward(x: torch.Tensor, modulation: torch.Tensor, weights: dict, cos: torch.Tensor,
+                  sin: torch.Tensor, heads: int, eps: float = 1e-6, qk_eps: float = 1e-6,
+                  valid_tokens: int | None = None, norm: str = "rms") -> torch.Tensor:
+    """One DiT block on [N, Hd] tokens with one modulation row [6*Hd] (columns
+    shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp, :1313-1318).
+
+    weights: w_qkv [3*Hd, Hd] rows [q|k|v] head-major; norm_q, norm_k [D];
+    w_o [Hd, Hd]; w_gate_up [2F, Hd] rows [up; gate]; w_down [Hd, F];
+    norm1, norm2 [Hd].  cos/sin [N, half] token-ordered.  norm="ln" uses the
+    LayerNorm AdaLN variant for both norms."""
+    n, hd = x.shape
+    d = hd // heads
+    mod = modulation.view(6, hd)
+    shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = (mod[i] for i in range(6))
+    if norm == "ln":
+        normalized = ln_modulate(x, scale_msa, shift_msa, eps)
+    else:
+        normalized = rms_modulate(x, weights["norm1"], scale_msa, shift_msa, eps)
+    qkv = linear(normalized, weights["w_qkv"]).view(n, 3, heads, d)
+    q = qk_norm_rope(qkv[:, 0], weights["norm_q"], cos, sin, qk_eps)
+    k = qk_norm_rope(qkv[:, 1], weights["norm_k"], cos, sin, qk_eps)
+    v = qkv[:, 2]
+    kv = n if valid_tokens is None else valid_tokens
+    attn = _r(attention_fp32(q[None], k[None, :kv], v[None, :kv], d ** -0.5)[0]).reshape(n, hd)
+    attn_out = linear(attn, weights["w_o"])
+    residual = gated_residual(x, gate_msa, attn_out)
+    if norm == "ln":
+        normalized2 = ln_modulate(residual, scale_mlp, shift_mlp, eps)
+    else:
+        normalized2 = rms_modulate(residual, weights["norm2"], scale_mlp, shift_mlp, eps)
+    gate_up = linear(normalized2, weights["w_gate_up"])
+    f = gate_up.shape[1] // 2
+    hidden = swiglu(gate_up[:, :f], gate_up[:, f:])
+    mlp = linear(hidden, weights["w_down"])
+    return gated_residual(residual, gate_mlp, mlp)
+
+
+# --------------------------------------------------------------------------
+# Tolerance metrics
+# --------------------------------------------------------------------------
+def bf16_ulp_distance(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """Distance in BF16 units-in-the-last-place between two BF16 tensors
+    (monotone integer mapping of the bit patterns; +0 and -0 coincide)."""
+    def key(t):
+        i = t.contiguous().view(torch.int16).to(torch.int32)
+        return torch.where(i < 0, -(i & 0x7FFF), i)
+    return (key(a) - key(b)).abs()
+
+
+def max_abs_rel(out: torch.Tensor, ref: torch.Tensor) -> float:
+    """max |out - ref| / max |ref| (the block tolerance metric)."""
+    o, r = out.float(), ref.float()
+    return float((o - r).abs().max() / r.abs().max().clamp_min(1e-30))

@@ -1,0 +1,118 @@
+"""Parity of the tcgen05 projections (h3_linear*, through the C-ABI).
+
+The plain GEMM is compared with an fp32-accumulated reference rounded to BF16
+(the GEMM accumulation order is not pinned by the reference, which only checks
+its BLAS for determinism): max-abs-rel <= 1e-2 and >= 95% of outputs within 1
+BF16 ulp.  The fused epilogues must equal the unfused composition (same GEMM,
+then the pointwise op) bit for bit.
+"""
+import pytest
+import torch
+
+from oracle import h3_oracle as O
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def h3():
+    import h3b200
+    h3b200.load()
+    return h3b200
+
+
+def _ref(x, w):
+    return (x.float() @ w.float().t()).bfloat16()
+
+
+def _assert_gemm_close(y, ref):
+    rel = O.max_abs_rel(y.cpu(), ref.cpu())
+    within = float((O.bf16_ulp_distance(y.cpu(), ref.cpu()) <= 1).float().mean())
+    assert rel <= 1e-2 and within >= 0.95, f"max-abs-rel {rel:.3e}, within-1-ulp {within:.4f}"
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (1, 32, 64), (300, 384, 128), (1000, 1024, 512),
+                                   (257, 5120, 1024), (4096, 768, 5120)])
+def test_linear_shapes(h3, M, N, K):
+    torch.manual_seed(M + N + K)
+    x = torch.randn(M, K, dtype=torch.bfloat16, device=DEV)
+    w = (torch.randn(N, K, device=DEV) * 0.02).bfloat16()
+    y = h3.linear(x, w)
+    _assert_gemm_close(y, _ref(x, w))
+
+
+def test_linear_strided_rows(h3):
+    torch.manual_seed(9)
+    big = torch.randn(500, 1024 + 64, dtype=torch.bfloat16, device=DEV)
+    x = big[:, 64:]                                  # row stride 1088, 16-B aligned
+    w = (torch.randn(512, 1024, device=DEV) * 0.02).bfloat16()
+    out = torch.zeros(500, 512 + 32, dtype=torch.bfloat16, device=DEV)[:, :512]
+    h3.linear_(out, x, w)
+    _assert_gemm_close(out, _ref(x, w))
+
+
+def test_linear_deterministic(h3):
+    torch.manual_seed(10)
+    x = torch.randn(2048, 2048, dtype=torch.bfloat16, device=DEV)
+    w = (torch.randn(2048, 2048, device=DEV) * 0.02).bfloat16()
+    a = h3.linear(x, w)
+    b = h3.linear(x, w)
+    assert torch.equal(a, b)
+
+
+def test_pack_gate_up(h3):
+    F, K = 384, 128
+    w = torch.arange(2 * F, device=DEV).float().unsqueeze(1).expand(2 * F, K).bfloat16().contiguous()
+    packed = h3.pack_gate_up(w)
+    rows = packed[:, 0].float().long().cpu()
+    expect = []
+    for blk in range(F // 128):
+        expect += list(range(blk * 128, blk * 128 + 128)) + list(range(F + blk * 128, F + blk * 128 + 128))
+    assert rows.tolist() == expect
+
+
+@pytest.mark.parametrize("M,F,K", [(300, 384, 256), (1024, 1536, 1024)])
+def test_linear_swiglu_fused_equals_unfused(h3, M, F, K):
+    torch.manual_seed(M + F)
+    x = torch.randn(M, K, dtype=torch.bfloat16, device=DEV)
+    w = (torch.randn(2 * F, K, device=DEV) * 0.05).bfloat16()   # [up; gate]
+    fused = h3.linear_swiglu(x, h3.pack_gate_up(w))
+    gate_up = h3.linear(x, w)
+    unfused = h3.h3_swiglu(gate_up[:, :F], gate_up[:, F:])
+    assert torch.equal(fused, unfused)
+    ref = O.swiglu(_ref(x, w)[:, :F].cpu(), _ref(x, w)[:, F:].cpu())
+    assert O.max_abs_rel(fused.cpu(), ref) <= 2e-2
+
+
+@pytest.mark.parametrize("broadcast_gate", [True, False])
+def test_linear_gated_residual_fused_equals_unfused(h3, broadcast_gate):
+    torch.manual_seed(12)
+    M, N, K = 777, 1024, 512
+    x = torch.randn(M, K, dtype=torch.bfloat16, device=DEV)
+    w = (torch.randn(N, K, device=DEV) * 0.05).bfloat16()
+    res = torch.randn(M, N, dtype=torch.bfloat16, device=DEV) * 4
+    gate = (torch.randn(N, device=DEV) * 0.3).bfloat16() if broadcast_gate else \
+        (torch.randn(M, N, device=DEV) * 0.3).bfloat16()
+    fused = h3.linear_gated_residual(x, w, res, gate)
+    unfused = h3.h3_gated_residual(res, gate, h3.linear(x, w))
+    assert torch.equal(fused, unfused)
+
+
+def test_qkv_projection_shape_sampled(h3):
+    """The config-3 QKV projection shape, 18432 x 15360 x 5120, on sampled rows."""
+    torch.manual_seed(0)
+    M, N, K = 18432, 15360, 5120
+    x = torch.randn(M, K, dtype=torch.bfloat16, device=DEV)
+    w = (torch.randn(N, K, device=DEV) * 0.02).bfloat16()
+    y = h3.linear(x, w)
+    rows = torch.linspace(0, M - 1, 64, device=DEV).long()
+    _assert_gemm_close(y[rows], _ref(x[rows], w))
+    assert h3.load().h3_device_error() == 0
+
+
+def test_bad_k_rejected(h3):
+    x = torch.zeros(4, 100, dtype=torch.bfloat16, device=DEV)
+    w = torch.zeros(32, 100, dtype=torch.bfloat16, device=DEV)
+    with pytest.raises(RuntimeError):
+        h3.linear(x, w)
