@@ -1,0 +1,426 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 H3 DiT hot path (the 40-block
+denoising step on 18432 latent + 512 conditioning tokens).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...   (Ulysses sequence parallel)
+
+Prints ONE JSON line on rank 0.  ``value`` is seconds per step measured on the
+device with CUDA events (max over ranks), inputs already resident in HBM;
+``e2e`` is the same step through the public entry point ``DiTStep.__call__``
+with the step's input copied from pinned host memory and the output copied
+back, inside the timed region.  ``roofline`` reports the dominant kernel
+(attention), timed live here with CUDA events on its launch stream.
+``--impl reference`` times the CPU oracle (the reference's torch compositions
+restated) on a bounded sample of the same workload, on all host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "DiT s/step (40 blocks, 18432 tok)"
+UNIT = "s/step"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--blocks", type=int, default=40)
+    p.add_argument("--no-graph", action="store_true", help="eager launches instead of a CUDA graph (N=1)")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    except (OSError, ValueError):
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def workload_config(args, world):
+    return {
+        "workload": "config5: 40-block MiniMax-H3 DiT denoising step, joint sequence 18432 latent "
+                    "(32x24x24) + 512 conditioning tokens, hidden 5120, 40x128 heads, SwiGLU FFN 13824, "
+                    "timestep 500, random-init bf16 weights",
+        "model": "MiniMax-H3 DiT block stack (BASELINE config 5)",
+        "blocks": args.blocks,
+        "global_batch": 1,
+        "seq_len": 18944,
+        "parallelism": f"ulysses-sp{world}" if world > 1 else "single-gpu",
+        "l2": "no flush needed: each step streams ~63 GB of weights, far larger than the 126 MB L2",
+    }
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled with nvidia-smi during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                clk, cmax, power = float(parts[1]), float(parts[2]), float(parts[3])
+            except ValueError:
+                continue
+            mx = max(mx, cmax)
+            if power > 200:           # under load
+                sm.append(clk)
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples_under_load": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle (reference torch compositions) on a bounded sample
+# ---------------------------------------------------------------------------
+_CPU_WEIGHTS = {}
+
+
+def cpu_sample_step_seconds(sample_tokens=128, total_tokens=18944, blocks=40, seed=0):
+    """Time one block's token-local ops on `sample_tokens` tokens and the
+    attention of `sample_tokens` queries over all keys (all 40 heads), at full
+    width, with the CPU oracle; extrapolate linearly in the query count to one
+    block on all tokens and to the 40-block step.  Weights are held in fp32
+    (BF16-valued) so the timed region is the arithmetic, not dtype conversion."""
+    from oracle import h3_oracle as O
+    hd, heads, d, f = 5120, 40, 128, 13824
+    n = sample_tokens
+    if seed not in _CPU_WEIGHTS:
+        g = torch.Generator().manual_seed(seed)
+        r = lambda *s: (torch.randn(*s, generator=g) * 0.02).bfloat16().float()  # noqa: E731
+        _CPU_WEIGHTS[seed] = {"w_qkv": r(3 * hd, hd), "w_o": r(hd, hd), "w_gate_up": r(2 * f, hd),
+                              "w_down": r(hd, f),
+                              "kv": torch.randn(1, total_tokens, heads, d, generator=g).bfloat16()}
+    w = _CPU_WEIGHTS[seed]
+    g = torch.Generator().manual_seed(seed + 1)
+    ones = torch.ones(hd).bfloat16()
+    x = torch.randn(n, hd, generator=g).bfloat16()
+    mod = (torch.randn(6, hd, generator=g) * 0.3).bfloat16()
+    tbl = O.rotary_cache(O.grid_positions(1, 1, n))
+    cos, sin = tbl[:, :48], tbl[:, 48:]
+    kv = w["kv"]
+    t0 = time.perf_counter()
+    nrm = O.rms_modulate(x, ones, mod[1], mod[0], 1e-6)
+    qkv = O.linear(nrm, w["w_qkv"]).view(n, 3, heads, d)
+    q = O.qk_norm_rope(qkv[:, 0], torch.ones(d).bfloat16(), cos, sin, 1e-6)
+    O.qk_norm_rope(qkv[:, 1], torch.ones(d).bfloat16(), cos, sin, 1e-6)
+    t1 = time.perf_counter()
+    attn = O.attention_fp32(q[None], kv, kv, d ** -0.5, chunk=n).bfloat16()[0].reshape(n, hd)
+    t2 = time.perf_counter()
+    o = O.linear(attn, w["w_o"])
+    res, n2 = O.gated_residual_rms_modulate(x, mod[2], o, ones, mod[4], mod[3], 1e-6)
+    gu = O.linear(n2, w["w_gate_up"])
+    hidden = O.swiglu(gu[:, :f], gu[:, f:])
+    O.gated_residual(res, mod[5], O.linear(hidden, w["w_down"]))
+    t3 = time.perf_counter()
+    per_block = (t3 - t0) * (total_tokens / n)
+    return per_block * blocks, (t3 - t0)
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args, rank, world, local_rank, group):
+    import h3b200
+    from h3b200 import _lib
+    from h3b200.step import DiTStep, StepConfig
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    h3b200.load()
+    cfg = StepConfig(blocks=args.blocks)
+    step = DiTStep(cfg, device, world=world, rank=rank, group=group, seed=0)
+    gen = torch.Generator(device="cpu")
+    gen.manual_seed(1234)
+    x_full = torch.randn(cfg.tokens, cfg.block.hidden, generator=gen).bfloat16()
+    t = step.local
+    x_local = torch.zeros(t, cfg.block.hidden, dtype=torch.bfloat16)
+    rows = x_full[step.start:min(step.start + t, cfg.tokens)]
+    x_local[:rows.shape[0]] = rows
+    x_host = x_local.pin_memory()
+    out_host = torch.empty_like(x_host).pin_memory()
+    x_dev = step.x_dev
+    x_dev.copy_(x_host)
+
+    def sync_all():
+        torch.cuda.synchronize(device)
+        if world > 1:
+            torch.distributed.barrier(group=group)
+            torch.cuda.synchronize(device)
+
+    # count our kernel launches per step (one per C-ABI call)
+    c0 = _lib.CALLS["n"]
+    step.forward(x_dev)
+    launches_per_step = _lib.CALLS["n"] - c0
+    sync_all()
+
+    use_graph = world == 1 and not args.no_graph
+    graph = None
+    if use_graph:
+        s = torch.cuda.Stream(device)
+        s.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(s):
+            step.forward(x_dev)
+        torch.cuda.current_stream(device).wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            graph_out = step.forward(x_dev)
+
+    def one_step():
+        if graph is not None:
+            graph.replay()
+        else:
+            step.forward(x_dev)
+
+    for _ in range(args.warmup):
+        one_step()
+    sync_all()
+
+    sampler = ClockSampler() if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    stream = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sync_all()
+    e0.record(stream)
+    for _ in range(args.steps):
+        one_step()
+    e1.record(stream)
+    sync_all()
+    clocks = sampler.stop() if sampler else None
+    dev_s = e0.elapsed_time(e1) / 1e3 / args.steps
+
+    # end to end through the public entry point: pinned host in, host out
+    def e2e_step():
+        if graph is not None:
+            x_dev.copy_(x_host, non_blocking=True)
+            graph.replay()
+            out_host.copy_(graph_out, non_blocking=True)
+            stream.synchronize()
+        else:
+            step(x_host, out_host)
+
+    e2e_step()
+    sync_all()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    f1.record(stream)
+    sync_all()
+    e2e_s = f0.elapsed_time(f1) / 1e3 / args.steps
+
+    # dominant kernel, timed live on its launch stream: the step's attention call
+    ws = step.ws
+    bc = cfg.block
+    from h3b200 import ops
+    if step.sp is None:
+        qkv = ws.qkv.view(t, 3, bc.heads, bc.head_dim)
+        attn_call = lambda: ops.mha_(ws.attn.unsqueeze(0), ws.q.unsqueeze(0), ws.k.unsqueeze(0),  # noqa: E731
+                                     qkv[:, 2].unsqueeze(0), 1.0 / math.sqrt(bc.head_dim))
+        sq, sk, hh = t, cfg.tokens, bc.heads
+    else:
+        b = step.sp.bufs
+        w_ = world
+        attn_call = lambda: ops.mha_(b.attn.unsqueeze(0), b.recv[0].view(1, w_ * t, -1, bc.head_dim),  # noqa: E731
+                                     b.recv[1].view(1, w_ * t, -1, bc.head_dim)[:, :cfg.tokens],
+                                     b.recv[2].view(1, w_ * t, -1, bc.head_dim)[:, :cfg.tokens],
+                                     1.0 / math.sqrt(bc.head_dim))
+        sq, sk, hh = w_ * t, cfg.tokens, bc.heads // world
+    for _ in range(2):
+        attn_call()
+    reps = 5
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    a0.record(stream)
+    for _ in range(reps):
+        attn_call()
+    a1.record(stream)
+    torch.cuda.synchronize(device)
+    attn_ms = a0.elapsed_time(a1) / reps
+    attn_flop = 4.0 * sq * sk * bc.head_dim * hh
+
+    # GEMM share (same live method) for the breakdown
+    def time_call(fn, reps=3):
+        fn()
+        torch.cuda.synchronize(device)
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for _ in range(reps):
+            fn()
+        g1.record(stream)
+        torch.cuda.synchronize(device)
+        return g0.elapsed_time(g1) / reps
+
+    w0 = step.weights[0]
+    gemm = {
+        "qkv": (time_call(lambda: ops.linear_(ws.qkv, ws.normalized, w0.w_qkv)), 2.0 * t * 3 * bc.hidden * bc.hidden),
+        "out": (time_call(lambda: ops.linear_(ws.attn_out, ws.attn.view(t, -1), w0.w_o)), 2.0 * t * bc.hidden * bc.hidden),
+        "gate_up_swiglu": (time_call(lambda: ops.linear_swiglu(ws.normalized2, w0.w_gate_up_packed, out=ws.hidden)),
+                           2.0 * t * 2 * bc.ffn * bc.hidden),
+        "down_gated_residual": (time_call(lambda: ops.linear_gated_residual(
+            ws.hidden, w0.w_down, ws.residual, ws.residual[0], out=ws.out[1])), 2.0 * t * bc.ffn * bc.hidden),
+    }
+
+    # max over ranks
+    vals = torch.tensor([dev_s, e2e_s, attn_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX, group=group)
+    dev_s, e2e_s, attn_ms = vals.tolist()
+
+    if rank != 0:
+        return None
+    pk, pk_kind = peaks()
+    peak = pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+    achieved = attn_flop / (attn_ms * 1e-3) / 1e12
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    if os.path.exists(tpath):
+        try:
+            traffic = json.load(open(tpath)).get("fa_fwd_kernel", {}).get("bytes_per_launch_at_bench_shape")
+        except ValueError:
+            traffic = None
+    breakdown = {"attention": {"ms": round(attn_ms, 3), "tflops": round(achieved, 1), "launches_per_step": args.blocks}}
+    for k, (ms, fl) in gemm.items():
+        breakdown[k] = {"ms": round(ms, 3), "tflops": round(fl / (ms * 1e-3) / 1e12, 1),
+                        "launches_per_step": args.blocks}
+    step_flop = args.blocks * (attn_flop * world + sum(fl for _, fl in gemm.values()) * world)
+    line = {
+        "metric": METRIC, "value": round(dev_s, 5), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(dev_s * 1e3, 3), "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": workload_config(args, world),
+        "e2e": {"value": round(e2e_s, 5), "unit": UNIT,
+                "h2d_bytes_per_step": int(x_host.numel() * 2 * world),
+                "d2h_bytes_per_step": int(out_host.numel() * 2 * world)},
+        "gpu_launches": int(launches_per_step * args.steps),
+        "roofline": {"kernel": "fa_fwd_kernel (tcgen05 flash attention)", "bound": "tensor",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 4), "peak_source": f"{pk_kind} bf16_tflops (burst; kernel timed alone)",
+                     "traffic": traffic, "flop_per_launch": attn_flop, "ms_per_launch": round(attn_ms, 3)},
+        "step_tflops": round(step_flop / dev_s / 1e12, 1),
+        "kernels": breakdown,
+        "cuda_graph": graph is not None,
+        "clocks": clocks,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        torch.set_num_threads(os.cpu_count() or 1)
+        cpu_sample_step_seconds(sample_tokens=256)            # first call: weights, thread pools
+        est, spent = cpu_sample_step_seconds(sample_tokens=256)
+        line["cpu_baseline"] = {
+            "value": round(est, 2), "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"CPU oracle (reference torch compositions): one block's token-local ops on 256 of 18944 "
+                      f"tokens + attention of those 256 queries over all 18944 keys (40 heads), full widths, "
+                      f"measured {spent:.1f} s; extrapolated linearly x74 per block and x40 blocks "
+                      f"(AdaLN projection and time embedding not included)"}
+    return line
+
+
+def run_reference(args, rank):
+    """The reference arm: the CPU oracle (restated reference torch path) on the
+    host cores, each step a bounded sample of the step workload, extrapolated."""
+    if rank != 0:
+        return None
+    torch.set_num_threads(os.cpu_count() or 1)
+    for _ in range(args.warmup):
+        cpu_sample_step_seconds(sample_tokens=256)
+    ests = []
+    wall = 0.0
+    for _ in range(args.steps):
+        est, spent = cpu_sample_step_seconds(sample_tokens=256)
+        ests.append(est)
+        wall += spent
+    v = statistics.mean(ests)
+    cores = torch.get_num_threads()
+    sample = ("CPU oracle (reference torch compositions restated): per step one block's token-local ops on 256 "
+              "of 18944 tokens + attention of those 256 queries over all 18944 keys (40 heads) at full width, "
+              "extrapolated x74 per block and x40 blocks (AdaLN projection and time embedding not included)")
+    return {"metric": METRIC, "value": round(v, 2), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(v * 1e3, 1), "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "impl": "reference",
+            "config": workload_config(args, args.gpus),
+            "cpu_baseline": {"value": round(v, 2), "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": round(v, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        line = run_reference(args, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return 0
+    group = None
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=torch.device("cuda", local_rank))
+        group = torch.distributed.group.WORLD
+    try:
+        line = run_ours(args, rank, world, local_rank, group)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

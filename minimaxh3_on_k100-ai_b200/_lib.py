@@ -118,9 +118,15 @@ def check(status: int, op: str) -> None:
     raise RuntimeError(msg)
 
 
+# Number of C-ABI entry-point calls made (each launches exactly one kernel, or
+# none for an empty input); bench.py reads it to count its kernel launches.
+CALLS = {"n": 0}
+
+
 def call(name: str, *args) -> None:
     lib = load()
     conv = [ctypes.byref(a) if isinstance(a, H3Tensor) else a for a in args]
+    CALLS["n"] += 1
     check(getattr(lib, name)(*conv), name)
 
 

@@ -1,0 +1,206 @@
+"""Host composition of one MiniMax-H3 DiT block and of the 40-block denoising
+step over the sm_100a C-ABI kernels.
+
+Follows ``MiniMaxH3TransformerBlock::forward_segmented`` (patches/InfiniLM.patch:
+1353-1397) and ``MiniMaxH3Transformer::forward`` (:1626-1826):
+
+    per segment  n1  = h3_rms_modulate(x, norm1.w, scale_msa, shift_msa)      (K6)
+                 qkv = n1 W_qkv^T                                              (K10, tcgen05)
+                 q,k = h3_qk_norm_rope(qkv[q|k], norm_q/k.w, cos, sin)         (K2)
+                 a   = mha(q, k, v)                                            (K1, tcgen05)
+                 o   = a W_o^T                                                 (K10)
+    per segment  res, n2 = h3_gated_residual_rms_modulate(x, gate_msa, o, ...) (K8)
+                 h   = swiglu(n2 W_up^T, n2 W_gate^T)   (fused epilogue)       (K10+K9)
+    per segment  out = bf16(res + bf16(gate_mlp * bf16(h W_down^T)))          (K10+K7 fused)
+
+Modulation columns are ordered shift_msa, scale_msa, gate_msa, shift_mlp,
+scale_mlp, gate_mlp (:1313-1318); a segment's row is broadcast over its tokens
+with stride 0 (:1360-1364).  Under sequence parallelism (``ulysses``) the
+attention part runs on the all-to-all-exchanged heads; everything else is
+token-local.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+
+from . import ops
+
+
+@dataclass
+class Segment:
+    """Tokens [start, start+length) of this rank share modulation row ``row``
+    (MiniMaxH3ModulationSegment, patches/InfiniLM.patch:2041-2045)."""
+    start: int
+    length: int
+    row: int
+
+
+@dataclass
+class BlockWeights:
+    w_qkv: torch.Tensor          # [3*Hd, Hd], rows [q | k | v], head-major
+    norm_q: torch.Tensor         # [D]
+    norm_k: torch.Tensor         # [D]
+    w_o: torch.Tensor            # [Hd, Hd]
+    w_gate_up: torch.Tensor      # [2F, Hd], rows [up; gate] (Diffusers ff.net.0.proj order)
+    w_down: torch.Tensor         # [Hd, F]
+    norm1: torch.Tensor          # [Hd]
+    norm2: torch.Tensor          # [Hd]
+    w_adaln: torch.Tensor | None = None   # [modalities*6*Hd, Hd]
+    b_adaln: torch.Tensor | None = None   # [modalities*6*Hd]
+    w_gate_up_packed: torch.Tensor | None = field(default=None, repr=False)
+
+    def prepare(self) -> "BlockWeights":
+        """One-time weight layout for the fused SwiGLU epilogue (like the
+        reference's first-call QKV regroup, patches/InfiniLM.patch:1020-1045)."""
+        if self.w_gate_up_packed is None:
+            self.w_gate_up_packed = ops.pack_gate_up(self.w_gate_up)
+        return self
+
+
+@dataclass
+class BlockConfig:
+    hidden: int = 5120
+    heads: int = 40
+    head_dim: int = 128
+    ffn: int = 13824
+    eps: float = 1e-6
+    qk_eps: float = 1e-6
+    modalities: int = 3
+
+
+def random_block_weights(cfg: BlockConfig, device, seed: int = 0, std: float = 0.02,
+                         adaln: bool = True) -> BlockWeights:
+    """Random-init weights ~N(0, std), norm weights ones,
+    qk-norm weights ones.  Generated on the device (no checkpoint is used)."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    hd, f, d = cfg.hidden, cfg.ffn, cfg.head_dim
+
+    def rnd(*shape):
+        return (torch.randn(*shape, generator=g, device=device) * std).to(torch.bfloat16)
+
+    w = BlockWeights(
+        w_qkv=rnd(3 * hd, hd), norm_q=torch.ones(d, dtype=torch.bfloat16, device=device),
+        norm_k=torch.ones(d, dtype=torch.bfloat16, device=device), w_o=rnd(hd, hd),
+        w_gate_up=rnd(2 * f, hd), w_down=rnd(hd, f),
+        norm1=torch.ones(hd, dtype=torch.bfloat16, device=device),
+        norm2=torch.ones(hd, dtype=torch.bfloat16, device=device))
+    if adaln:
+        w.w_adaln = rnd(cfg.modalities * 6 * hd, hd)
+        w.b_adaln = rnd(cfg.modalities * 6 * hd)
+    return w.prepare()
+
+
+class Workspace:
+    """Per-shape activation buffers reused across blocks (the step allocates
+    nothing per block, which also keeps CUDA-graph capture simple)."""
+
+    def __init__(self, tokens: int, cfg: BlockConfig, device):
+        hd, f = cfg.hidden, cfg.ffn
+        e = dict(dtype=torch.bfloat16, device=device)
+        self.tokens = tokens
+        self.normalized = torch.empty(tokens, hd, **e)
+        self.qkv = torch.empty(tokens, 3 * hd, **e)
+        self.q = torch.empty(tokens, cfg.heads, cfg.head_dim, **e)
+        self.k = torch.empty(tokens, cfg.heads, cfg.head_dim, **e)
+        self.attn = torch.empty(tokens, cfg.heads, cfg.head_dim, **e)
+        self.attn_out = torch.empty(tokens, hd, **e)
+        self.residual = torch.empty(tokens, hd, **e)
+        self.normalized2 = torch.empty(tokens, hd, **e)
+        self.hidden = torch.empty(tokens, f, **e)
+        self.out = [torch.empty(tokens, hd, **e), torch.empty(tokens, hd, **e)]
+
+
+def _col(modulation: torch.Tensor, index: int, hidden: int, seg: Segment) -> torch.Tensor:
+    """Column block ``index`` of the segment's modulation row, broadcast over its tokens."""
+    row = modulation[seg.row, index * hidden:(index + 1) * hidden]
+    return row.unsqueeze(0).expand(seg.length, hidden)
+
+
+def block_forward(x: torch.Tensor, modulation: torch.Tensor, segments: list[Segment], w: BlockWeights,
+                  cos: torch.Tensor, sin: torch.Tensor, cfg: BlockConfig, ws: Workspace,
+                  out: torch.Tensor | None = None, sp=None) -> torch.Tensor:
+    """One block on this rank's tokens x [T, Hd] -> out [T, Hd].
+
+    modulation [rows, 6*Hd]; cos/sin [T, half] for this rank's tokens.  ``sp``
+    is a ``ulysses.SequenceParallel`` (None on one GPU)."""
+    t, hd = x.shape
+    h, d = cfg.heads, cfg.head_dim
+    out = ws.out[0] if out is None else out
+    for s in segments:
+        r = slice(s.start, s.start + s.length)
+        ops.h3_rms_modulate_(ws.normalized[r], x[r], w.norm1, _col(modulation, 1, hd, s),
+                             _col(modulation, 0, hd, s), cfg.eps)
+    if sp is None or sp.world == 1:
+        ops.linear_(ws.qkv, ws.normalized, w.w_qkv)
+        qkv = ws.qkv.view(t, 3, h, d)
+        ops.h3_qk_norm_rope_(ws.q.unsqueeze(1), qkv[:, 0].unsqueeze(1), w.norm_q, cos, sin, cfg.qk_eps)
+        ops.h3_qk_norm_rope_(ws.k.unsqueeze(1), qkv[:, 1].unsqueeze(1), w.norm_k, cos, sin, cfg.qk_eps)
+        ops.mha_(ws.attn.unsqueeze(0), ws.q.unsqueeze(0), ws.k.unsqueeze(0), qkv[:, 2].unsqueeze(0),
+                 1.0 / math.sqrt(d))
+        attn_flat = ws.attn.view(t, hd)
+    else:
+        attn_flat = sp.attention(ws, w, cos, sin, cfg)
+    ops.linear_(ws.attn_out, attn_flat, w.w_o)
+    for s in segments:
+        r = slice(s.start, s.start + s.length)
+        ops.h3_gated_residual_rms_modulate_(ws.residual[r], ws.normalized2[r], x[r], _col(modulation, 2, hd, s),
+                                            ws.attn_out[r], w.norm2, _col(modulation, 4, hd, s),
+                                            _col(modulation, 3, hd, s), cfg.eps)
+    ops.linear_swiglu(ws.normalized2, w.w_gate_up_packed, out=ws.hidden)
+    for s in segments:
+        r = slice(s.start, s.start + s.length)
+        ops.linear_gated_residual(ws.hidden[r], w.w_down, ws.residual[r], modulation[s.row, 5 * hd:6 * hd],
+                                  out=out[r])
+    return out
+
+
+# ---------------------------------------------------------------------------
+# step-level pieces (patches/InfiniLM.patch:1489-1517, 1718-1793)
+# ---------------------------------------------------------------------------
+@dataclass
+class TimeEmbedderWeights:
+    """fp32 time MLP: linear_1 [Hd, 256] + bias, silu, linear_2 [Hd, Hd] + bias."""
+    w1: torch.Tensor
+    b1: torch.Tensor
+    w2: torch.Tensor
+    b2: torch.Tensor
+
+
+def random_time_embedder(hidden: int, device, in_dim: int = 256, seed: int = 1) -> TimeEmbedderWeights:
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    r = lambda *s: torch.randn(*s, generator=g, device=device) * 0.02  # noqa: E731
+    return TimeEmbedderWeights(r(hidden, in_dim), r(hidden), r(hidden, hidden), r(hidden))
+
+
+def time_embedding(t: torch.Tensor, tw: TimeEmbedderWeights, in_dim: int = 256) -> torch.Tensor:
+    """temb [N, Hd] fp32 = linear_2(silu(linear_1(sinusoid(t))))  (fp32 linears are
+    library GEMMs: two tiny matrix-vector products once per step)."""
+    emb = ops.timestep_embedding(t, in_dim)
+    hidden = torch.nn.functional.silu(emb @ tw.w1.t() + tw.b1)
+    return hidden @ tw.w2.t() + tw.b2
+
+
+def adaln_modulation(temb: torch.Tensor, w: BlockWeights, cfg: BlockConfig) -> torch.Tensor:
+    """[N*modalities, 6*Hd] BF16 modulation rows of one block: silu(temb) -> bf16,
+    projected by the block's AdaLN linear (tcgen05 GEMM) plus bias
+    (MiniMaxH3AdaLNProjection::forward, patches/InfiniLM.patch:1260-1279)."""
+    activated = torch.nn.functional.silu(temb).to(torch.bfloat16)
+    mod = ops.linear(activated, w.w_adaln) + w.b_adaln
+    return mod.view(temb.shape[0] * cfg.modalities, 6 * cfg.hidden)
+
+
+def segments_from_indices(indices) -> list[Segment]:
+    """Run-length segments of per-token modulation rows (:1770-1792)."""
+    segs: list[Segment] = []
+    for i, row in enumerate(indices):
+        row = int(row)
+        if segs and segs[-1].row == row:
+            segs[-1].length += 1
+        else:
+            segs.append(Segment(i, 1, row))
+    return segs

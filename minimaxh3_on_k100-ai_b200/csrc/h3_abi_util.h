@@ -16,14 +16,23 @@
 
 namespace h3 {
 
-inline int check_bf16(const h3_tensor *t) {
-    if (!t || !t->data) return H3_ERR_NULL;
-    if (t->dtype != H3_BF16) return H3_ERR_BAD_DTYPE;
+inline int64_t numel(const h3_tensor *t) {
+    int64_t n = 1;
+    for (int i = 0; i < t->ndim; ++i) n *= t->shape[i];
+    return n;
+}
+
+// A descriptor must exist; its data pointer may be null only when it is empty.
+inline int check_desc(const h3_tensor *t, int dtype) {
+    if (!t) return H3_ERR_NULL;
+    if (t->dtype != dtype) return H3_ERR_BAD_DTYPE;
     if (t->ndim < 1 || t->ndim > H3_MAX_DIMS) return H3_ERR_BAD_SHAPE;
     for (int i = 0; i < t->ndim; ++i)
         if (t->shape[i] < 0) return H3_ERR_BAD_SHAPE;
+    if (!t->data && numel(t) != 0) return H3_ERR_NULL;
     return H3_OK;
 }
+inline int check_bf16(const h3_tensor *t) { return check_desc(t, H3_BF16); }
 
 inline int check_rank(const h3_tensor *t, int lo, int hi) {
     if (!t) return H3_ERR_NULL;

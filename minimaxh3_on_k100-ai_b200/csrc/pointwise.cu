@@ -390,9 +390,13 @@ __global__ void __launch_bounds__(256) timestep_embedding_kernel(float *out, int
         const int64_t i = idx / dim, c = idx - i * dim;
         const int64_t half = dim / 2;
         const int64_t k = c < half ? c : c - half;
-        const float freq = expf(__fdiv_rn(__fmul_rn(-log_max_period, (float)k), (float)half));
+        // exp / cos / sin evaluated in double and rounded once: the correctly
+        // rounded fp32 values, so large timesteps (t * f up to ~1e3 rad) do not
+        // amplify a 1-ulp frequency difference
+        const float expo = __fdiv_rn(__fmul_rn(-log_max_period, (float)k), (float)half);
+        const float freq = (float)exp((double)expo);
         const float angle = __fmul_rn(t[i * ts], freq);
-        out[i * os0 + c * os1] = c < half ? cosf(angle) : sinf(angle);
+        out[i * os0 + c * os1] = c < half ? (float)cos((double)angle) : (float)sin((double)angle);
     }
 }
 
@@ -517,8 +521,7 @@ static int fill_row_args(RowArgs &a, const h3_tensor *out, const h3_tensor *x, c
 }
 
 static int check_weight(const h3_tensor *w, int64_t C) {
-    if (!w || !w->data) return H3_ERR_NULL;
-    if (w->dtype != H3_BF16) return H3_ERR_BAD_DTYPE;
+    H3_CHECK(check_bf16(w));
     if (w->ndim != 1 || w->shape[0] != C) return H3_ERR_BAD_SHAPE;
     return H3_OK;
 }
@@ -667,8 +670,9 @@ static int rope_cache_launch(const h3_tensor *out, const h3_tensor *position, co
 
 extern "C" int h3_rope_cache(const h3_tensor *out, const h3_tensor *position, const h3_tensor *power,
                              void *stream) {
-    if (!out || !position || !power || !out->data || !position->data || !power->data) return H3_ERR_NULL;
-    if (position->dtype != H3_F64 || power->dtype != H3_F32 || out->dtype != H3_BF16) return H3_ERR_BAD_DTYPE;
+    H3_CHECK(check_desc(out, H3_BF16));
+    H3_CHECK(check_desc(position, H3_F64));
+    H3_CHECK(check_desc(power, H3_F32));
     if (position->ndim != 2 || position->shape[1] != 3 || power->ndim != 1 || power->shape[0] != 16)
         return H3_ERR_BAD_SHAPE;
     if (out->ndim != 2 || out->shape[0] != position->shape[0] || out->shape[1] != 96) return H3_ERR_BAD_SHAPE;
@@ -678,8 +682,9 @@ extern "C" int h3_rope_cache(const h3_tensor *out, const h3_tensor *position, co
 
 extern "C" int h3_rope_cache_sectioned(const h3_tensor *out, const h3_tensor *position, const h3_tensor *power,
                                        int32_t f0, int32_t f1, int32_t f2, void *stream) {
-    if (!out || !position || !power || !out->data || !position->data || !power->data) return H3_ERR_NULL;
-    if (position->dtype != H3_F64 || power->dtype != H3_F32 || out->dtype != H3_BF16) return H3_ERR_BAD_DTYPE;
+    H3_CHECK(check_desc(out, H3_BF16));
+    H3_CHECK(check_desc(position, H3_F64));
+    H3_CHECK(check_desc(power, H3_F32));
     if (f0 <= 0 || f1 <= 0 || f2 <= 0) return H3_ERR_BAD_SHAPE;
     const int ftot = f0 + f1 + f2;
     if (position->ndim != 2 || position->shape[1] != 3 || power->ndim != 1 || power->shape[0] != ftot)
@@ -692,8 +697,8 @@ extern "C" int h3_rope_cache_sectioned(const h3_tensor *out, const h3_tensor *po
 }
 
 extern "C" int h3_timestep_embedding(const h3_tensor *out, const h3_tensor *t, float max_period, void *stream) {
-    if (!out || !t || !out->data || !t->data) return H3_ERR_NULL;
-    if (out->dtype != H3_F32 || t->dtype != H3_F32) return H3_ERR_BAD_DTYPE;
+    H3_CHECK(check_desc(out, H3_F32));
+    H3_CHECK(check_desc(t, H3_F32));
     if (t->ndim != 1 || out->ndim != 2 || out->shape[0] != t->shape[0] || out->shape[1] % 2 != 0 ||
         out->shape[1] <= 0)
         return H3_ERR_BAD_SHAPE;

@@ -1,0 +1,110 @@
+"""The 40-block DiT denoising step on 1..W GPUs.
+
+Mirrors ``MiniMaxH3Transformer::forward`` (patches/InfiniLM.patch:1626-1826)
+for the parts on the hot path: RoPE table for the joint sequence, time
+embedding at the step's timestep, every block's AdaLN modulation computed up
+front (the batched AdaLN of :1718-1761), run-length modulation segments of the
+local tokens (:1765-1792), then the block loop.  Under sequence parallelism
+rank r runs the loop on its T = ceil(S/W) tokens and the blocks exchange heads
+through ``ulysses``.
+
+Inputs are the joint sequence's hidden states (video latent tokens followed by
+conditioning tokens) already at model width, as BASELINE config 5 specifies;
+weights are random-init (no checkpoint).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+
+from . import ops
+from .block import (BlockConfig, Segment, Workspace, adaln_modulation, block_forward, random_block_weights,
+                    random_time_embedder, segments_from_indices, time_embedding)
+from .ulysses import SequenceParallel, local_rows
+
+VIDEO_TAG, TEXT_TAG = 0, 2   # token tags; adaln row = 3 * timestep_index + tag (:1695-1697)
+
+
+@dataclass
+class StepConfig:
+    blocks: int = 40
+    video_grid: tuple = (32, 24, 24)
+    cond_tokens: int = 512
+    timestep: float = 500.0
+    block: BlockConfig = field(default_factory=BlockConfig)
+
+    @property
+    def video_tokens(self) -> int:
+        t, h, w = self.video_grid
+        return t * h * w
+
+    @property
+    def tokens(self) -> int:
+        return self.video_tokens + self.cond_tokens
+
+
+def joint_positions(cfg: StepConfig) -> torch.Tensor:
+    """[S, 3] fp64: the video latent grid enumerated t-major, then conditioning
+    token j at (j, j, j) (text tokens advance all three axes together)."""
+    t, h, w = cfg.video_grid
+    tt, hh, ww = torch.meshgrid(torch.arange(t), torch.arange(h), torch.arange(w), indexing="ij")
+    video = torch.stack((tt, hh, ww), -1).reshape(-1, 3)
+    j = torch.arange(cfg.cond_tokens)
+    cond = torch.stack((j, j, j), -1)
+    return torch.cat([video, cond]).double()
+
+
+class DiTStep:
+    """One denoising step of the block stack.  ``forward`` takes this rank's
+    tokens [T, Hd] on the device; ``__call__`` is the end-to-end entry point
+    (host tensor in, host tensor out)."""
+
+    def __init__(self, cfg: StepConfig, device, world: int = 1, rank: int = 0, group=None, seed: int = 0):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        bc = cfg.block
+        self.world, self.rank = world, rank
+        self.local, start, padded = local_rows(cfg.tokens, world, rank)
+        self.start = start
+        self.weights = [random_block_weights(bc, self.device, seed=seed + 1000 * i) for i in range(cfg.blocks)]
+        self.time = random_time_embedder(bc.hidden, self.device, seed=seed + 7)
+        # per-token tables of the local rows; padded rows reuse row 0 (:1706-1710)
+        pos = joint_positions(cfg)
+        tags = torch.cat([torch.full((cfg.video_tokens,), VIDEO_TAG), torch.full((cfg.cond_tokens,), TEXT_TAG)])
+        idx = torch.arange(start, start + self.local)
+        idx = torch.where(idx < cfg.tokens, idx, torch.zeros_like(idx))
+        power = ops.rope_powers((16, 16, 16), device=self.device)[:16].contiguous()
+        table = ops.h3_rope_cache(pos[idx].to(self.device), power)
+        self.cos, self.sin = table[:, :48], table[:, 48:]
+        self.segments: list[Segment] = segments_from_indices((3 * 0 + tags[idx]).tolist())
+        self.ws = Workspace(self.local, bc, self.device)
+        self.sp = None
+        if world > 1:
+            self.sp = SequenceParallel(world, rank, group, cfg.tokens, self.local, bc.heads, bc.head_dim,
+                                       self.device)
+        self.timestep = torch.full((1,), cfg.timestep, dtype=torch.float32, device=self.device)
+        self.x_dev = torch.empty(self.local, bc.hidden, dtype=torch.bfloat16, device=self.device)
+
+    def modulations(self, timestep: torch.Tensor) -> list[torch.Tensor]:
+        temb = time_embedding(timestep, self.time)
+        return [adaln_modulation(temb, w, self.cfg.block) for w in self.weights]
+
+    def forward(self, x: torch.Tensor, timestep: torch.Tensor | None = None) -> torch.Tensor:
+        ts = self.timestep if timestep is None else timestep
+        mods = self.modulations(ts)
+        h = x
+        for i, w in enumerate(self.weights):
+            h = block_forward(h, mods[i], self.segments, w, self.cos, self.sin, self.cfg.block, self.ws,
+                              out=self.ws.out[i % 2], sp=self.sp)
+        return h
+
+    def __call__(self, x_host: torch.Tensor, out_host: torch.Tensor | None = None) -> torch.Tensor:
+        """End to end: host (pinned) tokens in, host tokens out."""
+        self.x_dev.copy_(x_host, non_blocking=True)
+        y = self.forward(self.x_dev)
+        if out_host is None:
+            out_host = torch.empty(y.shape, dtype=y.dtype, pin_memory=True)
+        out_host.copy_(y, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        return out_host

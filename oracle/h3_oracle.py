@@ -226,11 +226,23 @@ def linear(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     return _r(x.float() @ weight.float().t())
 
 
+def token_modulation(modulation: torch.Tensor, segments, n: int) -> torch.Tensor:
+    """Per-token modulation [n, 6*Hd] from a table [rows, 6*Hd] and run-length
+    segments (start, length, row) (the gather_rows path, patches/InfiniLM.patch:1306-1318)."""
+    if modulation.dim() == 1:
+        return modulation.unsqueeze(0).expand(n, -1)
+    rows = torch.empty(n, dtype=torch.long)
+    for start, length, row in segments:
+        rows[start:start + length] = row
+    return modulation[rows]
+
+
 def block_forward(x: torch.Tensor, modulation: torch.Tensor, weights: dict, cos: torch.Tensor,
                   sin: torch.Tensor, heads: int, eps: float = 1e-6, qk_eps: float = 1e-6,
-                  valid_tokens: int | None = None, norm: str = "rms") -> torch.Tensor:
-    """One DiT block on [N, Hd] tokens with one modulation row [6*Hd] (columns
-    shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp, :1313-1318).
+                  valid_tokens: int | None = None, norm: str = "rms", segments=None) -> torch.Tensor:
+    """One DiT block on [N, Hd] tokens.  ``modulation`` is one row [6*Hd] or a
+    table [rows, 6*Hd] addressed by ``segments`` [(start, length, row)]; columns
+    are shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp (:1313-1318).
 
     weights: w_qkv [3*Hd, Hd] rows [q|k|v] head-major; norm_q, norm_k [D];
     w_o [Hd, Hd]; w_gate_up [2F, Hd] rows [up; gate]; w_down [Hd, F];
@@ -238,8 +250,8 @@ def block_forward(x: torch.Tensor, modulation: torch.Tensor, weights: dict, cos:
     LayerNorm AdaLN variant for both norms."""
     n, hd = x.shape
     d = hd // heads
-    mod = modulation.view(6, hd)
-    shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = (mod[i] for i in range(6))
+    mod = token_modulation(modulation, segments, n).reshape(n, 6, hd)
+    shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = (mod[:, i] for i in range(6))
     if norm == "ln":
         normalized = ln_modulate(x, scale_msa, shift_msa, eps)
     else:

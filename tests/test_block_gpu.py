@@ -1,0 +1,98 @@
+"""One DiT block and a short block stack on one GPU against the CPU oracle.
+
+Tolerance: max-abs-rel <= 2e-2 per block output, where
+max-abs-rel = max|out - ref| / max|ref|.  The GEMM accumulation order is the
+only unpinned arithmetic (the reference's BLAS is not bitwise specified), so
+the block is compared by tolerance; repeated runs must be bitwise identical.
+"""
+import dataclasses
+
+import pytest
+import torch
+
+from oracle import h3_oracle as O
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def h3():
+    import h3b200
+    import h3b200.block  # noqa: F401
+    h3b200.load()
+    return h3b200
+
+
+def _oracle_weights(w):
+    return {k: getattr(w, k).cpu() for k in ("w_qkv", "norm_q", "norm_k", "w_o", "w_gate_up", "w_down",
+                                              "norm1", "norm2")}
+
+
+def _run_block(h3, cfg, tokens, segments, rows, seed=0, grid=None):
+    from h3b200.block import Segment, Workspace, block_forward, random_block_weights
+    torch.manual_seed(seed)
+    w = random_block_weights(cfg, DEV, seed=seed, adaln=False)
+    # non-trivial norm weights
+    for name in ("norm1", "norm2"):
+        getattr(w, name).copy_((torch.randn(cfg.hidden) * 0.1 + 1).bfloat16())
+    for name in ("norm_q", "norm_k"):
+        getattr(w, name).copy_((torch.randn(cfg.head_dim) * 0.1 + 1).bfloat16())
+    x = torch.randn(tokens, cfg.hidden).bfloat16()
+    mod = (torch.randn(rows, 6 * cfg.hidden) * 0.3).bfloat16()
+    pos = O.grid_positions(*grid) if grid else torch.stack([torch.arange(tokens)] * 3, -1).double()
+    table = O.rotary_cache(pos[:tokens])
+    cos, sin = table[:, :48], table[:, 48:]
+    ws = Workspace(tokens, cfg, DEV)
+    segs = [Segment(*s) for s in segments]
+    out = block_forward(x.to(DEV), mod.to(DEV), segs, w, cos.to(DEV), sin.to(DEV), cfg, ws).clone()
+    ref = O.block_forward(x, mod, _oracle_weights(w), cos, sin, cfg.heads, cfg.eps, cfg.qk_eps,
+                          segments=segments)
+    return out, ref, (x, mod, w, cos, sin, ws, segs)
+
+
+def test_block_small(h3):
+    from h3b200.block import BlockConfig
+    cfg = BlockConfig(hidden=512, heads=4, ffn=1536)
+    out, ref, _ = _run_block(h3, cfg, 300, [(0, 300, 0)], 1)
+    assert O.max_abs_rel(out.cpu(), ref) <= 2e-2
+
+
+def test_block_two_segments(h3):
+    """Video tokens and conditioning tokens with different modulation rows (config 5 layout)."""
+    from h3b200.block import BlockConfig
+    cfg = BlockConfig(hidden=1024, heads=8, ffn=2816)
+    out, ref, _ = _run_block(h3, cfg, 640, [(0, 512, 0), (512, 128, 2)], 3, seed=1)
+    assert O.max_abs_rel(out.cpu(), ref) <= 2e-2
+
+
+def test_block_config3_width(h3):
+    """Config-3 widths (hidden 5120, 40 heads x 128, FFN 13824) on a 576-token slice
+    of the (32, 24, 24) latent grid."""
+    from h3b200.block import BlockConfig
+    cfg = BlockConfig()
+    out, ref, (x, mod, w, cos, sin, ws, segs) = _run_block(h3, cfg, 576, [(0, 576, 0)], 1, seed=3,
+                                                            grid=(1, 24, 24))
+    assert O.max_abs_rel(out.cpu(), ref) <= 2e-2
+    from h3b200.block import block_forward
+    again = block_forward(x.to(DEV), mod.to(DEV), segs, w, cos.to(DEV), sin.to(DEV), cfg, ws).clone()
+    assert torch.equal(out, again), "block is not deterministic"
+
+
+def test_step_short_stack(h3):
+    """Three blocks of the step class (joint video + conditioning sequence, two
+    segments, AdaLN from the time embedding) against the oracle block loop."""
+    from h3b200.block import BlockConfig
+    from h3b200.step import DiTStep, StepConfig
+    cfg = StepConfig(blocks=3, video_grid=(2, 8, 16), cond_tokens=64, block=BlockConfig(hidden=512, heads=4, ffn=1536))
+    step = DiTStep(cfg, DEV, seed=5)
+    torch.manual_seed(0)
+    x = torch.randn(cfg.tokens, 512).bfloat16()
+    out = step.forward(x.to(DEV)).clone()
+    mods = [m.cpu() for m in step.modulations(step.timestep)]
+    segs = [(s.start, s.length, s.row) for s in step.segments]
+    h = x
+    for i, w in enumerate(step.weights):
+        h = O.block_forward(h, mods[i], _oracle_weights(w), step.cos.cpu(), step.sin.cpu(), 4, segments=segs)
+    assert O.max_abs_rel(out.cpu(), h) <= 2e-2
+    assert h3.load().h3_device_error() == 0

@@ -62,14 +62,14 @@ def test_linear_deterministic(h3):
 
 
 def test_pack_gate_up(h3):
+    torch.manual_seed(2)
     F, K = 384, 128
-    w = torch.arange(2 * F, device=DEV).float().unsqueeze(1).expand(2 * F, K).bfloat16().contiguous()
+    w = torch.randn(2 * F, K, dtype=torch.bfloat16, device=DEV)
     packed = h3.pack_gate_up(w)
-    rows = packed[:, 0].float().long().cpu()
-    expect = []
+    order = []
     for blk in range(F // 128):
-        expect += list(range(blk * 128, blk * 128 + 128)) + list(range(F + blk * 128, F + blk * 128 + 128))
-    assert rows.tolist() == expect
+        order += list(range(blk * 128, blk * 128 + 128)) + list(range(F + blk * 128, F + blk * 128 + 128))
+    assert torch.equal(packed, w[torch.tensor(order, device=DEV)])
 
 
 @pytest.mark.parametrize("M,F,K", [(300, 384, 256), (1024, 1536, 1024)])
@@ -112,7 +112,9 @@ def test_qkv_projection_shape_sampled(h3):
 
 
 def test_bad_k_rejected(h3):
-    x = torch.zeros(4, 100, dtype=torch.bfloat16, device=DEV)
-    w = torch.zeros(32, 100, dtype=torch.bfloat16, device=DEV)
+    x = torch.zeros(4, 96, dtype=torch.bfloat16, device=DEV)      # K not a multiple of 64
+    w = torch.zeros(32, 96, dtype=torch.bfloat16, device=DEV)
     with pytest.raises(RuntimeError):
         h3.linear(x, w)
+    with pytest.raises(ValueError):                               # K mismatch
+        h3.linear(x, torch.zeros(32, 64, dtype=torch.bfloat16, device=DEV))
