@@ -44,6 +44,9 @@ def parse():
     p.add_argument("--blocks", type=int, default=40)
     p.add_argument("--no-graph", action="store_true", help="eager launches instead of a CUDA graph (N=1)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--workload", choices=["step", "attention", "pointwise"], default="step",
+                   help="step: BASELINE config 5 (default, the headline); attention: config 2; "
+                        "pointwise: config 1 op set")
     return p.parse_args()
 
 
@@ -395,11 +398,172 @@ def run_reference(args, rank):
             "e2e": {"value": round(v, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+# ---------------------------------------------------------------------------
+# sub-workloads: config 2 (attention) and config 1 (pointwise op set), one GPU
+# ---------------------------------------------------------------------------
+def _timed(fn, reps, stream):
+    fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(reps):
+        fn()
+    b.record(stream)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def run_attention(args):
+    """non-causal attention, Q,K,V [1, 40, 18432, 128] (passed in
+    the mha [B, S, H, D] layout), scale 1/sqrt(128).  Inputs (3 x 189 MB) exceed L2."""
+    import h3b200
+    from h3b200 import _lib, ops
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    h3b200.load()
+    S, H, D = 18432, 40, 128
+    g = torch.Generator(device=device).manual_seed(0)
+    q, k, v = (torch.randn(1, S, H, D, generator=g, device=device).bfloat16() for _ in range(3))
+    out = torch.empty_like(q)
+    flop = 4.0 * S * S * D * H
+    stream = torch.cuda.current_stream(device)
+    for _ in range(args.warmup):
+        ops.mha_(out, q, k, v)
+    sampler = ClockSampler()
+    sampler.start()
+    time.sleep(0.3)
+    c0 = _lib.CALLS["n"]
+    ms = _timed(lambda: ops.mha_(out, q, k, v), args.steps, stream)
+    launches = _lib.CALLS["n"] - c0
+    clocks = sampler.stop()
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    ho = torch.empty_like(hq).pin_memory()
+
+    def e2e():
+        dq, dk, dv = (t.to(device, non_blocking=True) for t in (hq, hk, hv))
+        ho.copy_(ops.mha(dq, dk, dv), non_blocking=True)
+        stream.synchronize()
+    e2e_ms = _timed(e2e, args.steps, stream)
+    pk, kind = peaks()
+    achieved = flop / (ms * 1e-3) / 1e12
+    line = {"metric": "attn TFLOP/s (config 2: [1,40,18432,128] non-causal)", "value": round(achieved, 1),
+            "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "config2: non-causal attention B=1 H=40 S=18432 D=128, bf16, fp32 softmax",
+                       "l2": "inputs 3 x 189 MB > 126 MB L2"},
+            "e2e": {"value": round(flop / (e2e_ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": 3 * q.numel() * 2, "d2h_bytes_per_step": out.numel() * 2},
+            "gpu_launches": launches,
+            "roofline": {"kernel": "fa_fwd_kernel", "bound": "tensor", "achieved": round(achieved, 1),
+                         "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": round(achieved / pk["bf16_tflops"], 4),
+                         "peak_source": f"{kind} bf16_tflops (burst)", "traffic": _ncu_traffic("fa_fwd_kernel")},
+            "clocks": clocks}
+    if not args.no_cpu_baseline:
+        from oracle import h3_oracle as O
+        torch.set_num_threads(os.cpu_count() or 1)
+        qc, kc, vc = hq[:, :256], hk, hv
+        O.attention_fp32(qc[:, :16], kc, vc, D ** -0.5)
+        t0 = time.perf_counter()
+        O.attention_fp32(qc, kc, vc, D ** -0.5, chunk=256)
+        spent = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": round(flop / (spent * S / 256) / 1e12, 4), "unit": "TFLOP/s",
+                                "cores": torch.get_num_threads(), "kind": "port",
+                                "sample": f"oracle fp32 attention of 256 of 18432 queries over all keys, 40 heads "
+                                          f"({spent:.1f} s), extrapolated x72"}
+    return line
+
+
+POINTWISE_BYTES = {  # algorithmic bytes at config 1 (bf16)
+    "qk_norm_rope": 119_013_376, "rms_modulate": 58_731_008, "swiglu": 239_075_328,
+    "gated_residual": 88_083_968, "gated_residual_rms_modulate": 117_440_512 + 2 * 3584,
+}
+
+
+def run_pointwise(args):
+    """BASELINE config 1 op set at its shapes; GB/s of algorithmic bytes per op."""
+    import h3b200
+    from h3b200 import _lib, ops
+    from oracle import h3_oracle as O
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    h3b200.load()
+    g = torch.Generator(device=device).manual_seed(0)
+    S, H, D, C, F = 8192, 14, 128, 1792, 4864
+    r = lambda *s: torch.randn(*s, generator=g, device=device).bfloat16()  # noqa: E731
+    q, k = r(S, H, D), r(S, H, D)
+    qw = (r(D) * 0.1 + 1).bfloat16()
+    table = ops.h3_rope_cache(O.grid_positions(8, 32, 32).to(device), ops.rope_powers(device=device)[:16].contiguous())
+    cos, sin = table[:, :48], table[:, 48:]
+    x, y = r(S, C), r(S, C)
+    sc, sh, gate, nw = (r(C) * 0.1).bfloat16(), (r(C) * 0.1).bfloat16(), (r(C) * 0.1).bfloat16(), r(C)
+    a, b = r(S, F), r(S, F)
+    qo, ko, xo, ro, fo = torch.empty_like(q), torch.empty_like(k), torch.empty_like(x), torch.empty_like(x), \
+        torch.empty_like(a)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)   # 256 MB > L2
+    ops_ = {
+        "qk_norm_rope": lambda: (ops.h3_qk_norm_rope_(qo.unsqueeze(1), q.unsqueeze(1), qw, cos, sin, 1e-6),
+                                 ops.h3_qk_norm_rope_(ko.unsqueeze(1), k.unsqueeze(1), qw, cos, sin, 1e-6)),
+        "rms_modulate": lambda: ops.h3_rms_modulate_(xo, x, nw, sc, sh, 1e-6),
+        "swiglu": lambda: ops.h3_swiglu_(fo, a, b),
+        "gated_residual": lambda: ops.h3_gated_residual_(xo, x, gate, y),
+        "gated_residual_rms_modulate": lambda: ops.h3_gated_residual_rms_modulate_(ro, xo, x, gate, y, nw, sc, sh,
+                                                                                    1e-6),
+    }
+    stream = torch.cuda.current_stream(device)
+    pk, kind = peaks()
+    res = {}
+    c0 = _lib.CALLS["n"]
+    for name, fn in ops_.items():
+        for _ in range(args.warmup):
+            fn()
+        # flush L2 between timed launches (flush not timed).  No host sync inside the
+        # loop: the host enqueues ahead while the 256 MB flush runs, so the events
+        # bracket device time only, not Python/ctypes launch latency.
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+        torch.cuda.synchronize()
+        for e0, e1 in evs:
+            flush.zero_()
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        ms = sum(e0.elapsed_time(e1) for e0, e1 in evs) / args.steps
+        gbs = POINTWISE_BYTES[name] / (ms * 1e-3) / 1e9
+        res[name] = {"us": round(ms * 1e3, 2), "GB/s": round(gbs, 1), "frac": round(gbs / pk["hbm_gbs"], 3)}
+    launches = _lib.CALLS["n"] - c0
+    mean = statistics.mean(v["GB/s"] for v in res.values())
+    top = max(res, key=lambda n: res[n]["us"])
+    return {"metric": "pointwise GB/s (config 1 op set, mean over ops)", "value": round(mean, 1), "unit": "GB/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "config1: q/k [8192,14,128] norm+RoPE, AdaLN [8192,1792], SwiGLU [8192,4864], "
+                                   "gated residual [8192,1792]", "l2": "256 MB buffer written between timed launches"},
+            "gpu_launches": launches, "ops": res,
+            "roofline": {"kernel": top, "bound": "hbm", "achieved": res[top]["GB/s"], "peak": pk["hbm_gbs"],
+                         "unit": "GB/s", "frac": res[top]["frac"], "peak_source": f"{kind} hbm_gbs",
+                         "traffic": _ncu_traffic(top)}}
+
+
+def _ncu_traffic(kernel):
+    tpath = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    try:
+        return json.load(open(tpath)).get(kernel, {}).get("bytes_per_launch_at_bench_shape")
+    except (OSError, ValueError):
+        return None
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.workload != "step" and args.impl == "ours":
+        if rank == 0:
+            line = run_attention(args) if args.workload == "attention" else run_pointwise(args)
+            print(json.dumps(line), flush=True)
+        return 0
     if args.impl == "reference":
         line = run_reference(args, rank)
         if line is not None:

@@ -72,6 +72,12 @@ const char *h3_status_string(int status);
  * counterpart (the reference's waits are unbounded). */
 int h3_device_error(void);
 
+/* Failure-detection self test: launches one CTA that waits, with a limit of
+ * limit_ns (at most 1 s), on a barrier nothing arrives at.  The wait gives up,
+ * the kernel ends normally, and the next h3_device_error() returns
+ * H3_ERR_TIMEOUT.  No fault, trap or hang is involved.  No reference counterpart. */
+int h3_selftest_wait_timeout(uint64_t limit_ns, void *stream);
+
 /* ---------------- fused pointwise ops (BF16, reference rounding) ---------------- */
 
 /* y = staged-BF16 RMSNorm(x) * weight over the last axis.  x, y [S,C] or [B,S,C]; weight [C]. */

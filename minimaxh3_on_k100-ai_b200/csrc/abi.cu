@@ -1,5 +1,6 @@
 // Library-wide C-ABI entry points: version, status strings, device error word.
 #include "h3_abi_util.h"
+#include "sm100_ptx.cuh"
 
 extern "C" unsigned int h3_attention_device_error_read_and_clear(void);
 extern "C" unsigned int h3_gemm_device_error_read_and_clear(void);
@@ -26,6 +27,31 @@ extern "C" const char *h3_status_string(int status) {
 // since the last call, H3_ERR_LAUNCH if the device reports an error, else H3_OK.
 extern "C" int h3_device_error(void) {
     if (cudaDeviceSynchronize() != cudaSuccess) return H3_ERR_LAUNCH;
-    const unsigned int w = h3_attention_device_error_read_and_clear() | h3_gemm_device_error_read_and_clear();
+    unsigned int own = 0, zero = 0;
+    cudaMemcpyFromSymbol(&own, h3::g_h3_device_error, sizeof(own));
+    cudaMemcpyToSymbol(h3::g_h3_device_error, &zero, sizeof(zero));
+    const unsigned int w = own | h3_attention_device_error_read_and_clear() | h3_gemm_device_error_read_and_clear();
     return w ? H3_ERR_TIMEOUT : H3_OK;
+}
+
+namespace {
+// One thread waits on an mbarrier that nothing ever arrives at, with a short
+// limit: the bounded-wait path must give up, record the expiry in the device
+// error word and let the kernel finish, leaving the context usable.
+__global__ void wait_timeout_selftest_kernel(uint64_t limit_ns) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        h3::mbar_init(&bar, 1);
+        h3::fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) h3::mbar_wait_ns(&bar, 0, nullptr, limit_ns);
+    __syncthreads();
+}
+}  // namespace
+
+extern "C" int h3_selftest_wait_timeout(uint64_t limit_ns, void *stream) {
+    if (limit_ns == 0 || limit_ns > 1000000000ull) return H3_ERR_UNSUPPORTED;
+    wait_timeout_selftest_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(limit_ns);
+    return h3::launch_status();
 }

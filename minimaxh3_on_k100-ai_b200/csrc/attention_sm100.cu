@@ -6,7 +6,7 @@
 //   O = sum P_bf16 V / sum P  (fp32 accumulation), keys masked by K's length.
 //
 // One CTA owns two 128-row Q tiles of one (batch, head) and streams the K/V tiles
-// of 128 keys through a 3-slot TMA ring (no multicast).  Warp roles (384 threads):
+// of 128 keys through a 5-slot TMA ring (no multicast).  Warp roles (384 threads):
 //   warp 0        TMA producer (one elected lane)
 //   warp 1        tcgen05.mma issuer (one lane) and TMEM owner
 //   warps 4..7    softmax + correction + epilogue for Q tile 0
@@ -14,9 +14,17 @@
 // TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512), fp32,
 // one query row per TMEM lane.  The two tiles ping-pong: while one softmax
 // warpgroup exponentiates its S, the tensor core computes the other tile's S or
-// P V.  P is written by the softmax threads as BF16 into shared memory in the
-// 128B-swizzled K-major layout and consumed by an SS MMA; V is the MN-major B
-// operand.  The running max is updated lazily (only when it grows by more than
+// P V.  P is written by the softmax threads as packed BF16 pairs back into the
+// first 64 columns of their own S region (tcgen05.st) and consumed from TMEM by
+// a TS MMA (A operand in tensor memory); V is the MN-major B operand in shared
+// memory.  Before S_t(j+1) overwrites that region the MMA warp waits for the
+// commit of P_t(j) V_j, which is already in flight behind the other tile's PV,
+// so the tensor pipe does not drain.  A fixed share of the exponentials (3 of
+// every 8 key pairs of a full tile) is computed on the FMA pipe with a
+// Cody-Waite split 2^x = 2^round(x) * 2^f, f in [-1/2, 1/2], and a degree-3
+// polynomial for 2^f fitted here by Lawson's minimax iteration (max relative
+// error 7.5e-5, far below the BF16 rounding P receives), the rest on the MUFU
+// ex2 unit, balancing the two pipes.  The running max is updated lazily (only when it grows by more than
 // 2^8 in the exp2 domain), so O is rescaled rarely; the normalisation uses the
 // same stale max in numerator and denominator, so the result is unchanged up to
 // fp32 rounding.  The epilogue divides by the row sum, rounds to BF16 and writes
@@ -36,17 +44,18 @@ constexpr int BM = 128;                       // query rows per tile
 constexpr int BN = 128;                       // keys per K/V tile
 constexpr int HD = 128;                       // head dim
 constexpr int NQ = 2;                         // Q tiles per CTA
-constexpr int STAGES = 3;                     // K/V ring slots
+constexpr int STAGES = 5;                     // K/V ring slots
 constexpr int TILE = BM * HD * 2;             // 32 KB: one 128x128 BF16 tile
 constexpr int HALF = TILE / 2;                // 16 KB: 64 columns (one 128B swizzle span)
 constexpr int THREADS = 384;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr float RESCALE_THRESHOLD = 8.0f;     // log2 domain
 
+constexpr int POLY_PAIRS = 3;                 // of every 8 key pairs, exponentiated on the FMA pipe
+
 constexpr int OFF_Q = 0;
 constexpr int OFF_KV = OFF_Q + NQ * TILE;
-constexpr int OFF_P = OFF_KV + STAGES * TILE;
-constexpr int OFF_BAR = OFF_P + NQ * TILE;
+constexpr int OFF_BAR = OFF_KV + STAGES * TILE;
 constexpr int NUM_BARS = 1 + 2 * STAGES + 3 * NQ;
 constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 16 + 1024;  // + tmem slot, abort flag, alignment slack
 
@@ -60,6 +69,20 @@ __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// 2^x on the FMA pipe: x = n + f with n = round(x) (the 1.5*2^23 addition
+// leaves n in the low mantissa bits), 2^f by a degree-3 polynomial on
+// [-1/2, 1/2], then n is added to the exponent field.  x is clamped at -126 so
+// the exponent never wraps (the result is then a tiny non-negative number).
+__device__ __forceinline__ float exp2_poly(float x) {
+    x = fmaxf(x, -126.0f);
+    const float t = __fadd_rn(x, 12582912.0f);
+    const float f = __fsub_rn(x, __fsub_rn(t, 12582912.0f));
+    float p = fmaf(0.0551716685295105f, f, 0.2426111251115799f);
+    p = fmaf(p, f, 0.6932609677314758f);
+    p = fmaf(p, f, 0.9999280571937561f);
+    return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -83,7 +106,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sQ = smem + OFF_Q;
     uint8_t *sKV = smem + OFF_KV;
-    uint8_t *sP = smem + OFF_P;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
     uint64_t *q_full = bars;
     uint64_t *kv_full = bars + 1;
@@ -153,49 +175,57 @@ __global__ void __launch_bounds__(THREADS, 1)
             constexpr uint32_t ID_PV = idesc_bf16_f32(BM, HD, true);  // P (K-major) x V (MN-major)
             bool ok = mbar_wait(q_full, 0, abort_flag);
             tc_fence_after();
-            const uint32_t q_base = smem_u32(sQ), kv_base = smem_u32(sKV), p_base = smem_u32(sP);
-            for (int j = 0; j < p.nkv && ok; ++j) {
-                const int ik = 2 * j, sk = ik % STAGES;
-                ok = mbar_wait(&kv_full[sk], (ik / STAGES) & 1, abort_flag);
-                if (!ok) break;
-                tc_fence_after();
-                const uint32_t kaddr = kv_base + sk * TILE;
-                for (int t = 0; t < NQ && ok; ++t) {
-                    if (j > 0) ok = mbar_wait(&p_ready[t], (j - 1) & 1, abort_flag);
-                    if (!ok) break;
-                    tc_fence_after();
-                    const uint32_t qaddr = q_base + t * TILE;
+            const uint32_t q_base = smem_u32(sQ), kv_base = smem_u32(sKV);
+            // S_t(j) = Q_t K_j^T into TMEM columns [t*BN, t*BN+BN)
+            auto issue_s = [&](int t, uint32_t kaddr) {
+                const uint32_t qaddr = q_base + t * TILE;
 #pragma unroll
-                    for (int kk = 0; kk < HD / 16; ++kk) {
-                        const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
-                        umma_ss(tmem + t * BN, smem_desc_sw128(qaddr + off, 16, 1024),
-                                smem_desc_sw128(kaddr + off, 16, 1024), ID_S, kk > 0);
-                    }
-                    umma_commit(&s_full[t]);
+                for (int kk = 0; kk < HD / 16; ++kk) {
+                    const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
+                    umma_ss(tmem + t * BN, smem_desc_sw128(qaddr + off, 16, 1024),
+                            smem_desc_sw128(kaddr + off, 16, 1024), ID_S, kk > 0);
                 }
-                if (!ok) break;
-                umma_commit(&kv_empty[sk]);
-
+                umma_commit(&s_full[t]);
+            };
+            // prologue: S_0(0), S_1(0)
+            if (ok) ok = mbar_wait(&kv_full[0], 0, abort_flag);
+            if (ok) {
+                tc_fence_after();
+                for (int t = 0; t < NQ; ++t) issue_s(t, kv_base);
+                umma_commit(&kv_empty[0]);
+            }
+            // steady state, ping-pong order: PV_0(j), S_0(j+1), PV_1(j), S_1(j+1).  S_t(j+1)
+            // overwrites P_t(j) (aliased in TMEM), so it waits for the commit of PV_t(j);
+            // meanwhile the tensor pipe is busy with PV_t(j) itself, and softmax t can start
+            // on tile j+1 while the other warpgroup still works on tile j.
+            for (int j = 0; j < p.nkv && ok; ++j) {
                 const int iv = 2 * j + 1, sv = iv % STAGES;
+                const int ik = 2 * j + 2, sk = ik % STAGES;
+                const bool more = j + 1 < p.nkv;
                 ok = mbar_wait(&kv_full[sv], (iv / STAGES) & 1, abort_flag);
                 if (!ok) break;
-                tc_fence_after();
                 const uint32_t vaddr = kv_base + sv * TILE;
+                const uint32_t kaddr = kv_base + sk * TILE;
                 for (int t = 0; t < NQ && ok; ++t) {
                     ok = mbar_wait(&p_ready[t], j & 1, abort_flag);
                     if (!ok) break;
                     tc_fence_after();
-                    const uint32_t paddr = p_base + t * TILE;
 #pragma unroll
-                    for (int kk = 0; kk < BN / 16; ++kk) {
-                        const uint32_t aoff = (kk >> 2) * HALF + (kk & 3) * 32;
-                        umma_ss(tmem + 2 * BN + t * HD, smem_desc_sw128(paddr + aoff, 16, 1024),
+                    for (int kk = 0; kk < BN / 16; ++kk)  // P: 16 keys = 8 packed columns per step
+                        umma_ts(tmem + 2 * BN + t * HD, tmem + t * BN + kk * 8,
                                 smem_desc_sw128(vaddr + kk * 2048, HALF, 1024), ID_PV, (j > 0 || kk > 0) ? 1u : 0u);
-                    }
                     umma_commit(&o_done[t]);
+                    if (more) {
+                        if (t == 0) ok = mbar_wait(&kv_full[sk], (ik / STAGES) & 1, abort_flag);
+                        if (ok) ok = mbar_wait(&o_done[t], j & 1, abort_flag);
+                        if (!ok) break;
+                        tc_fence_after();
+                        issue_s(t, kaddr);
+                    }
                 }
                 if (!ok) break;
                 umma_commit(&kv_empty[sv]);
+                if (more) umma_commit(&kv_empty[sk]);
             }
             if (!ok) drain_in_flight();
         }
@@ -206,11 +236,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
         const uint32_t s_addr = tmem + t * BN + lane_off;
         const uint32_t o_addr = tmem + 2 * BN + t * HD + lane_off;
-        const uint32_t p_tile = smem_u32(sP + t * TILE);
         const float c = p.scale_log2;
         float m = -INFINITY, l = 0.f;
         bool ok = true;
         for (int j = 0; j < p.nkv; ++j) {
+            // s_full(j) implies P_t(j-1) V_{j-1} has landed: S_t(j) was issued after its commit
             ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, abort_flag));
             if (!ok) break;
             tc_fence_after();
@@ -221,7 +251,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             tmem_ld32(s_addr + 96, *reinterpret_cast<uint32_t(*)[32]>(&s[96]));
             tmem_ld_wait();
             const int valid = p.Sk - j * BN;
-            if (valid < BN) {
+            const bool full = valid >= BN;
+            if (!full) {
 #pragma unroll
                 for (int i = 0; i < 128; ++i)
                     if (i >= valid) s[i] = __float_as_uint(-INFINITY);
@@ -244,12 +275,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                 m = mnew;
                 rescale = true;
             }
-            // PV of the previous tile must be complete before O is rescaled and P overwritten
-            if (j > 0) {
-                ok = __all_sync(0xffffffffu, mbar_wait(&o_done[t], (j - 1) & 1, abort_flag));
-                if (!ok) break;
-                tc_fence_after();
-            }
             // tcgen05.ld/st are warp-collective: rescale the whole warp's rows if any needs it
             if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
@@ -261,24 +286,42 @@ __global__ void __launch_bounds__(THREADS, 1)
                     for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
                     tmem_st32(o_addr + cc * 32, o);
                 }
-                tmem_st_wait();
             }
             const float neg_m = -m;
-            float rowsum = 0.f;
+            float rs[4] = {0.f, 0.f, 0.f, 0.f};
+            // P overwrites columns [0, 64) of this tile's S region (S is already in registers)
 #pragma unroll
-            for (int ch = 0; ch < 16; ++ch) {  // 16 chunks of 8 keys
-                uint32_t w[4];
+            for (int hf = 0; hf < 2; ++hf) {
+                uint32_t w[32];
+                if (full) {
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float p0 = ex2(fmaf(__uint_as_float(s[ch * 8 + 2 * e]), c, neg_m));
-                    const float p1 = ex2(fmaf(__uint_as_float(s[ch * 8 + 2 * e + 1]), c, neg_m));
-                    rowsum += p0 + p1;
-                    w[e] = pack_bf16x2(p0, p1);
+                    for (int i = 0; i < 32; ++i) {
+                        const float x0 = fmaf(__uint_as_float(s[64 * hf + 2 * i]), c, neg_m);
+                        const float x1 = fmaf(__uint_as_float(s[64 * hf + 2 * i + 1]), c, neg_m);
+                        float p0, p1;
+                        if ((i & 7) < POLY_PAIRS) {
+                            p0 = exp2_poly(x0);
+                            p1 = exp2_poly(x1);
+                        } else {
+                            p0 = ex2(x0);
+                            p1 = ex2(x1);
+                        }
+                        rs[i & 3] += p0 + p1;
+                        w[i] = pack_bf16x2(p0, p1);
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const float p0 = ex2(fmaf(__uint_as_float(s[64 * hf + 2 * i]), c, neg_m));
+                        const float p1 = ex2(fmaf(__uint_as_float(s[64 * hf + 2 * i + 1]), c, neg_m));
+                        rs[i & 3] += p0 + p1;
+                        w[i] = pack_bf16x2(p0, p1);
+                    }
                 }
-                st_shared_v4(p_tile + (ch >> 3) * HALF + swz(row, ch & 7), w[0], w[1], w[2], w[3]);
+                tmem_st32(s_addr + 32 * hf, w);
             }
-            l = l * alpha + rowsum;
-            fence_proxy_async_smem();
+            l = l * alpha + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
+            tmem_st_wait();
             tc_fence_before();
             mbar_arrive(&p_ready[t]);
         }

@@ -67,6 +67,7 @@ struct RowViewMut {
 };
 
 __device__ __forceinline__ int64_t row_offset(int64_t s0, int64_t s1, int64_t row, int64_t n1) {
+    if (row < n1) return row * s1;  // 2-D views (n0 == 1) and the first batch: no division
     const int64_t i0 = row / n1, i1 = row - i0 * n1;
     return i0 * s0 + i1 * s1;
 }

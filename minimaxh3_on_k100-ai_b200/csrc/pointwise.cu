@@ -2,21 +2,53 @@
 // BF16 rounding at every step (tools/h3_pointwise.py; torch compositions in
 // tools/bench_h3_ops.py:81-258), plus their C-ABI entry points.
 //
-// Design: HBM-bound.  Row ops (RMSNorm/AdaLN family) run one 128-thread CTA per
-// row with the row held in registers (one HBM read, one write); the reduction
-// order is fixed by the thread/vector assignment (per-thread serial sum over its
-// 8-wide vectors in column order, xor-shuffle tree, then warps 0..3 in order), so
-// a row's result never depends on which CTA or rank computes it.  Per-head ops
-// (q/k norm + RoPE) run one warp per 128-wide head row, lanes exchanging RoPE
-// partners by shuffle.  Each kernel has a vectorised path (16-byte / 8-byte
-// accesses, inner stride 1, aligned rows) and a strided path with the same
-// arithmetic and the same summation order, so both give identical bits.
+// Design: HBM-bound; every kernel reads its inputs once and writes its outputs
+// once with 16-byte accesses and enough independent loads in flight per thread.
+//  * Row ops (RMSNorm / AdaLN family, LayerNorm variant): one warp per row, the
+//    row held in registers as packed BF16 (it is BF16 anyway), sum of squares
+//    reduced serially per lane in column order then by an xor-shuffle tree: no
+//    shared memory, no block barrier, and a row's result never depends on which
+//    warp, CTA or rank computes it.
+//  * Per-head ops (q/k norm + RoPE): a half-warp per 128-wide head row (16 lanes x
+//    8 elements), two rows in flight per half-warp, RoPE partners exchanged by
+//    shuffle, output written straight into the (permuted) all-to-all send layout.
+//  * Element-wise ops (gated residual, SwiGLU): 2-D grid (column vectors x rows),
+//    two 16-byte vectors per thread, no 64-bit division per element.
+// Each kernel has a vectorised path (inner stride 1, 16-byte aligned rows) and a
+// strided path with the same arithmetic and summation order (identical bits).
 #include <math.h>
 
 #include "h3_abi_util.h"
 #include "h3_common.cuh"
 
 namespace h3 {
+
+template <bool VEC>
+__device__ __forceinline__ uint4 load8p(const __nv_bfloat16 *base, int64_t sc, int64_t col, int64_t C) {
+    if (VEC) return *reinterpret_cast<const uint4 *>(base + col);
+    float f[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = (col + i < C) ? __bfloat162float(base[(col + i) * sc]) : 0.f;
+    return pack8(f);
+}
+template <bool VEC>
+__device__ __forceinline__ void store8p(__nv_bfloat16 *base, int64_t sc, int64_t col, int64_t C, uint4 v) {
+    if (VEC) {
+        *reinterpret_cast<uint4 *>(base + col) = v;
+    } else {
+        float f[8];
+        unpack8(v, f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (col + i < C) base[(col + i) * sc] = __float2bfloat16_rn(f[i]);
+    }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = add_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
 
 // ===========================================================================
 // element-wise ops: gated residual, SwiGLU
@@ -28,6 +60,7 @@ struct EwArgs {
 };
 
 enum { EW_GATED_RESIDUAL = 0, EW_SWIGLU = 1 };
+constexpr int EW_THREADS = 256, EW_VPT = 2;   // vectors of 8 per thread
 
 template <int OP>
 __device__ __forceinline__ float ew_apply(float a, float b, float c) {
@@ -39,45 +72,37 @@ __device__ __forceinline__ float ew_apply(float a, float b, float c) {
     }
 }
 
-template <int OP>
-__global__ void __launch_bounds__(256) ew_vec_kernel(EwArgs args) {
-    const int64_t vpr = args.C >> 3;
-    const int64_t total = args.rows * vpr;
-    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-         idx += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t row = idx / vpr;
-        const int64_t col = (idx - row * vpr) << 3;
-        const uint4 va = *reinterpret_cast<const uint4 *>(
-            args.a.p + row_offset(args.a.s0, args.a.s1, row, args.n1) + col);
-        const uint4 vb = *reinterpret_cast<const uint4 *>(
-            args.b.p + row_offset(args.b.s0, args.b.s1, row, args.n1) + col);
-        uint4 vc = make_uint4(0, 0, 0, 0);
-        if (OP == EW_GATED_RESIDUAL)
-            vc = *reinterpret_cast<const uint4 *>(args.c.p + row_offset(args.c.s0, args.c.s1, row, args.n1) + col);
-        float fa[8], fb[8], fc[8], fo[8];
-        unpack8(va, fa);
-        unpack8(vb, fb);
-        unpack8(vc, fc);
+template <int OP, bool VEC>
+__global__ void __launch_bounds__(EW_THREADS) ew_kernel(EwArgs args) {
+    const int64_t nvec = (args.C + 7) >> 3;
+    for (int64_t row = blockIdx.y; row < args.rows; row += gridDim.y) {
+        const __nv_bfloat16 *pa = args.a.p + row_offset(args.a.s0, args.a.s1, row, args.n1);
+        const __nv_bfloat16 *pb = args.b.p + row_offset(args.b.s0, args.b.s1, row, args.n1);
+        const __nv_bfloat16 *pc = args.c.p + row_offset(args.c.s0, args.c.s1, row, args.n1);
+        __nv_bfloat16 *po = args.o.p + row_offset(args.o.s0, args.o.s1, row, args.n1);
+        uint4 va[EW_VPT], vb[EW_VPT], vc[EW_VPT];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) fo[i] = ew_apply<OP>(fa[i], fb[i], fc[i]);
-        *reinterpret_cast<uint4 *>(args.o.p + row_offset(args.o.s0, args.o.s1, row, args.n1) + col) = pack8(fo);
-    }
-}
-
-template <int OP>
-__global__ void __launch_bounds__(256) ew_strided_kernel(EwArgs args) {
-    const int64_t total = args.rows * args.C;
-    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-         idx += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t row = idx / args.C;
-        const int64_t col = idx - row * args.C;
-        const float a = __bfloat162float(args.a.p[row_offset(args.a.s0, args.a.s1, row, args.n1) + col * args.a.sc]);
-        const float b = __bfloat162float(args.b.p[row_offset(args.b.s0, args.b.s1, row, args.n1) + col * args.b.sc]);
-        float c = 0.f;
-        if (OP == EW_GATED_RESIDUAL)
-            c = __bfloat162float(args.c.p[row_offset(args.c.s0, args.c.s1, row, args.n1) + col * args.c.sc]);
-        args.o.p[row_offset(args.o.s0, args.o.s1, row, args.n1) + col * args.o.sc] =
-            __float2bfloat16_rn(ew_apply<OP>(a, b, c));
+        for (int k = 0; k < EW_VPT; ++k) {
+            const int64_t vi = (int64_t)blockIdx.x * (EW_THREADS * EW_VPT) + k * EW_THREADS + threadIdx.x;
+            if (vi < nvec) {
+                va[k] = load8p<VEC>(pa, args.a.sc, vi * 8, args.C);
+                vb[k] = load8p<VEC>(pb, args.b.sc, vi * 8, args.C);
+                if (OP == EW_GATED_RESIDUAL) vc[k] = load8p<VEC>(pc, args.c.sc, vi * 8, args.C);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < EW_VPT; ++k) {
+            const int64_t vi = (int64_t)blockIdx.x * (EW_THREADS * EW_VPT) + k * EW_THREADS + threadIdx.x;
+            if (vi < nvec) {
+                float fa[8], fb[8], fc[8], fo[8];
+                unpack8(va[k], fa);
+                unpack8(vb[k], fb);
+                if (OP == EW_GATED_RESIDUAL) unpack8(vc[k], fc);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) fo[i] = ew_apply<OP>(fa[i], fb[i], OP == EW_GATED_RESIDUAL ? fc[i] : 0.f);
+                store8p<VEC>(po, args.o.sc, vi * 8, args.C, pack8(fo));
+            }
+        }
     }
 }
 
@@ -95,62 +120,22 @@ struct RowArgs {
     float eps;
 };
 
-constexpr int ROW_THREADS = 128;
-
-template <bool VEC>
-__device__ __forceinline__ void row_load8(const __nv_bfloat16 *base, int64_t sc, int64_t col, int64_t C,
-                                          float f[8]) {
-    if (VEC) {
-        unpack8(*reinterpret_cast<const uint4 *>(base + col), f);
-    } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) f[i] = (col + i < C) ? __bfloat162float(base[(col + i) * sc]) : 0.f;
-    }
-}
-template <bool VEC>
-__device__ __forceinline__ void row_store8(__nv_bfloat16 *base, int64_t sc, int64_t col, int64_t C,
-                                           const float f[8]) {
-    if (VEC) {
-        *reinterpret_cast<uint4 *>(base + col) = pack8(f);
-    } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-            if (col + i < C) base[(col + i) * sc] = __float2bfloat16_rn(f[i]);
-    }
-}
-
-// Sum over the CTA in a fixed order: xor tree inside each warp, then warps in order.
-__device__ __forceinline__ float cta_sum(float v, float *red) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = add_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    __syncthreads();  // red[] may still be read from a previous reduction
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    float s = red[0];
-#pragma unroll
-    for (int w = 1; w < ROW_THREADS / 32; ++w) s = add_rn(s, red[w]);
-    return s;
-}
+constexpr int ROW_WARPS = 4;            // rows per CTA (one warp each)
 
 template <int MODE, bool VEC, int VPT>
-__global__ void __launch_bounds__(ROW_THREADS) row_kernel(RowArgs args) {
-    __shared__ float red[ROW_THREADS / 32];
-    const int64_t row = blockIdx.x;
+__global__ void __launch_bounds__(ROW_WARPS * 32) row_kernel(RowArgs args) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = (int64_t)blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
+    if (row >= args.rows) return;  // whole warp leaves together
     const int64_t C = args.C;
     const int64_t nvec = (C + 7) >> 3;
     const __nv_bfloat16 *xrow = args.x.p + row_offset(args.x.s0, args.x.s1, row, args.n1);
 
-    float v[VPT][8];
+    uint4 v[VPT];
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
-        const int64_t vi = threadIdx.x + (int64_t)k * ROW_THREADS;
-        if (vi < nvec) {
-            row_load8<VEC>(xrow, args.x.sc, vi * 8, C, v[k]);
-        } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[k][i] = 0.f;
-        }
+        const int64_t vi = lane + 32 * k;
+        v[k] = vi < nvec ? load8p<VEC>(xrow, args.x.sc, vi * 8, C) : make_uint4(0, 0, 0, 0);
     }
     if (MODE == ROW_RES_RMS_MOD) {
         const __nv_bfloat16 *grow = args.gate.p + row_offset(args.gate.s0, args.gate.s1, row, args.n1);
@@ -158,49 +143,59 @@ __global__ void __launch_bounds__(ROW_THREADS) row_kernel(RowArgs args) {
         __nv_bfloat16 *rrow = args.residual.p + row_offset(args.residual.s0, args.residual.s1, row, args.n1);
 #pragma unroll
         for (int k = 0; k < VPT; ++k) {
-            const int64_t vi = threadIdx.x + (int64_t)k * ROW_THREADS;
+            const int64_t vi = lane + 32 * k;
             if (vi < nvec) {
-                float g[8], y[8];
-                row_load8<VEC>(grow, args.gate.sc, vi * 8, C, g);
-                row_load8<VEC>(yrow, args.y.sc, vi * 8, C, y);
+                float fx[8], fg[8], fy[8];
+                unpack8(v[k], fx);
+                unpack8(load8p<VEC>(grow, args.gate.sc, vi * 8, C), fg);
+                unpack8(load8p<VEC>(yrow, args.y.sc, vi * 8, C), fy);
 #pragma unroll
-                for (int i = 0; i < 8; ++i) v[k][i] = bf(add_rn(v[k][i], bf(mul_rn(g[i], y[i]))));
-                row_store8<VEC>(rrow, args.residual.sc, vi * 8, C, v[k]);
+                for (int i = 0; i < 8; ++i) fx[i] = add_rn(fx[i], bf(mul_rn(fg[i], fy[i])));
+                v[k] = pack8(fx);                 // residual, rounded to BF16
+                store8p<VEC>(rrow, args.residual.sc, vi * 8, C, v[k]);
             }
         }
     }
 
-    // ---- statistics ----
+    // ---- statistics (padding lanes hold zeros) ----
     float r = 0.f, shift_ln = 0.f;
     if (MODE == ROW_LN_MOD) {
         float s = 0.f;
 #pragma unroll
-        for (int k = 0; k < VPT; ++k)
+        for (int k = 0; k < VPT; ++k) {
+            float f[8];
+            unpack8(v[k], f);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) s = add_rn(s, v[k][i]);
-        const float mean = __fdiv_rn(cta_sum(s, red), (float)C);
+            for (int i = 0; i < 8; ++i) s = add_rn(s, f[i]);
+        }
+        const float mean = __fdiv_rn(warp_sum(s), (float)C);
         float q = 0.f;
 #pragma unroll
         for (int k = 0; k < VPT; ++k) {
-            const int64_t vi = threadIdx.x + (int64_t)k * ROW_THREADS;
+            const int64_t vi = lane + 32 * k;
+            float f[8];
+            unpack8(v[k], f);
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 if (vi * 8 + i < C) {
-                    const float d = __fsub_rn(v[k][i], mean);
+                    const float d = __fsub_rn(f[i], mean);
                     q = __fmaf_rn(d, d, q);
                 }
             }
         }
-        const float var = __fdiv_rn(cta_sum(q, red), (float)C);
+        const float var = __fdiv_rn(warp_sum(q), (float)C);
         r = rsqrt_torch(add_rn(var, args.eps));
         shift_ln = -mul_rn(r, mean);  // y = x * rstd + (-rstd * mean), fused
     } else {
         float s = 0.f;
 #pragma unroll
-        for (int k = 0; k < VPT; ++k)
+        for (int k = 0; k < VPT; ++k) {
+            float f[8];
+            unpack8(v[k], f);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) s = add_rn(s, bf(mul_rn(v[k][i], v[k][i])));  // bf16(x^2)
-        const float mean = bf(__fdiv_rn(cta_sum(s, red), (float)C));
+            for (int i = 0; i < 8; ++i) s = add_rn(s, bf(mul_rn(f[i], f[i])));  // bf16(x^2)
+        }
+        const float mean = bf(__fdiv_rn(warp_sum(s), (float)C));
         const float var = bf(add_rn(mean, args.eps));
         r = bf(rsqrt_torch(var));
     }
@@ -214,12 +209,13 @@ __global__ void __launch_bounds__(ROW_THREADS) row_kernel(RowArgs args) {
     __nv_bfloat16 *orow = args.out.p + row_offset(args.out.s0, args.out.s1, row, args.n1);
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
-        const int64_t vi = threadIdx.x + (int64_t)k * ROW_THREADS;
+        const int64_t vi = lane + 32 * k;
         if (vi >= nvec) continue;
-        float o[8];
+        float f[8], o[8];
+        unpack8(v[k], f);
         if (MODE == ROW_LN_MOD) {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) o[i] = bf(__fmaf_rn(v[k][i], r, shift_ln));
+            for (int i = 0; i < 8; ++i) o[i] = bf(__fmaf_rn(f[i], r, shift_ln));
         } else {
             float w[8];
             if (VEC && args.wsc == 1) {
@@ -230,24 +226,24 @@ __global__ void __launch_bounds__(ROW_THREADS) row_kernel(RowArgs args) {
                     w[i] = (vi * 8 + i < C) ? __bfloat162float(args.weight[(vi * 8 + i) * args.wsc]) : 0.f;
             }
 #pragma unroll
-            for (int i = 0; i < 8; ++i) o[i] = bf(mul_rn(bf(mul_rn(v[k][i], r)), w[i]));
+            for (int i = 0; i < 8; ++i) o[i] = bf(mul_rn(bf(mul_rn(f[i], r)), w[i]));
         }
         if (MODE != ROW_RMS) {
             float sc[8], sh[8];
-            row_load8<VEC>(srow, args.scale.sc, vi * 8, C, sc);
-            row_load8<VEC>(hrow, args.shift.sc, vi * 8, C, sh);
+            unpack8(load8p<VEC>(srow, args.scale.sc, vi * 8, C), sc);
+            unpack8(load8p<VEC>(hrow, args.shift.sc, vi * 8, C), sh);
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 const float factor = bf(add_rn(sc[i], 1.0f));
                 o[i] = add_rn(bf(mul_rn(o[i], factor)), sh[i]);
             }
         }
-        row_store8<VEC>(orow, args.out.sc, vi * 8, C, o);
+        store8p<VEC>(orow, args.out.sc, vi * 8, C, pack8(o));
     }
 }
 
 // ===========================================================================
-// per-head q/k RMSNorm + RoPE (one warp per 128-wide head row)
+// per-head q/k RMSNorm + RoPE: a half-warp per 128-wide head row
 // ===========================================================================
 struct HeadArgs {
     const __nv_bfloat16 *x;
@@ -263,85 +259,94 @@ struct HeadArgs {
     float eps;
 };
 
+constexpr int HEAD_THREADS = 128;                                      // 8 half-warps
+constexpr int HEAD_ROWS_PER_HW = 2;                                    // rows in flight per half-warp
+constexpr int HEAD_ROWS_PER_CTA = (HEAD_THREADS / 16) * HEAD_ROWS_PER_HW;
+
+// grid: x over the P*Hs head rows of one token (HEAD_ROWS_PER_CTA per CTA), y over tokens
 template <bool NORM, bool VEC>
-__global__ void __launch_bounds__(256) head_kernel(HeadArgs a) {
+__global__ void __launch_bounds__(HEAD_THREADS) head_kernel(HeadArgs a) {
     const int lane = threadIdx.x & 31;
-    const int64_t rows = a.T * a.P * a.Hs;
-    const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    const int d = a.half >> 2;  // lanes per rotated half
-    for (int64_t rix = warp0; rix < rows; rix += nwarps) {
-        const int64_t h = rix % a.Hs;
-        const int64_t tp = rix / a.Hs;
-        const int64_t p = tp % a.P;
-        const int64_t t = tp / a.P;
-        const __nv_bfloat16 *xr = a.x + t * a.xs[0] + p * a.xs[1] + h * a.xs[2];
-        __nv_bfloat16 *orow = a.out + t * a.os[0] + p * a.os[1] + h * a.os[2];
-        float v[4];
-        if (VEC) {
-            unpack4(*reinterpret_cast<const uint2 *>(xr + 4 * lane), v);
-        } else {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) v[i] = __bfloat162float(xr[(4 * lane + i) * a.xs[3]]);
+    const int hl = lane & 15;                    // lane within the half-warp: elements [8hl, 8hl+8)
+    const int hw_base = lane & 16;
+    const int hw = threadIdx.x >> 4;             // half-warp index in the CTA
+    const int ph_count = (int)(a.P * a.Hs);
+    const int d = a.half >> 3;                   // lanes per rotated half
+    const int partner = hl < d ? hl + d : (hl < 2 * d ? hl - d : hl);
+
+    for (int64_t t = blockIdx.y; t < a.T; t += gridDim.y) {
+        uint4 xv[HEAD_ROWS_PER_HW];
+        int phs[HEAD_ROWS_PER_HW];
+        uint4 cv = make_uint4(0, 0, 0, 0), sv = make_uint4(0, 0, 0, 0);
+        if (a.half > 0 && hl < 2 * d) {          // the token's angles, shared by its heads
+            const int j = 8 * (hl < d ? hl : hl - d);
+            cv = load8p<VEC>(a.cos + t * a.cs0 + j * a.cs1, a.cs1, 0, 8);
+            sv = load8p<VEC>(a.sin + t * a.ss0 + j * a.ss1, a.ss1, 0, 8);
         }
-        if (NORM) {
-            float s = 0.f;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) s = add_rn(s, bf(mul_rn(v[i], v[i])));
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) s = add_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
-            const float mean = bf(__fdiv_rn(s, 128.0f));
-            const float var = bf(add_rn(mean, a.eps));
-            const float r = bf(rsqrt_torch(var));
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float w = __bfloat162float(a.weight[(4 * lane + i) * a.wsc]);
-                v[i] = bf(mul_rn(bf(mul_rn(v[i], r)), w));
+        for (int u = 0; u < HEAD_ROWS_PER_HW; ++u) {
+            const int ph = blockIdx.x * HEAD_ROWS_PER_CTA + u * (HEAD_THREADS / 16) + hw;
+            phs[u] = ph;
+            if (ph < ph_count) {
+                const int p = ph / (int)a.Hs, h = ph - p * (int)a.Hs;
+                xv[u] = load8p<VEC>(a.x + t * a.xs[0] + p * a.xs[1] + h * a.xs[2], a.xs[3], 8 * hl, 128);
+            } else {
+                xv[u] = make_uint4(0, 0, 0, 0);
             }
         }
-        float o[4];
-        if (a.half > 0) {
-            // exchange with the RoPE partner lane (values are exact BF16, packed losslessly)
-            const uint2 mine = pack4(v);
-            const int partner = lane < d ? lane + d : (lane < 2 * d ? lane - d : lane);
-            uint2 theirs;
-            theirs.x = __shfl_sync(0xffffffffu, mine.x, partner);
-            theirs.y = __shfl_sync(0xffffffffu, mine.y, partner);
-            float pv[4];
-            unpack4(theirs, pv);
-            if (lane < 2 * d) {
-                const int j = 4 * (lane < d ? lane : lane - d);
-                float c[4], s[4];
-                if (VEC) {
-                    unpack4(*reinterpret_cast<const uint2 *>(a.cos + t * a.cs0 + j), c);
-                    unpack4(*reinterpret_cast<const uint2 *>(a.sin + t * a.ss0 + j), s);
+        float w[8];
+        if (NORM) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) w[i] = __bfloat162float(a.weight[(8 * hl + i) * a.wsc]);
+        }
+        float c[8], sn[8];
+        unpack8(cv, c);
+        unpack8(sv, sn);
+#pragma unroll
+        for (int u = 0; u < HEAD_ROWS_PER_HW; ++u) {
+            float v[8];
+            unpack8(xv[u], v);
+            if (NORM) {
+                float s = 0.f;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) s = add_rn(s, bf(mul_rn(v[i], v[i])));
+#pragma unroll
+                for (int o = 8; o > 0; o >>= 1) s = add_rn(s, __shfl_xor_sync(0xffffffffu, s, o));  // within the half
+                const float mean = bf(__fdiv_rn(s, 128.0f));
+                const float var = bf(add_rn(mean, a.eps));
+                const float r = bf(rsqrt_torch(var));
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = bf(mul_rn(bf(mul_rn(v[i], r)), w[i]));
+            }
+            float o[8];
+            if (a.half > 0) {
+                const uint4 mine = pack8(v);   // exact: v is BF16-valued
+                uint4 theirs;
+                const int src = hw_base | partner;
+                theirs.x = __shfl_sync(0xffffffffu, mine.x, src);
+                theirs.y = __shfl_sync(0xffffffffu, mine.y, src);
+                theirs.z = __shfl_sync(0xffffffffu, mine.z, src);
+                theirs.w = __shfl_sync(0xffffffffu, mine.w, src);
+                float pv[8];
+                unpack8(theirs, pv);
+                if (hl < d) {            // first half: y0 = bf(bf(a*c) + bf(-b*s))
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) o[i] = add_rn(bf(mul_rn(v[i], c[i])), bf(mul_rn(-pv[i], sn[i])));
+                } else if (hl < 2 * d) { // second half: y1 = bf(bf(b*c) + bf(a*s))
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) o[i] = add_rn(bf(mul_rn(v[i], c[i])), bf(mul_rn(pv[i], sn[i])));
                 } else {
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        c[i] = __bfloat162float(a.cos[t * a.cs0 + (j + i) * a.cs1]);
-                        s[i] = __bfloat162float(a.sin[t * a.ss0 + (j + i) * a.ss1]);
-                    }
-                }
-                if (lane < d) {  // first half: y0 = bf(bf(a*c) + bf(-b*s))
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) o[i] = add_rn(bf(mul_rn(v[i], c[i])), bf(mul_rn(-pv[i], s[i])));
-                } else {         // second half: y1 = bf(bf(b*c) + bf(a*s))
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) o[i] = add_rn(bf(mul_rn(v[i], c[i])), bf(mul_rn(pv[i], s[i])));
+                    for (int i = 0; i < 8; ++i) o[i] = v[i];
                 }
             } else {
 #pragma unroll
-                for (int i = 0; i < 4; ++i) o[i] = v[i];
+                for (int i = 0; i < 8; ++i) o[i] = v[i];
             }
-        } else {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) o[i] = v[i];
-        }
-        if (VEC) {
-            *reinterpret_cast<uint2 *>(orow + 4 * lane) = pack4(o);
-        } else {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) orow[(4 * lane + i) * a.os[3]] = __float2bfloat16_rn(o[i]);
+            if (phs[u] < ph_count) {
+                const int p = phs[u] / (int)a.Hs, h = phs[u] - p * (int)a.Hs;
+                store8p<VEC>(a.out + t * a.os[0] + p * a.os[1] + h * a.os[2], a.os[3], 8 * hl, 128, pack8(o));
+            }
         }
     }
 }
@@ -439,13 +444,11 @@ static int launch_ew(const h3_tensor *o, const h3_tensor *a, const h3_tensor *b,
     if (args.rows == 0 || args.C == 0) return H3_OK;
     const bool vec = rows_vectorizable(o, 8) && rows_vectorizable(a, 8) && rows_vectorizable(b, 8) &&
                      (!c || rows_vectorizable(c, 8));
-    if (vec) {
-        const int g = grid_for(args.rows * (args.C / 8), 256);
-        ew_vec_kernel<OP><<<g, 256, 0, stream>>>(args);
-    } else {
-        const int g = grid_for(args.rows * args.C, 256);
-        ew_strided_kernel<OP><<<g, 256, 0, stream>>>(args);
-    }
+    const int64_t nvec = (args.C + 7) / 8;
+    const dim3 grid((unsigned)((nvec + EW_THREADS * EW_VPT - 1) / (EW_THREADS * EW_VPT)),
+                    (unsigned)(args.rows < 65535 ? args.rows : 65535));
+    if (vec) ew_kernel<OP, true><<<grid, EW_THREADS, 0, stream>>>(args);
+    else ew_kernel<OP, false><<<grid, EW_THREADS, 0, stream>>>(args);
     return launch_status();
 }
 
@@ -453,31 +456,37 @@ template <int MODE>
 static int launch_row(RowArgs &args, bool vec, cudaStream_t stream) {
     if (args.rows == 0 || args.C == 0) return H3_OK;
     const int64_t nvec = (args.C + 7) / 8;
-    const int vpt = (int)((nvec + ROW_THREADS - 1) / ROW_THREADS);
-    if (args.rows > 0x7fffffffLL) return H3_ERR_UNSUPPORTED;
-    const dim3 grid((unsigned)args.rows);
-#define H3_ROW_CASE(V)                                                                       \
-    case V:                                                                                  \
-        if (vec) row_kernel<MODE, true, V><<<grid, ROW_THREADS, 0, stream>>>(args);         \
-        else row_kernel<MODE, false, V><<<grid, ROW_THREADS, 0, stream>>>(args);            \
-        break;
-    switch (vpt) {
-        H3_ROW_CASE(1)
-        H3_ROW_CASE(2)
-        H3_ROW_CASE(3)
-        H3_ROW_CASE(4)
-        H3_ROW_CASE(5)
-        H3_ROW_CASE(6)
-        H3_ROW_CASE(8)
-        case 7:
-            if (vec) row_kernel<MODE, true, 8><<<grid, ROW_THREADS, 0, stream>>>(args);
-            else row_kernel<MODE, false, 8><<<grid, ROW_THREADS, 0, stream>>>(args);
-            break;
-        default:
-            return H3_ERR_UNSUPPORTED;  // rows wider than 8192 elements
+    const int vpt = (int)((nvec + 31) / 32);
+    const int64_t blocks = (args.rows + ROW_WARPS - 1) / ROW_WARPS;
+    if (blocks > 0x7fffffffLL) return H3_ERR_UNSUPPORTED;
+    const dim3 grid((unsigned)blocks);
+    // vectorised path: row widths up to 8192 in steps of 4 vectors per lane (extra
+    // iterations are masked); strided path: coarser steps (rarely used, same bits)
+#define H3_ROW_VEC(V)                                                                   \
+    if (vec && vpt <= V) {                                                              \
+        row_kernel<MODE, true, V><<<grid, ROW_WARPS * 32, 0, stream>>>(args);           \
+        return launch_status();                                                         \
     }
-#undef H3_ROW_CASE
-    return launch_status();
+#define H3_ROW_STRIDED(V)                                                               \
+    if (!vec && vpt <= V) {                                                             \
+        row_kernel<MODE, false, V><<<grid, ROW_WARPS * 32, 0, stream>>>(args);          \
+        return launch_status();                                                         \
+    }
+    H3_ROW_VEC(1)
+    H3_ROW_VEC(2)
+    H3_ROW_VEC(4)
+    H3_ROW_VEC(8)
+    H3_ROW_VEC(12)
+    H3_ROW_VEC(16)
+    H3_ROW_VEC(20)
+    H3_ROW_VEC(24)
+    H3_ROW_VEC(32)
+    H3_ROW_STRIDED(4)
+    H3_ROW_STRIDED(16)
+    H3_ROW_STRIDED(32)
+#undef H3_ROW_VEC
+#undef H3_ROW_STRIDED
+    return H3_ERR_UNSUPPORTED;  // rows wider than 8192 elements
 }
 
 }  // namespace h3
@@ -606,17 +615,19 @@ static int head_launch(const h3_tensor *out, const h3_tensor *x, const h3_tensor
     a.eps = eps;
     const int64_t rows = a.T * a.P * a.Hs;
     if (rows == 0) return H3_OK;
-    bool vec = xs[3] == 1 && os[3] == 1 && a.cs1 == 1 && a.ss1 == 1 && aligned_to(x->data, 8) &&
-               aligned_to(out->data, 8) && aligned_to(cos->data, 8) && aligned_to(sin->data, 8);
-    for (int i = 0; i < 3; ++i) vec = vec && (xs[i] % 4 == 0) && (os[i] % 4 == 0);
-    vec = vec && a.cs0 % 4 == 0 && a.ss0 % 4 == 0;
-    const int g = grid_for(rows * 32, 256);
+    bool vec = xs[3] == 1 && os[3] == 1 && a.cs1 == 1 && a.ss1 == 1 && aligned16(x->data) &&
+               aligned16(out->data) && aligned16(cos->data) && aligned16(sin->data);
+    for (int i = 0; i < 3; ++i) vec = vec && (xs[i] % 8 == 0) && (os[i] % 8 == 0);
+    vec = vec && a.cs0 % 8 == 0 && a.ss0 % 8 == 0;
+    if (a.P * a.Hs > (1 << 24)) return H3_ERR_UNSUPPORTED;
+    const dim3 g((unsigned)((a.P * a.Hs + HEAD_ROWS_PER_CTA - 1) / HEAD_ROWS_PER_CTA),
+                 (unsigned)(a.T < 65535 ? a.T : 65535));
     if (norm) {
-        if (vec) head_kernel<true, true><<<g, 256, 0, stream>>>(a);
-        else head_kernel<true, false><<<g, 256, 0, stream>>>(a);
+        if (vec) head_kernel<true, true><<<g, HEAD_THREADS, 0, stream>>>(a);
+        else head_kernel<true, false><<<g, HEAD_THREADS, 0, stream>>>(a);
     } else {
-        if (vec) head_kernel<false, true><<<g, 256, 0, stream>>>(a);
-        else head_kernel<false, false><<<g, 256, 0, stream>>>(a);
+        if (vec) head_kernel<false, true><<<g, HEAD_THREADS, 0, stream>>>(a);
+        else head_kernel<false, false><<<g, HEAD_THREADS, 0, stream>>>(a);
     }
     return launch_status();
 }
@@ -626,7 +637,7 @@ static int check_angles(const h3_tensor *cos, const h3_tensor *sin, int64_t T) {
     if (cos->ndim != 2 || cos->shape[0] != T) return H3_ERR_BAD_SHAPE;
     H3_CHECK(check_same_shape(cos, sin));
     const int64_t half = cos->shape[1];
-    if (half <= 0 || half % 4 != 0 || 2 * half > 128) return H3_ERR_BAD_SHAPE;
+    if (half <= 0 || half % 8 != 0 || 2 * half > 128) return H3_ERR_BAD_SHAPE;
     return H3_OK;
 }
 

@@ -58,7 +58,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // Bounded wait for the phase with the given parity to complete.  Returns false
 // (and flags the device error word) if it did not complete within H3_WAIT_NS,
 // or as soon as another role of the same CTA has raised `*abort`.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort = nullptr) {
+__device__ __forceinline__ bool mbar_wait_ns(uint64_t *bar, uint32_t parity, volatile int *abort,
+                                             uint64_t limit_ns) {
     const uint32_t a = smem_u32(bar);
     if (mbar_try_wait(a, parity)) return true;
     const uint64_t start = globaltimer();
@@ -67,12 +68,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
         for (int i = 0; i < 256; ++i)
             if (mbar_try_wait(a, parity)) return true;
         if (abort && *abort) return false;
-        if (globaltimer() - start > H3_WAIT_NS) {
+        if (globaltimer() - start > limit_ns) {
             atomicOr(&g_h3_device_error, 1u);
             if (abort) *abort = 1;
             return false;
         }
     }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort = nullptr) {
+    return mbar_wait_ns(bar, parity, abort, H3_WAIT_NS);
 }
 
 // After an abort: give copies and MMAs already in flight time to land before

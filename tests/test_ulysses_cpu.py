@@ -90,3 +90,40 @@ def test_ulysses_world2_matches_single_rank(tmp_path):
             assert torch.equal(glob, full[:, heads])
     gathered = torch.cat(outs)[:SEQ]
     assert O.max_abs_rel(gathered, ref) <= 1e-2
+
+
+def _dropout_worker(rank, port, result_path):
+    """Rank 1 leaves between steps (before the exchange); rank 0 must get an
+    error from its collective within the process-group timeout, not hang."""
+    import datetime
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=5))
+    import h3b200.ulysses as U
+    if rank == 1:
+        dist.destroy_process_group()
+        return
+    t, start, padded = U.local_rows(SEQ, WORLD, rank)
+    qkv, wq, wk, cos, sin = _inputs()
+    sp = U.SequenceParallel(WORLD, rank, None, SEQ, t, HEADS, D, "cpu", kernels=_oracle_kernels())
+    outcome = "no error"
+    try:
+        sp.attention_from_qkv(qkv[:t].contiguous(), wq, wk, cos[:t], sin[:t], 1e-6)
+    except Exception as exc:  # noqa: BLE001 - any collective error is the expected outcome
+        outcome = f"error: {type(exc).__name__}"
+    with open(result_path, "w") as f:
+        f.write(outcome)
+
+
+def test_ulysses_dropped_rank_reports_error(tmp_path):
+    port = _free_port()
+    path = str(tmp_path / "dropout")
+    ctx = mp.start_processes(_dropout_worker, args=(port, path), nprocs=WORLD, start_method="spawn",
+                             join=False)
+    deadline = 120
+    import time
+    t0 = time.time()
+    while not ctx.join(timeout=5):
+        assert time.time() - t0 < deadline, "a rank hung instead of reporting the dropped peer"
+    with open(path) as f:
+        assert f.read().startswith("error")

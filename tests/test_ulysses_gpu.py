@@ -1,0 +1,69 @@
+"""Ulysses sequence parallelism on real GPUs: a short DiT
+step on W = 2 ranks (one process per GPU, NCCL) must reproduce the 1-GPU run of
+the same kernels bit for bit, and match the CPU oracle within the block
+tolerance.  Skipped when fewer than two GPUs are visible."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+WORLD = 2
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _cfg():
+    from h3b200.block import BlockConfig
+    from h3b200.step import StepConfig
+    # 2 x 10 x 16 latent grid + 41 conditioning tokens = 361 tokens: T = 181 per rank,
+    # so the last rank carries one padding row; 4 heads -> 2 per rank
+    return StepConfig(blocks=3, video_grid=(2, 10, 16), cond_tokens=41,
+                      block=BlockConfig(hidden=512, heads=4, ffn=1536))
+
+
+def _x(cfg):
+    g = torch.Generator().manual_seed(123)
+    return torch.randn(cfg.tokens, cfg.block.hidden, generator=g).bfloat16()
+
+
+def _worker(rank, port, path):
+    import datetime
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    from h3b200.step import DiTStep
+    cfg = _cfg()
+    step = DiTStep(cfg, f"cuda:{rank}", world=WORLD, rank=rank, group=dist.group.WORLD, seed=9)
+    x = _x(cfg)
+    local = torch.zeros(step.local, cfg.block.hidden, dtype=torch.bfloat16)
+    rows = x[step.start:min(step.start + step.local, cfg.tokens)]
+    local[:rows.shape[0]] = rows
+    out = step.forward(local.to(f"cuda:{rank}")).cpu()
+    torch.save(out, f"{path}.{rank}")
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+def test_ulysses_two_gpus_bitwise_equal_to_one(tmp_path):
+    path = str(tmp_path / "sp")
+    mp.start_processes(_worker, args=(_free_port(), path), nprocs=WORLD, start_method="spawn")
+    from h3b200.step import DiTStep
+    cfg = _cfg()
+    one = DiTStep(cfg, "cuda:0", seed=9)
+    ref = one.forward(_x(cfg).to("cuda:0")).cpu()
+    sp = torch.cat([torch.load(f"{path}.{r}") for r in range(WORLD)])[:cfg.tokens]
+    assert torch.equal(sp, ref), "W-GPU output differs from the 1-GPU run"
