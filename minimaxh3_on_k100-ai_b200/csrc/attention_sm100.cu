@@ -19,12 +19,14 @@
 // a TS MMA (A operand in tensor memory); V is the MN-major B operand in shared
 // memory.  Before S_t(j+1) overwrites that region the MMA warp waits for the
 // commit of P_t(j) V_j, which is already in flight behind the other tile's PV,
-// so the tensor pipe does not drain.  A fixed share of the exponentials (3 of
-// every 8 key pairs of a full tile) is computed on the FMA pipe with a
-// Cody-Waite split 2^x = 2^round(x) * 2^f, f in [-1/2, 1/2], and a degree-3
-// polynomial for 2^f fitted here by Lawson's minimax iteration (max relative
-// error 7.5e-5, far below the BF16 rounding P receives), the rest on the MUFU
-// ex2 unit, balancing the two pipes.  The running max is updated lazily (only when it grows by more than
+// so the tensor pipe does not drain.  A configurable share of the exponentials
+// (H3_ATTN_POLY_PAIRS of every 8 key pairs of a full tile) can be computed on the
+// FMA pipe with a Cody-Waite split 2^x = 2^round(x) * 2^f, f in [-1/2, 1/2], and
+// a degree-3 polynomial for 2^f fitted by Lawson's minimax iteration (max
+// relative error 7.5e-5, far below the BF16 rounding P receives); on B200 the
+// sweep 0/2/3/4/5 measured 1054/942/948/904/876 TFLOP/s at [1,40,18432,128],
+// so the default keeps every exponential on the MUFU ex2 unit (the softmax is
+// issue-bound, not MUFU-bound).  The running max is updated lazily (only when it grows by more than
 // 2^8 in the exp2 domain), so O is rescaled rarely; the normalisation uses the
 // same stale max in numerator and denominator, so the result is unchanged up to
 // fp32 rounding.  The epilogue divides by the row sum, rounds to BF16 and writes
@@ -51,7 +53,10 @@ constexpr int THREADS = 384;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr float RESCALE_THRESHOLD = 8.0f;     // log2 domain
 
-constexpr int POLY_PAIRS = 3;                 // of every 8 key pairs, exponentiated on the FMA pipe
+#ifndef H3_ATTN_POLY_PAIRS
+#define H3_ATTN_POLY_PAIRS 0   // measured fastest on B200: the MUFU is not the limit here
+#endif
+constexpr int POLY_PAIRS = H3_ATTN_POLY_PAIRS; // of every 8 key pairs, exponentiated on the FMA pipe
 
 constexpr int OFF_Q = 0;
 constexpr int OFF_KV = OFF_Q + NQ * TILE;

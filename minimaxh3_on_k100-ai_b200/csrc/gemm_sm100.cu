@@ -185,15 +185,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                         uint32_t w[16];
 #pragma unroll
                         for (int i = 0; i < 16; ++i) {
-                            float o2[2];
-#pragma unroll
-                            for (int e = 0; e < 2; ++e) {
-                                const float up = bf(__uint_as_float(u[2 * i + e]));
-                                const float gt = bf(__uint_as_float(g[2 * i + e]));
-                                const float act = bf(__fdiv_rn(gt, add_rn(1.0f, expf(-gt))));
-                                o2[e] = mul_rn(up, act);
-                            }
-                            w[i] = pack2(o2[0], o2[1]);
+                            float up0 = __uint_as_float(u[2 * i]), up1 = __uint_as_float(u[2 * i + 1]);
+                            float g0 = __uint_as_float(g[2 * i]), g1 = __uint_as_float(g[2 * i + 1]);
+                            bf2(up0, up1);   // the linear's BF16 outputs
+                            bf2(g0, g1);
+                            float a0 = __fdiv_rn(g0, add_rn(1.0f, expf(-g0)));
+                            float a1 = __fdiv_rn(g1, add_rn(1.0f, expf(-g1)));
+                            bf2(a0, a1);
+                            w[i] = pack2(mul_rn(up0, a0), mul_rn(up1, a1));
                         }
                         __nv_bfloat16 *dst = p.out + (int64_t)row * p.ldo + col;
 #pragma unroll
@@ -223,14 +222,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                                 unpack8(*reinterpret_cast<const uint4 *>(gp + 8 * q), gf);
 #pragma unroll
                                 for (int e = 0; e < 4; ++e) {
-                                    float o2[2];
-#pragma unroll
-                                    for (int k = 0; k < 2; ++k) {
-                                        const int idx = 8 * q + 2 * e + k;
-                                        const float yv = bf(__uint_as_float(v[idx]));
-                                        o2[k] = add_rn(rf[2 * e + k], bf(mul_rn(gf[2 * e + k], yv)));
-                                    }
-                                    w[4 * q + e] = pack2(o2[0], o2[1]);
+                                    const int idx = 8 * q + 2 * e;
+                                    float y0 = __uint_as_float(v[idx]), y1 = __uint_as_float(v[idx + 1]);
+                                    bf2(y0, y1);   // the linear's BF16 output
+                                    float p0 = mul_rn(gf[2 * e], y0), p1 = mul_rn(gf[2 * e + 1], y1);
+                                    bf2(p0, p1);
+                                    w[4 * q + e] = pack2(add_rn(rf[2 * e], p0), add_rn(rf[2 * e + 1], p1));
                                 }
                             }
                         }

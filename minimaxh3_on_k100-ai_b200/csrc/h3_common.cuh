@@ -17,6 +17,13 @@ namespace h3 {
 __device__ __forceinline__ float bf(float v) {  // round to BF16 and back
     return __bfloat162float(__float2bfloat16_rn(v));
 }
+// Round two values to BF16 and back with one paired conversion (cvt.rn.bf16x2.f32):
+// the same round-to-nearest-even as bf() on each value, at half the conversions.
+__device__ __forceinline__ void bf2(float &a, float &b) {
+    const float2 f = __bfloat1622float2(__floats2bfloat162_rn(a, b));
+    a = f.x;
+    b = f.y;
+}
 __device__ __forceinline__ float mul_rn(float a, float b) { return __fmul_rn(a, b); }
 __device__ __forceinline__ float add_rn(float a, float b) { return __fadd_rn(a, b); }
 

@@ -62,13 +62,20 @@ struct EwArgs {
 enum { EW_GATED_RESIDUAL = 0, EW_SWIGLU = 1 };
 constexpr int EW_THREADS = 256, EW_VPT = 2;   // vectors of 8 per thread
 
+// two elements at a time (paired BF16 roundings); outputs are rounded by the store
 template <int OP>
-__device__ __forceinline__ float ew_apply(float a, float b, float c) {
-    if (OP == EW_GATED_RESIDUAL) {
-        return add_rn(a, bf(mul_rn(b, c)));  // bf16(x + bf16(gate * y)), rounded by the store
-    } else {
-        const float act = bf(__fdiv_rn(b, add_rn(1.0f, expf(-b))));  // bf16(g / (1 + exp(-g)))
-        return mul_rn(a, act);
+__device__ __forceinline__ void ew_apply2(const float *a, const float *b, const float *c, float *o) {
+    if (OP == EW_GATED_RESIDUAL) {          // bf16(x + bf16(gate * y))
+        float p0 = mul_rn(b[0], c[0]), p1 = mul_rn(b[1], c[1]);
+        bf2(p0, p1);
+        o[0] = add_rn(a[0], p0);
+        o[1] = add_rn(a[1], p1);
+    } else {                                // bf16(up * bf16(g / (1 + exp(-g))))
+        float a0 = __fdiv_rn(b[0], add_rn(1.0f, expf(-b[0])));
+        float a1 = __fdiv_rn(b[1], add_rn(1.0f, expf(-b[1])));
+        bf2(a0, a1);
+        o[0] = mul_rn(a[0], a0);
+        o[1] = mul_rn(a[1], a1);
     }
 }
 
@@ -99,7 +106,7 @@ __global__ void __launch_bounds__(EW_THREADS) ew_kernel(EwArgs args) {
                 unpack8(vb[k], fb);
                 if (OP == EW_GATED_RESIDUAL) unpack8(vc[k], fc);
 #pragma unroll
-                for (int i = 0; i < 8; ++i) fo[i] = ew_apply<OP>(fa[i], fb[i], OP == EW_GATED_RESIDUAL ? fc[i] : 0.f);
+                for (int i = 0; i < 8; i += 2) ew_apply2<OP>(fa + i, fb + i, fc + i, fo + i);
                 store8p<VEC>(po, args.o.sc, vi * 8, args.C, pack8(fo));
             }
         }
@@ -150,7 +157,12 @@ __global__ void __launch_bounds__(ROW_WARPS * 32) row_kernel(RowArgs args) {
                 unpack8(load8p<VEC>(grow, args.gate.sc, vi * 8, C), fg);
                 unpack8(load8p<VEC>(yrow, args.y.sc, vi * 8, C), fy);
 #pragma unroll
-                for (int i = 0; i < 8; ++i) fx[i] = add_rn(fx[i], bf(mul_rn(fg[i], fy[i])));
+                for (int i = 0; i < 8; i += 2) {
+                    float p0 = mul_rn(fg[i], fy[i]), p1 = mul_rn(fg[i + 1], fy[i + 1]);
+                    bf2(p0, p1);
+                    fx[i] = add_rn(fx[i], p0);
+                    fx[i + 1] = add_rn(fx[i + 1], p1);
+                }
                 v[k] = pack8(fx);                 // residual, rounded to BF16
                 store8p<VEC>(rrow, args.residual.sc, vi * 8, C, v[k]);
             }
@@ -193,7 +205,12 @@ __global__ void __launch_bounds__(ROW_WARPS * 32) row_kernel(RowArgs args) {
             float f[8];
             unpack8(v[k], f);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) s = add_rn(s, bf(mul_rn(f[i], f[i])));  // bf16(x^2)
+            for (int i = 0; i < 8; i += 2) {  // bf16(x^2), summed in column order
+                float q0 = mul_rn(f[i], f[i]), q1 = mul_rn(f[i + 1], f[i + 1]);
+                bf2(q0, q1);
+                s = add_rn(s, q0);
+                s = add_rn(s, q1);
+            }
         }
         const float mean = bf(__fdiv_rn(warp_sum(s), (float)C));
         const float var = bf(add_rn(mean, args.eps));
@@ -215,7 +232,11 @@ __global__ void __launch_bounds__(ROW_WARPS * 32) row_kernel(RowArgs args) {
         unpack8(v[k], f);
         if (MODE == ROW_LN_MOD) {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) o[i] = bf(__fmaf_rn(f[i], r, shift_ln));
+            for (int i = 0; i < 8; i += 2) {
+                o[i] = __fmaf_rn(f[i], r, shift_ln);
+                o[i + 1] = __fmaf_rn(f[i + 1], r, shift_ln);
+                bf2(o[i], o[i + 1]);
+            }
         } else {
             float w[8];
             if (VEC && args.wsc == 1) {
@@ -226,16 +247,26 @@ __global__ void __launch_bounds__(ROW_WARPS * 32) row_kernel(RowArgs args) {
                     w[i] = (vi * 8 + i < C) ? __bfloat162float(args.weight[(vi * 8 + i) * args.wsc]) : 0.f;
             }
 #pragma unroll
-            for (int i = 0; i < 8; ++i) o[i] = bf(mul_rn(bf(mul_rn(f[i], r)), w[i]));
+            for (int i = 0; i < 8; i += 2) {
+                float n0 = mul_rn(f[i], r), n1 = mul_rn(f[i + 1], r);
+                bf2(n0, n1);
+                o[i] = mul_rn(n0, w[i]);
+                o[i + 1] = mul_rn(n1, w[i + 1]);
+                bf2(o[i], o[i + 1]);
+            }
         }
         if (MODE != ROW_RMS) {
             float sc[8], sh[8];
             unpack8(load8p<VEC>(srow, args.scale.sc, vi * 8, C), sc);
             unpack8(load8p<VEC>(hrow, args.shift.sc, vi * 8, C), sh);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const float factor = bf(add_rn(sc[i], 1.0f));
-                o[i] = add_rn(bf(mul_rn(o[i], factor)), sh[i]);
+            for (int i = 0; i < 8; i += 2) {
+                float f0 = add_rn(sc[i], 1.0f), f1 = add_rn(sc[i + 1], 1.0f);
+                bf2(f0, f1);
+                float m0 = mul_rn(o[i], f0), m1 = mul_rn(o[i + 1], f1);
+                bf2(m0, m1);
+                o[i] = add_rn(m0, sh[i]);
+                o[i + 1] = add_rn(m1, sh[i + 1]);
             }
         }
         store8p<VEC>(orow, args.out.sc, vi * 8, C, pack8(o));
@@ -296,8 +327,12 @@ __global__ void __launch_bounds__(HEAD_THREADS) head_kernel(HeadArgs a) {
         }
         float w[8];
         if (NORM) {
+            if (VEC && a.wsc == 1) {
+                unpack8(*reinterpret_cast<const uint4 *>(a.weight + 8 * hl), w);
+            } else {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) w[i] = __bfloat162float(a.weight[(8 * hl + i) * a.wsc]);
+                for (int i = 0; i < 8; ++i) w[i] = __bfloat162float(a.weight[(8 * hl + i) * a.wsc]);
+            }
         }
         float c[8], sn[8];
         unpack8(cv, c);
@@ -309,14 +344,25 @@ __global__ void __launch_bounds__(HEAD_THREADS) head_kernel(HeadArgs a) {
             if (NORM) {
                 float s = 0.f;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) s = add_rn(s, bf(mul_rn(v[i], v[i])));
+                for (int i = 0; i < 8; i += 2) {
+                    float q0 = mul_rn(v[i], v[i]), q1 = mul_rn(v[i + 1], v[i + 1]);
+                    bf2(q0, q1);
+                    s = add_rn(s, q0);
+                    s = add_rn(s, q1);
+                }
 #pragma unroll
                 for (int o = 8; o > 0; o >>= 1) s = add_rn(s, __shfl_xor_sync(0xffffffffu, s, o));  // within the half
-                const float mean = bf(__fdiv_rn(s, 128.0f));
+                const float mean = bf(__fmul_rn(s, 0.0078125f));   // s / 128, exact (power of two)
                 const float var = bf(add_rn(mean, a.eps));
                 const float r = bf(rsqrt_torch(var));
 #pragma unroll
-                for (int i = 0; i < 8; ++i) v[i] = bf(mul_rn(bf(mul_rn(v[i], r)), w[i]));
+                for (int i = 0; i < 8; i += 2) {
+                    float n0 = mul_rn(v[i], r), n1 = mul_rn(v[i + 1], r);
+                    bf2(n0, n1);
+                    v[i] = mul_rn(n0, w[i]);
+                    v[i + 1] = mul_rn(n1, w[i + 1]);
+                    bf2(v[i], v[i + 1]);
+                }
             }
             float o[8];
             if (a.half > 0) {
@@ -329,12 +375,18 @@ __global__ void __launch_bounds__(HEAD_THREADS) head_kernel(HeadArgs a) {
                 theirs.w = __shfl_sync(0xffffffffu, mine.w, src);
                 float pv[8];
                 unpack8(theirs, pv);
-                if (hl < d) {            // first half: y0 = bf(bf(a*c) + bf(-b*s))
+                if (hl < 2 * d) {
+                    // first half: y0 = bf(bf(a*c) + bf(-b*s)); second half: y1 = bf(bf(b*c) + bf(a*s))
+                    const float sign = hl < d ? -1.0f : 1.0f;
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) o[i] = add_rn(bf(mul_rn(v[i], c[i])), bf(mul_rn(-pv[i], sn[i])));
-                } else if (hl < 2 * d) { // second half: y1 = bf(bf(b*c) + bf(a*s))
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) o[i] = add_rn(bf(mul_rn(v[i], c[i])), bf(mul_rn(pv[i], sn[i])));
+                    for (int i = 0; i < 8; i += 2) {
+                        float c0 = mul_rn(v[i], c[i]), c1 = mul_rn(v[i + 1], c[i + 1]);
+                        float s0 = mul_rn(sign * pv[i], sn[i]), s1 = mul_rn(sign * pv[i + 1], sn[i + 1]);
+                        bf2(c0, c1);
+                        bf2(s0, s1);
+                        o[i] = add_rn(c0, s0);
+                        o[i + 1] = add_rn(c1, s1);
+                    }
                 } else {
 #pragma unroll
                     for (int i = 0; i < 8; ++i) o[i] = v[i];
