@@ -185,14 +185,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                         uint32_t w[16];
 #pragma unroll
                         for (int i = 0; i < 16; ++i) {
-                            float up0 = __uint_as_float(u[2 * i]), up1 = __uint_as_float(u[2 * i + 1]);
-                            float g0 = __uint_as_float(g[2 * i]), g1 = __uint_as_float(g[2 * i + 1]);
-                            bf2(up0, up1);   // the linear's BF16 outputs
-                            bf2(g0, g1);
-                            float a0 = __fdiv_rn(g0, add_rn(1.0f, expf(-g0)));
-                            float a1 = __fdiv_rn(g1, add_rn(1.0f, expf(-g1)));
-                            bf2(a0, a1);
-                            w[i] = pack2(mul_rn(up0, a0), mul_rn(up1, a1));
+                            // the linear's BF16 outputs, then bf16(up * bf16(g / (1 + exp(-g))))
+                            const uint32_t up2 = pack2(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1]));
+                            const uint32_t g2 = pack2(__uint_as_float(g[2 * i]), __uint_as_float(g[2 * i + 1]));
+                            const float g0 = blo(g2), g1 = bhi(g2);
+                            const float a0 = __fdiv_rn(g0, add_rn(1.0f, expf(-g0)));
+                            const float a1 = __fdiv_rn(g1, add_rn(1.0f, expf(-g1)));
+                            w[i] = bmul2(up2, pack2(a0, a1));
                         }
                         __nv_bfloat16 *dst = p.out + (int64_t)row * p.ldo + col;
 #pragma unroll
@@ -217,17 +216,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                             const __nv_bfloat16 *gp = p.gate + (int64_t)row * p.ldg + col;
 #pragma unroll
                             for (int q = 0; q < 4; ++q) {
-                                float rf[8], gf[8];
-                                unpack8(*reinterpret_cast<const uint4 *>(rp + 8 * q), rf);
-                                unpack8(*reinterpret_cast<const uint4 *>(gp + 8 * q), gf);
+                                const uint4 r4 = *reinterpret_cast<const uint4 *>(rp + 8 * q);
+                                const uint4 g4 = *reinterpret_cast<const uint4 *>(gp + 8 * q);
 #pragma unroll
-                                for (int e = 0; e < 4; ++e) {
+                                for (int e = 0; e < 4; ++e) {   // bf16(res + bf16(gate * bf16(acc)))
                                     const int idx = 8 * q + 2 * e;
-                                    float y0 = __uint_as_float(v[idx]), y1 = __uint_as_float(v[idx + 1]);
-                                    bf2(y0, y1);   // the linear's BF16 output
-                                    float p0 = mul_rn(gf[2 * e], y0), p1 = mul_rn(gf[2 * e + 1], y1);
-                                    bf2(p0, p1);
-                                    w[4 * q + e] = pack2(add_rn(rf[2 * e], p0), add_rn(rf[2 * e + 1], p1));
+                                    const uint32_t y2 = pack2(__uint_as_float(v[idx]), __uint_as_float(v[idx + 1]));
+                                    w[4 * q + e] = badd2(w32(r4, e), bmul2(w32(g4, e), y2));
                                 }
                             }
                         }

@@ -25,6 +25,33 @@ __device__ __forceinline__ void bf2(float &a, float &b) {
     b = f.y;
 }
 __device__ __forceinline__ float mul_rn(float a, float b) { return __fmul_rn(a, b); }
+
+// Packed BF16x2 arithmetic.  For BF16 operands a, b: bf16(fp32(a*b)) is the
+// correctly rounded BF16 product (the fp32 product is exact), and
+// bf16(fp32(a+b)) is the correctly rounded BF16 sum (the fp32 sum is exact
+// unless the smaller term is below 2^-16 of the larger, where both roundings
+// return the larger term).  So one mul.rn.bf16x2 / add.rn.bf16x2 reproduces
+// the reference's "fp32 op, then .to(bf16)" step bit for bit, two lanes at a time.
+// The .rn modifier is explicit: without it ptxas may contract a mul followed by
+// an add into one fma (one rounding instead of the reference's two).
+__device__ __forceinline__ __nv_bfloat162 u2bf(uint32_t u) { return *reinterpret_cast<__nv_bfloat162 *>(&u); }
+__device__ __forceinline__ uint32_t bf2u(__nv_bfloat162 b) { return *reinterpret_cast<uint32_t *>(&b); }
+__device__ __forceinline__ uint32_t bmul2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t badd2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t bneg2(uint32_t a) { return a ^ 0x80008000u; }
+__device__ __forceinline__ uint32_t bsplat(float v) { return bf2u(__float2bfloat162_rn(v)); }  // v BF16-valued
+__device__ __forceinline__ float blo(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bhi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
+__device__ __forceinline__ uint32_t &w32(uint4 &v, int i) { return reinterpret_cast<uint32_t *>(&v)[i]; }
+__device__ __forceinline__ uint32_t w32(const uint4 &v, int i) { return reinterpret_cast<const uint32_t *>(&v)[i]; }
 __device__ __forceinline__ float add_rn(float a, float b) { return __fadd_rn(a, b); }
 
 __device__ __forceinline__ void unpack8(const uint4 &v, float f[8]) {
@@ -64,6 +91,29 @@ __device__ __forceinline__ float rsqrt_torch(float v) { return __fdiv_rn(1.0f, _
 // Row views: a tensor seen as [n0, n1, C] rows of C elements.  Leading dims of
 // a 2-D tensor collapse to n0 = 1.  Strides in elements; stride 0 broadcasts.
 // ---------------------------------------------------------------------------
+// Unsigned 32-bit division by a run-time invariant divisor with one multiply-high
+// (Granlund & Montgomery, "Division by invariant integers using multiplication",
+// PLDI 1994, round-up method): for d > 1, l = ceil(log2 d),
+// m = floor(2^32 (2^l - d) / d) + 1, q = (t + ((n - t) >> 1)) >> (l - 1) with
+// t = umulhi(n, m).  Exact for every 32-bit n; d == 1 is handled separately.
+struct FastDiv {
+    uint32_t d, m, l;
+    __host__ static FastDiv make(uint32_t d) {
+        FastDiv f;
+        f.d = d;
+        uint32_t l = 0;
+        while ((1ull << l) < d) ++l;
+        f.l = l;
+        f.m = d > 1 ? (uint32_t)((((1ull << 32) * ((1ull << l) - d)) / d) + 1) : 0;
+        return f;
+    }
+    __device__ __forceinline__ uint32_t div(uint32_t n) const {
+        if (d == 1) return n;
+        const uint32_t t = __umulhi(n, m);
+        return (t + ((n - t) >> 1)) >> (l - 1);
+    }
+};
+
 struct RowView {
     const __nv_bfloat16 *p;
     int64_t s0, s1, sc;

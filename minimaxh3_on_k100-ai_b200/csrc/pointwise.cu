@@ -62,21 +62,23 @@ struct EwArgs {
 enum { EW_GATED_RESIDUAL = 0, EW_SWIGLU = 1 };
 constexpr int EW_THREADS = 256, EW_VPT = 2;   // vectors of 8 per thread
 
-// two elements at a time (paired BF16 roundings); outputs are rounded by the store
+// 8 elements (one 16-byte vector) of either op
 template <int OP>
-__device__ __forceinline__ void ew_apply2(const float *a, const float *b, const float *c, float *o) {
-    if (OP == EW_GATED_RESIDUAL) {          // bf16(x + bf16(gate * y))
-        float p0 = mul_rn(b[0], c[0]), p1 = mul_rn(b[1], c[1]);
-        bf2(p0, p1);
-        o[0] = add_rn(a[0], p0);
-        o[1] = add_rn(a[1], p1);
-    } else {                                // bf16(up * bf16(g / (1 + exp(-g))))
-        float a0 = __fdiv_rn(b[0], add_rn(1.0f, expf(-b[0])));
-        float a1 = __fdiv_rn(b[1], add_rn(1.0f, expf(-b[1])));
-        bf2(a0, a1);
-        o[0] = mul_rn(a[0], a0);
-        o[1] = mul_rn(a[1], a1);
+__device__ __forceinline__ uint4 ew_apply8(uint4 a, uint4 b, uint4 c) {
+    uint4 o;
+    if (OP == EW_GATED_RESIDUAL) {           // bf16(x + bf16(gate * y))
+#pragma unroll
+        for (int i = 0; i < 4; ++i) w32(o, i) = badd2(w32(a, i), bmul2(w32(b, i), w32(c, i)));
+    } else {                                 // bf16(up * bf16(g / (1 + exp(-g))))
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float g0 = blo(w32(b, i)), g1 = bhi(w32(b, i));
+            float a0 = __fdiv_rn(g0, add_rn(1.0f, expf(-g0)));
+            float a1 = __fdiv_rn(g1, add_rn(1.0f, expf(-g1)));
+            w32(o, i) = bmul2(w32(a, i), bf2u(__floats2bfloat162_rn(a0, a1)));
+        }
     }
+    return o;
 }
 
 template <int OP, bool VEC>
@@ -91,6 +93,7 @@ __global__ void __launch_bounds__(EW_THREADS) ew_kernel(EwArgs args) {
 #pragma unroll
         for (int k = 0; k < EW_VPT; ++k) {
             const int64_t vi = (int64_t)blockIdx.x * (EW_THREADS * EW_VPT) + k * EW_THREADS + threadIdx.x;
+            vc[k] = make_uint4(0, 0, 0, 0);
             if (vi < nvec) {
                 va[k] = load8p<VEC>(pa, args.a.sc, vi * 8, args.C);
                 vb[k] = load8p<VEC>(pb, args.b.sc, vi * 8, args.C);
@@ -100,15 +103,7 @@ __global__ void __launch_bounds__(EW_THREADS) ew_kernel(EwArgs args) {
 #pragma unroll
         for (int k = 0; k < EW_VPT; ++k) {
             const int64_t vi = (int64_t)blockIdx.x * (EW_THREADS * EW_VPT) + k * EW_THREADS + threadIdx.x;
-            if (vi < nvec) {
-                float fa[8], fb[8], fc[8], fo[8];
-                unpack8(va[k], fa);
-                unpack8(vb[k], fb);
-                if (OP == EW_GATED_RESIDUAL) unpack8(vc[k], fc);
-#pragma unroll
-                for (int i = 0; i < 8; i += 2) ew_apply2<OP>(fa + i, fb + i, fc + i, fo + i);
-                store8p<VEC>(po, args.o.sc, vi * 8, args.C, pack8(fo));
-            }
+            if (vi < nvec) store8p<VEC>(po, args.o.sc, vi * 8, args.C, ew_apply8<OP>(va[k], vb[k], vc[k]));
         }
     }
 }
@@ -139,33 +134,29 @@ __global__ void __launch_bounds__(ROW_WARPS * 32) row_kernel(RowArgs args) {
     const __nv_bfloat16 *xrow = args.x.p + row_offset(args.x.s0, args.x.s1, row, args.n1);
 
     uint4 v[VPT];
-#pragma unroll
-    for (int k = 0; k < VPT; ++k) {
-        const int64_t vi = lane + 32 * k;
-        v[k] = vi < nvec ? load8p<VEC>(xrow, args.x.sc, vi * 8, C) : make_uint4(0, 0, 0, 0);
-    }
     if (MODE == ROW_RES_RMS_MOD) {
+        // residual = bf16(x + bf16(gate * y)), written out and normalised
         const __nv_bfloat16 *grow = args.gate.p + row_offset(args.gate.s0, args.gate.s1, row, args.n1);
         const __nv_bfloat16 *yrow = args.y.p + row_offset(args.y.s0, args.y.s1, row, args.n1);
         __nv_bfloat16 *rrow = args.residual.p + row_offset(args.residual.s0, args.residual.s1, row, args.n1);
 #pragma unroll
         for (int k = 0; k < VPT; ++k) {
             const int64_t vi = lane + 32 * k;
+            v[k] = make_uint4(0, 0, 0, 0);
             if (vi < nvec) {
-                float fx[8], fg[8], fy[8];
-                unpack8(v[k], fx);
-                unpack8(load8p<VEC>(grow, args.gate.sc, vi * 8, C), fg);
-                unpack8(load8p<VEC>(yrow, args.y.sc, vi * 8, C), fy);
+                const uint4 x = load8p<VEC>(xrow, args.x.sc, vi * 8, C);
+                const uint4 g = load8p<VEC>(grow, args.gate.sc, vi * 8, C);
+                const uint4 y = load8p<VEC>(yrow, args.y.sc, vi * 8, C);
 #pragma unroll
-                for (int i = 0; i < 8; i += 2) {
-                    float p0 = mul_rn(fg[i], fy[i]), p1 = mul_rn(fg[i + 1], fy[i + 1]);
-                    bf2(p0, p1);
-                    fx[i] = add_rn(fx[i], p0);
-                    fx[i + 1] = add_rn(fx[i + 1], p1);
-                }
-                v[k] = pack8(fx);                 // residual, rounded to BF16
+                for (int i = 0; i < 4; ++i) w32(v[k], i) = badd2(w32(x, i), bmul2(w32(g, i), w32(y, i)));
                 store8p<VEC>(rrow, args.residual.sc, vi * 8, C, v[k]);
             }
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < VPT; ++k) {
+            const int64_t vi = lane + 32 * k;
+            v[k] = vi < nvec ? load8p<VEC>(xrow, args.x.sc, vi * 8, C) : make_uint4(0, 0, 0, 0);
         }
     }
 
@@ -174,23 +165,25 @@ __global__ void __launch_bounds__(ROW_WARPS * 32) row_kernel(RowArgs args) {
     if (MODE == ROW_LN_MOD) {
         float s = 0.f;
 #pragma unroll
-        for (int k = 0; k < VPT; ++k) {
-            float f[8];
-            unpack8(v[k], f);
+        for (int k = 0; k < VPT; ++k)
 #pragma unroll
-            for (int i = 0; i < 8; ++i) s = add_rn(s, f[i]);
-        }
+            for (int i = 0; i < 4; ++i) {
+                s = add_rn(s, blo(w32(v[k], i)));
+                s = add_rn(s, bhi(w32(v[k], i)));
+            }
         const float mean = __fdiv_rn(warp_sum(s), (float)C);
         float q = 0.f;
 #pragma unroll
         for (int k = 0; k < VPT; ++k) {
             const int64_t vi = lane + 32 * k;
-            float f[8];
-            unpack8(v[k], f);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                if (vi * 8 + i < C) {
-                    const float d = __fsub_rn(f[i], mean);
+            for (int i = 0; i < 4; ++i) {
+                if (vi * 8 + 2 * i < C) {
+                    const float d = __fsub_rn(blo(w32(v[k], i)), mean);
+                    q = __fmaf_rn(d, d, q);
+                }
+                if (vi * 8 + 2 * i + 1 < C) {
+                    const float d = __fsub_rn(bhi(w32(v[k], i)), mean);
                     q = __fmaf_rn(d, d, q);
                 }
             }
@@ -201,17 +194,13 @@ __global__ void __launch_bounds__(ROW_WARPS * 32) row_kernel(RowArgs args) {
     } else {
         float s = 0.f;
 #pragma unroll
-        for (int k = 0; k < VPT; ++k) {
-            float f[8];
-            unpack8(v[k], f);
+        for (int k = 0; k < VPT; ++k)
 #pragma unroll
-            for (int i = 0; i < 8; i += 2) {  // bf16(x^2), summed in column order
-                float q0 = mul_rn(f[i], f[i]), q1 = mul_rn(f[i + 1], f[i + 1]);
-                bf2(q0, q1);
-                s = add_rn(s, q0);
-                s = add_rn(s, q1);
+            for (int i = 0; i < 4; ++i) {   // bf16(x^2), summed in fp32 in column order
+                const uint32_t sq = bmul2(w32(v[k], i), w32(v[k], i));
+                s = add_rn(s, blo(sq));
+                s = add_rn(s, bhi(sq));
             }
-        }
         const float mean = bf(__fdiv_rn(warp_sum(s), (float)C));
         const float var = bf(add_rn(mean, args.eps));
         r = bf(rsqrt_torch(var));
@@ -224,52 +213,40 @@ __global__ void __launch_bounds__(ROW_WARPS * 32) row_kernel(RowArgs args) {
         hrow = args.shift.p + row_offset(args.shift.s0, args.shift.s1, row, args.n1);
     }
     __nv_bfloat16 *orow = args.out.p + row_offset(args.out.s0, args.out.s1, row, args.n1);
+    const uint32_t r2 = bsplat(r);
+    const uint32_t one2 = 0x3f803f80u;                       // (1.0, 1.0) in BF16
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
         const int64_t vi = lane + 32 * k;
         if (vi >= nvec) continue;
-        float f[8], o[8];
-        unpack8(v[k], f);
+        uint4 o;
         if (MODE == ROW_LN_MOD) {
 #pragma unroll
-            for (int i = 0; i < 8; i += 2) {
-                o[i] = __fmaf_rn(f[i], r, shift_ln);
-                o[i + 1] = __fmaf_rn(f[i + 1], r, shift_ln);
-                bf2(o[i], o[i + 1]);
-            }
+            for (int i = 0; i < 4; ++i)
+                w32(o, i) = bf2u(__floats2bfloat162_rn(__fmaf_rn(blo(w32(v[k], i)), r, shift_ln),
+                                                       __fmaf_rn(bhi(w32(v[k], i)), r, shift_ln)));
         } else {
-            float w[8];
+            uint4 w;
             if (VEC && args.wsc == 1) {
-                unpack8(*reinterpret_cast<const uint4 *>(args.weight + vi * 8), w);
+                w = *reinterpret_cast<const uint4 *>(args.weight + vi * 8);
             } else {
+                float f[8];
 #pragma unroll
                 for (int i = 0; i < 8; ++i)
-                    w[i] = (vi * 8 + i < C) ? __bfloat162float(args.weight[(vi * 8 + i) * args.wsc]) : 0.f;
+                    f[i] = (vi * 8 + i < C) ? __bfloat162float(args.weight[(vi * 8 + i) * args.wsc]) : 0.f;
+                w = pack8(f);
             }
 #pragma unroll
-            for (int i = 0; i < 8; i += 2) {
-                float n0 = mul_rn(f[i], r), n1 = mul_rn(f[i + 1], r);
-                bf2(n0, n1);
-                o[i] = mul_rn(n0, w[i]);
-                o[i + 1] = mul_rn(n1, w[i + 1]);
-                bf2(o[i], o[i + 1]);
-            }
+            for (int i = 0; i < 4; ++i) w32(o, i) = bmul2(bmul2(w32(v[k], i), r2), w32(w, i));  // bf(bf(x*r)*w)
         }
         if (MODE != ROW_RMS) {
-            float sc[8], sh[8];
-            unpack8(load8p<VEC>(srow, args.scale.sc, vi * 8, C), sc);
-            unpack8(load8p<VEC>(hrow, args.shift.sc, vi * 8, C), sh);
+            const uint4 sc = load8p<VEC>(srow, args.scale.sc, vi * 8, C);
+            const uint4 sh = load8p<VEC>(hrow, args.shift.sc, vi * 8, C);
 #pragma unroll
-            for (int i = 0; i < 8; i += 2) {
-                float f0 = add_rn(sc[i], 1.0f), f1 = add_rn(sc[i + 1], 1.0f);
-                bf2(f0, f1);
-                float m0 = mul_rn(o[i], f0), m1 = mul_rn(o[i + 1], f1);
-                bf2(m0, m1);
-                o[i] = add_rn(m0, sh[i]);
-                o[i + 1] = add_rn(m1, sh[i + 1]);
-            }
+            for (int i = 0; i < 4; ++i)     // bf(bf(o * bf(1 + scale)) + shift)
+                w32(o, i) = badd2(bmul2(w32(o, i), badd2(w32(sc, i), one2)), w32(sh, i));
         }
-        store8p<VEC>(orow, args.out.sc, vi * 8, C, pack8(o));
+        store8p<VEC>(orow, args.out.sc, vi * 8, C, o);
     }
 }
 
@@ -286,120 +263,97 @@ struct HeadArgs {
     const __nv_bfloat16 *cos, *sin;
     int64_t cs0, cs1, ss0, ss1;
     int64_t T, P, Hs;
+    FastDiv div_ph, div_hs;        // by P*Hs and by Hs
     int half;                      // rotated pairs (48 or 64); 0 = no rotation
     float eps;
 };
 
 constexpr int HEAD_THREADS = 128;                                      // 8 half-warps
-constexpr int HEAD_ROWS_PER_HW = 2;                                    // rows in flight per half-warp
+constexpr int HEAD_ROWS_PER_HW = 4;                                    // rows in flight per half-warp
 constexpr int HEAD_ROWS_PER_CTA = (HEAD_THREADS / 16) * HEAD_ROWS_PER_HW;
 
-// grid: x over the P*Hs head rows of one token (HEAD_ROWS_PER_CTA per CTA), y over tokens
+// Flat head rows r = (t * P + p) * Hs + h; a CTA takes HEAD_ROWS_PER_CTA
+// consecutive rows, each half-warp HEAD_ROWS_PER_HW of them (loads first).
 template <bool NORM, bool VEC>
 __global__ void __launch_bounds__(HEAD_THREADS) head_kernel(HeadArgs a) {
     const int lane = threadIdx.x & 31;
     const int hl = lane & 15;                    // lane within the half-warp: elements [8hl, 8hl+8)
     const int hw_base = lane & 16;
     const int hw = threadIdx.x >> 4;             // half-warp index in the CTA
-    const int ph_count = (int)(a.P * a.Hs);
+    const uint32_t PH = (uint32_t)(a.P * a.Hs), Hs = (uint32_t)a.Hs;
+    const uint32_t rows = (uint32_t)a.T * PH;
     const int d = a.half >> 3;                   // lanes per rotated half
     const int partner = hl < d ? hl + d : (hl < 2 * d ? hl - d : hl);
+    const bool rot_lane = a.half > 0 && hl < 2 * d;
 
-    for (int64_t t = blockIdx.y; t < a.T; t += gridDim.y) {
-        uint4 xv[HEAD_ROWS_PER_HW];
-        int phs[HEAD_ROWS_PER_HW];
-        uint4 cv = make_uint4(0, 0, 0, 0), sv = make_uint4(0, 0, 0, 0);
-        if (a.half > 0 && hl < 2 * d) {          // the token's angles, shared by its heads
-            const int j = 8 * (hl < d ? hl : hl - d);
-            cv = load8p<VEC>(a.cos + t * a.cs0 + j * a.cs1, a.cs1, 0, 8);
-            sv = load8p<VEC>(a.sin + t * a.ss0 + j * a.ss1, a.ss1, 0, 8);
-        }
+    uint4 xv[HEAD_ROWS_PER_HW], cv[HEAD_ROWS_PER_HW], sv[HEAD_ROWS_PER_HW];
+    uint32_t rr[HEAD_ROWS_PER_HW], tt[HEAD_ROWS_PER_HW], pp[HEAD_ROWS_PER_HW], hh[HEAD_ROWS_PER_HW];
 #pragma unroll
-        for (int u = 0; u < HEAD_ROWS_PER_HW; ++u) {
-            const int ph = blockIdx.x * HEAD_ROWS_PER_CTA + u * (HEAD_THREADS / 16) + hw;
-            phs[u] = ph;
-            if (ph < ph_count) {
-                const int p = ph / (int)a.Hs, h = ph - p * (int)a.Hs;
-                xv[u] = load8p<VEC>(a.x + t * a.xs[0] + p * a.xs[1] + h * a.xs[2], a.xs[3], 8 * hl, 128);
-            } else {
-                xv[u] = make_uint4(0, 0, 0, 0);
+    for (int u = 0; u < HEAD_ROWS_PER_HW; ++u) {
+        const uint32_t r = blockIdx.x * (uint32_t)HEAD_ROWS_PER_CTA + u * (HEAD_THREADS / 16) + hw;
+        rr[u] = r;
+        xv[u] = cv[u] = sv[u] = make_uint4(0, 0, 0, 0);
+        const uint32_t t = a.div_ph.div(r), ph = r - t * PH, p = a.div_hs.div(ph), h = ph - p * Hs;
+        tt[u] = t;
+        pp[u] = p;
+        hh[u] = h;
+        if (r < rows) {
+            xv[u] = load8p<VEC>(a.x + t * a.xs[0] + p * a.xs[1] + h * a.xs[2], a.xs[3], 8 * hl, 128);
+            if (rot_lane) {
+                const int j = 8 * (hl < d ? hl : hl - d);
+                cv[u] = load8p<VEC>(a.cos + t * a.cs0 + j * a.cs1, a.cs1, 0, 8);
+                sv[u] = load8p<VEC>(a.sin + t * a.ss0 + j * a.ss1, a.ss1, 0, 8);
             }
         }
-        float w[8];
+    }
+    uint4 w = make_uint4(0, 0, 0, 0);
+    if (NORM) {
+        if (VEC && a.wsc == 1) {
+            w = *reinterpret_cast<const uint4 *>(a.weight + 8 * hl);
+        } else {
+            float f[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) f[i] = __bfloat162float(a.weight[(8 * hl + i) * a.wsc]);
+            w = pack8(f);
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < HEAD_ROWS_PER_HW; ++u) {
+        uint4 v = xv[u];
         if (NORM) {
-            if (VEC && a.wsc == 1) {
-                unpack8(*reinterpret_cast<const uint4 *>(a.weight + 8 * hl), w);
-            } else {
+            float s = 0.f;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) w[i] = __bfloat162float(a.weight[(8 * hl + i) * a.wsc]);
+            for (int i = 0; i < 4; ++i) {        // bf16(x^2), fp32 sum in column order
+                const uint32_t sq = bmul2(w32(v, i), w32(v, i));
+                s = add_rn(s, blo(sq));
+                s = add_rn(s, bhi(sq));
+            }
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) s = add_rn(s, __shfl_xor_sync(0xffffffffu, s, o));  // within the half
+            const float mean = bf(__fmul_rn(s, 0.0078125f));   // s / 128, exact (power of two)
+            const float var = bf(add_rn(mean, a.eps));
+            const uint32_t r2 = bsplat(bf(rsqrt_torch(var)));
+#pragma unroll
+            for (int i = 0; i < 4; ++i) w32(v, i) = bmul2(bmul2(w32(v, i), r2), w32(w, i));  // bf(bf(x*r)*w)
+        }
+        uint4 o = v;
+        if (a.half > 0) {
+            uint4 pv;                            // the RoPE partner's values (same row)
+            const int src = hw_base | partner;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) w32(pv, i) = __shfl_sync(0xffffffffu, w32(v, i), src);
+            if (rot_lane) {
+                // first half:  y0 = bf(bf(a*c) + bf(-b*s));  second half: y1 = bf(bf(b*c) + bf(a*s))
+                const bool first = hl < d;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const uint32_t other = first ? bneg2(w32(pv, i)) : w32(pv, i);
+                    w32(o, i) = badd2(bmul2(w32(v, i), w32(cv[u], i)), bmul2(other, w32(sv[u], i)));
+                }
             }
         }
-        float c[8], sn[8];
-        unpack8(cv, c);
-        unpack8(sv, sn);
-#pragma unroll
-        for (int u = 0; u < HEAD_ROWS_PER_HW; ++u) {
-            float v[8];
-            unpack8(xv[u], v);
-            if (NORM) {
-                float s = 0.f;
-#pragma unroll
-                for (int i = 0; i < 8; i += 2) {
-                    float q0 = mul_rn(v[i], v[i]), q1 = mul_rn(v[i + 1], v[i + 1]);
-                    bf2(q0, q1);
-                    s = add_rn(s, q0);
-                    s = add_rn(s, q1);
-                }
-#pragma unroll
-                for (int o = 8; o > 0; o >>= 1) s = add_rn(s, __shfl_xor_sync(0xffffffffu, s, o));  // within the half
-                const float mean = bf(__fmul_rn(s, 0.0078125f));   // s / 128, exact (power of two)
-                const float var = bf(add_rn(mean, a.eps));
-                const float r = bf(rsqrt_torch(var));
-#pragma unroll
-                for (int i = 0; i < 8; i += 2) {
-                    float n0 = mul_rn(v[i], r), n1 = mul_rn(v[i + 1], r);
-                    bf2(n0, n1);
-                    v[i] = mul_rn(n0, w[i]);
-                    v[i + 1] = mul_rn(n1, w[i + 1]);
-                    bf2(v[i], v[i + 1]);
-                }
-            }
-            float o[8];
-            if (a.half > 0) {
-                const uint4 mine = pack8(v);   // exact: v is BF16-valued
-                uint4 theirs;
-                const int src = hw_base | partner;
-                theirs.x = __shfl_sync(0xffffffffu, mine.x, src);
-                theirs.y = __shfl_sync(0xffffffffu, mine.y, src);
-                theirs.z = __shfl_sync(0xffffffffu, mine.z, src);
-                theirs.w = __shfl_sync(0xffffffffu, mine.w, src);
-                float pv[8];
-                unpack8(theirs, pv);
-                if (hl < 2 * d) {
-                    // first half: y0 = bf(bf(a*c) + bf(-b*s)); second half: y1 = bf(bf(b*c) + bf(a*s))
-                    const float sign = hl < d ? -1.0f : 1.0f;
-#pragma unroll
-                    for (int i = 0; i < 8; i += 2) {
-                        float c0 = mul_rn(v[i], c[i]), c1 = mul_rn(v[i + 1], c[i + 1]);
-                        float s0 = mul_rn(sign * pv[i], sn[i]), s1 = mul_rn(sign * pv[i + 1], sn[i + 1]);
-                        bf2(c0, c1);
-                        bf2(s0, s1);
-                        o[i] = add_rn(c0, s0);
-                        o[i + 1] = add_rn(c1, s1);
-                    }
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) o[i] = v[i];
-                }
-            } else {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) o[i] = v[i];
-            }
-            if (phs[u] < ph_count) {
-                const int p = phs[u] / (int)a.Hs, h = phs[u] - p * (int)a.Hs;
-                store8p<VEC>(a.out + t * a.os[0] + p * a.os[1] + h * a.os[2], a.os[3], 8 * hl, 128, pack8(o));
-            }
-        }
+        if (rr[u] < rows)
+            store8p<VEC>(a.out + tt[u] * a.os[0] + pp[u] * a.os[1] + hh[u] * a.os[2], a.os[3], 8 * hl, 128, o);
     }
 }
 
@@ -663,6 +617,9 @@ static int head_launch(const h3_tensor *out, const h3_tensor *x, const h3_tensor
     a.cs0 = cos->strides[0]; a.cs1 = cos->strides[1];
     a.ss0 = sin->strides[0]; a.ss1 = sin->strides[1];
     a.T = shp[0]; a.P = shp[1]; a.Hs = shp[2];
+    if (a.P * a.Hs <= 0 || a.P * a.Hs > 0x7fffffffLL) return a.T == 0 || a.P * a.Hs == 0 ? H3_OK : H3_ERR_UNSUPPORTED;
+    a.div_ph = FastDiv::make((uint32_t)(a.P * a.Hs));
+    a.div_hs = FastDiv::make((uint32_t)a.Hs);
     a.half = (int)cos->shape[1];
     a.eps = eps;
     const int64_t rows = a.T * a.P * a.Hs;
@@ -671,9 +628,8 @@ static int head_launch(const h3_tensor *out, const h3_tensor *x, const h3_tensor
                aligned16(out->data) && aligned16(cos->data) && aligned16(sin->data);
     for (int i = 0; i < 3; ++i) vec = vec && (xs[i] % 8 == 0) && (os[i] % 8 == 0);
     vec = vec && a.cs0 % 8 == 0 && a.ss0 % 8 == 0;
-    if (a.P * a.Hs > (1 << 24)) return H3_ERR_UNSUPPORTED;
-    const dim3 g((unsigned)((a.P * a.Hs + HEAD_ROWS_PER_CTA - 1) / HEAD_ROWS_PER_CTA),
-                 (unsigned)(a.T < 65535 ? a.T : 65535));
+    if (rows > 0x7fffffffLL) return H3_ERR_UNSUPPORTED;
+    const unsigned g = (unsigned)((rows + HEAD_ROWS_PER_CTA - 1) / HEAD_ROWS_PER_CTA);
     if (norm) {
         if (vec) head_kernel<true, true><<<g, HEAD_THREADS, 0, stream>>>(a);
         else head_kernel<true, false><<<g, HEAD_THREADS, 0, stream>>>(a);
