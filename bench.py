@@ -42,7 +42,7 @@ def parse():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--blocks", type=int, default=40)
-    p.add_argument("--no-graph", action="store_true", help="eager launches instead of a CUDA graph (N=1)")
+    p.add_argument("--no-graph", action="store_true", help="eager launches instead of one CUDA graph per step")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--workload", choices=["step", "attention", "pointwise"], default="step",
                    help="step: BASELINE config 5 (default, the headline); attention: config 2; "
@@ -82,16 +82,21 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self):
+    def __init__(self, n_gpus: int = 1):
         self.proc = None
         self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+        # the physical GPUs this job runs on (rank i uses visible device i)
+        visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+        ids = visible.split(",")[:n_gpus] if visible else [str(i) for i in range(n_gpus)]
+        self.ids = ",".join(x.strip() for x in ids)
 
     def start(self):
         try:
             os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.f = open(self.path, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", self.ids, f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
 
@@ -208,29 +213,32 @@ def run_ours(args, rank, world, local_rank, group):
     launches_per_step = _lib.CALLS["n"] - c0
     sync_all()
 
-    use_graph = world == 1 and not args.no_graph
-    graph = None
-    if use_graph:
-        s = torch.cuda.Stream(device)
-        s.wait_stream(torch.cuda.current_stream(device))
-        with torch.cuda.stream(s):
-            step.forward(x_dev)
-        torch.cuda.current_stream(device).wait_stream(s)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            graph_out = step.forward(x_dev)
+    # The whole step (kernels and, at N > 1, the NCCL all-to-alls) is captured in
+    # one CUDA graph and replayed; if capture is not possible the step runs eagerly.
+    graph_note = "disabled"
+    if not args.no_graph:
+        try:
+            step.capture()
+            graph_note = "captured"
+        except Exception as exc:  # noqa: BLE001 - fall back to eager launches, say so in the line
+            step.release_graph()
+            graph_note = f"eager ({type(exc).__name__})"
+            torch.cuda.synchronize(device)
+        if world > 1:
+            ok = torch.tensor([1 if step.graph is not None else 0], device=device)
+            torch.distributed.all_reduce(ok, op=torch.distributed.ReduceOp.MIN, group=group)
+            if int(ok.item()) == 0 and step.graph is not None:   # every rank must take the same path
+                step.release_graph()
+                graph_note = "eager (another rank could not capture)"
 
     def one_step():
-        if graph is not None:
-            graph.replay()
-        else:
-            step.forward(x_dev)
+        step.run()
 
     for _ in range(args.warmup):
         one_step()
     sync_all()
 
-    sampler = ClockSampler() if rank == 0 else None
+    sampler = ClockSampler(world) if rank == 0 else None
     if sampler:
         sampler.start()
         time.sleep(0.3)
@@ -247,13 +255,7 @@ def run_ours(args, rank, world, local_rank, group):
 
     # end to end through the public entry point: pinned host in, host out
     def e2e_step():
-        if graph is not None:
-            x_dev.copy_(x_host, non_blocking=True)
-            graph.replay()
-            out_host.copy_(graph_out, non_blocking=True)
-            stream.synchronize()
-        else:
-            step(x_host, out_host)
+        step(x_host, out_host)
 
     e2e_step()
     sync_all()
@@ -323,6 +325,9 @@ def run_ours(args, rank, world, local_rank, group):
         torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX, group=group)
     dev_s, e2e_s, attn_ms = vals.tolist()
 
+    # a graph holding NCCL calls must be released before destroy_process_group
+    step.release_graph()
+    torch.cuda.synchronize(device)
     if rank != 0:
         return None
     pk, pk_kind = peaks()
@@ -355,7 +360,7 @@ def run_ours(args, rank, world, local_rank, group):
                      "traffic": traffic, "flop_per_launch": attn_flop, "ms_per_launch": round(attn_ms, 3)},
         "step_tflops": round(step_flop / dev_s / 1e12, 1),
         "kernels": breakdown,
-        "cuda_graph": graph is not None,
+        "cuda_graph": graph_note,
         "clocks": clocks,
     }
     if world == 1 and not args.no_cpu_baseline:
@@ -559,20 +564,34 @@ def _ncu_traffic(kernel):
         return None
 
 
+def _json_stdout():
+    """Keep stdout for the one JSON line: libraries (NCCL prints its version on
+    rank 0) write to file descriptor 1, so fd 1 is pointed at stderr for the run
+    and the line is written to a saved copy of the original stdout."""
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    return os.fdopen(saved, "w")
+
+
+def _emit(out, line):
+    if line is not None:
+        out.write(json.dumps(line) + "\n")
+        out.flush()
+
+
 def main():
+    out = _json_stdout()
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.workload != "step" and args.impl == "ours":
         if rank == 0:
-            line = run_attention(args) if args.workload == "attention" else run_pointwise(args)
-            print(json.dumps(line), flush=True)
+            _emit(out, run_attention(args) if args.workload == "attention" else run_pointwise(args))
         return 0
     if args.impl == "reference":
-        line = run_reference(args, rank)
-        if line is not None:
-            print(json.dumps(line), flush=True)
+        _emit(out, run_reference(args, rank))
         return 0
     group = None
     if world > 1:
@@ -586,8 +605,7 @@ def main():
     finally:
         if world > 1:
             torch.distributed.destroy_process_group()
-    if line is not None:
-        print(json.dumps(line), flush=True)
+    _emit(out, line)
     return 0
 
 

@@ -85,6 +85,7 @@ class DiTStep:
                                        self.device)
         self.timestep = torch.full((1,), cfg.timestep, dtype=torch.float32, device=self.device)
         self.x_dev = torch.empty(self.local, bc.hidden, dtype=torch.bfloat16, device=self.device)
+        self.graph, self.graph_out = None, None
 
     def modulations(self, timestep: torch.Tensor) -> list[torch.Tensor]:
         temb = time_embedding(timestep, self.time)
@@ -99,10 +100,37 @@ class DiTStep:
                               out=self.ws.out[i % 2], sp=self.sp)
         return h
 
+    def capture(self) -> None:
+        """Record ``forward(self.x_dev)`` -- every kernel of the step and, under
+        sequence parallelism, its NCCL all-to-alls -- into one CUDA graph that
+        ``run()`` and ``__call__`` replay.  All ranks must capture together."""
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            self.forward(self.x_dev)          # warm-up outside the graph
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out = self.forward(self.x_dev)
+        self.graph, self.graph_out = graph, out
+
+    def release_graph(self) -> None:
+        """Drop the graph (required before destroying a process group whose
+        collectives it holds)."""
+        self.graph, self.graph_out = None, None
+
+    def run(self) -> torch.Tensor:
+        """One step on ``self.x_dev`` (graph replay when captured)."""
+        if getattr(self, "graph", None) is not None:
+            self.graph.replay()
+            return self.graph_out
+        return self.forward(self.x_dev)
+
     def __call__(self, x_host: torch.Tensor, out_host: torch.Tensor | None = None) -> torch.Tensor:
         """End to end: host (pinned) tokens in, host tokens out."""
         self.x_dev.copy_(x_host, non_blocking=True)
-        y = self.forward(self.x_dev)
+        y = self.run()
         if out_host is None:
             out_host = torch.empty(y.shape, dtype=y.dtype, pin_memory=True)
         out_host.copy_(y, non_blocking=True)
