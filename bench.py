@@ -277,13 +277,13 @@ def run_ours(args, rank, world, local_rank, group):
                                      qkv[:, 2].unsqueeze(0), 1.0 / math.sqrt(bc.head_dim))
         sq, sk, hh = t, cfg.tokens, bc.heads
     else:
-        b = step.sp.bufs
-        w_ = world
-        attn_call = lambda: ops.mha_(b.attn.unsqueeze(0), b.recv[0].view(1, w_ * t, -1, bc.head_dim),  # noqa: E731
-                                     b.recv[1].view(1, w_ * t, -1, bc.head_dim)[:, :cfg.tokens],
-                                     b.recv[2].view(1, w_ * t, -1, bc.head_dim)[:, :cfg.tokens],
+        sp = step.sp
+        w_, hs = world, sp.group_heads[0]
+        attn_call = lambda: ops.mha_(sp.attn[0].unsqueeze(0), sp.recv[0][0].view(1, w_ * t, hs, bc.head_dim),  # noqa: E731
+                                     sp.recv[0][1].view(1, w_ * t, hs, bc.head_dim)[:, :cfg.tokens],
+                                     sp.recv[0][2].view(1, w_ * t, hs, bc.head_dim)[:, :cfg.tokens],
                                      1.0 / math.sqrt(bc.head_dim))
-        sq, sk, hh = w_ * t, cfg.tokens, bc.heads // world
+        sq, sk, hh = w_ * t, cfg.tokens, hs
     for _ in range(2):
         attn_call()
     reps = 5
@@ -340,11 +340,16 @@ def run_ours(args, rank, world, local_rank, group):
             traffic = json.load(open(tpath)).get("fa_fwd_kernel", {}).get("bytes_per_launch_at_bench_shape")
         except ValueError:
             traffic = None
-    breakdown = {"attention": {"ms": round(attn_ms, 3), "tflops": round(achieved, 1), "launches_per_step": args.blocks}}
+    attn_launches = args.blocks * (len(step.sp.group_heads) if step.sp is not None else 1)
+    breakdown = {"attention": {"ms": round(attn_ms, 3), "tflops": round(achieved, 1),
+                               "launches_per_step": attn_launches}}
     for k, (ms, fl) in gemm.items():
         breakdown[k] = {"ms": round(ms, 3), "tflops": round(fl / (ms * 1e-3) / 1e12, 1),
                         "launches_per_step": args.blocks}
-    step_flop = args.blocks * (attn_flop * world + sum(fl for _, fl in gemm.values()) * world)
+    # model FLOPs of the step: all heads' attention over the joint sequence plus the
+    # block GEMMs on all tokens (AdaLN GEMVs excluded)
+    attn_total = 4.0 * cfg.tokens * cfg.tokens * bc.head_dim * bc.heads
+    step_flop = args.blocks * (attn_total + sum(fl for _, fl in gemm.values()) * world)
     line = {
         "metric": METRIC, "value": round(dev_s, 5), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(dev_s * 1e3, 3), "higher_is_better": False,

@@ -143,7 +143,7 @@ def block_forward(x: torch.Tensor, modulation: torch.Tensor, segments: list[Segm
                  1.0 / math.sqrt(d))
         attn_flat = ws.attn.view(t, hd)
     else:
-        attn_flat = sp.attention(ws, w, cos, sin, cfg)
+        attn_flat = sp.attention(ws.normalized, w.w_qkv, w.norm_q, w.norm_k, cos, sin, cfg.qk_eps)
     ops.linear_(ws.attn_out, attn_flat, w.w_o)
     for s in segments:
         r = slice(s.start, s.start + s.length)

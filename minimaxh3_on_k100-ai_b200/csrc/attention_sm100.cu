@@ -90,6 +90,32 @@ __device__ __forceinline__ float exp2_poly(float x) {
     return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
+// Blackwell packed fp32 pairs (fma.rn.f32x2 / add.rn.f32x2) and the 3-input
+// max halve the issue slots of the softmax's per-element fp32 work.
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void up2(uint64_t v, float &a, float &b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t *>(&v);
@@ -264,13 +290,13 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
-            for (int i = 0; i < 128; i += 4) {
-                mx0 = fmaxf(mx0, __uint_as_float(s[i]));
-                mx1 = fmaxf(mx1, __uint_as_float(s[i + 1]));
-                mx2 = fmaxf(mx2, __uint_as_float(s[i + 2]));
-                mx3 = fmaxf(mx3, __uint_as_float(s[i + 3]));
+            for (int i = 0; i < 128; i += 8) {
+                mx0 = max3f(mx0, __uint_as_float(s[i]), __uint_as_float(s[i + 1]));
+                mx1 = max3f(mx1, __uint_as_float(s[i + 2]), __uint_as_float(s[i + 3]));
+                mx2 = max3f(mx2, __uint_as_float(s[i + 4]), __uint_as_float(s[i + 5]));
+                mx3 = max3f(mx3, __uint_as_float(s[i + 6]), __uint_as_float(s[i + 7]));
             }
-            const float mnew = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * c;
+            const float mnew = fmaxf(max3f(mx0, mx1, mx2), mx3) * c;
             float alpha = 1.f;
             bool rescale = false;
             if (j == 0) {
@@ -293,39 +319,35 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
             }
             const float neg_m = -m;
-            float rs[4] = {0.f, 0.f, 0.f, 0.f};
+            const uint64_t c2 = pk2(c, c), nm2 = pk2(neg_m, neg_m);
+            uint64_t rs0 = pk2(0.f, 0.f), rs1 = pk2(0.f, 0.f);
             // P overwrites columns [0, 64) of this tile's S region (S is already in registers)
 #pragma unroll
             for (int hf = 0; hf < 2; ++hf) {
                 uint32_t w[32];
-                if (full) {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const float x0 = fmaf(__uint_as_float(s[64 * hf + 2 * i]), c, neg_m);
-                        const float x1 = fmaf(__uint_as_float(s[64 * hf + 2 * i + 1]), c, neg_m);
-                        float p0, p1;
-                        if ((i & 7) < POLY_PAIRS) {
-                            p0 = exp2_poly(x0);
-                            p1 = exp2_poly(x1);
-                        } else {
-                            p0 = ex2(x0);
-                            p1 = ex2(x1);
-                        }
-                        rs[i & 3] += p0 + p1;
-                        w[i] = pack_bf16x2(p0, p1);
+                for (int i = 0; i < 32; ++i) {
+                    float x0, x1;   // s * c - m for a key pair, one packed FMA
+                    up2(ffma2(pk2(__uint_as_float(s[64 * hf + 2 * i]), __uint_as_float(s[64 * hf + 2 * i + 1])),
+                              c2, nm2), x0, x1);
+                    float p0, p1;
+                    if (full && (i & 7) < POLY_PAIRS) {
+                        p0 = exp2_poly(x0);
+                        p1 = exp2_poly(x1);
+                    } else {
+                        p0 = ex2(x0);
+                        p1 = ex2(x1);
                     }
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const float p0 = ex2(fmaf(__uint_as_float(s[64 * hf + 2 * i]), c, neg_m));
-                        const float p1 = ex2(fmaf(__uint_as_float(s[64 * hf + 2 * i + 1]), c, neg_m));
-                        rs[i & 3] += p0 + p1;
-                        w[i] = pack_bf16x2(p0, p1);
-                    }
+                    if (i & 1) rs1 = fadd2(rs1, pk2(p0, p1));
+                    else rs0 = fadd2(rs0, pk2(p0, p1));
+                    w[i] = pack_bf16x2(p0, p1);
                 }
                 tmem_st32(s_addr + 32 * hf, w);
             }
-            l = l * alpha + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
+            float r0, r1, r2, r3;
+            up2(rs0, r0, r1);
+            up2(rs1, r2, r3);
+            l = l * alpha + ((r0 + r1) + (r2 + r3));
             tmem_st_wait();
             tc_fence_before();
             mbar_arrive(&p_ready[t]);

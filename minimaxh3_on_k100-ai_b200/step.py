@@ -68,6 +68,20 @@ class DiTStep:
         self.local, start, padded = local_rows(cfg.tokens, world, rank)
         self.start = start
         self.weights = [random_block_weights(bc, self.device, seed=seed + 1000 * i) for i in range(cfg.blocks)]
+        self.group = group
+        if world > 1:
+            # AdaLN projections stay column-parallel (as the reference keeps them,
+            # patches/InfiniLM.patch:1286-1292, 1740-1761): rank r holds output columns
+            # [r*n, (r+1)*n) of every block's projection and the rows are all-gathered
+            # once per step.  Each column's dot product is computed the same way on any
+            # rank, so the gathered modulation is bitwise the 1-GPU one.
+            rows = self.weights[0].w_adaln.shape[0]
+            if rows % world != 0 or (rows // world) % 32 != 0:
+                raise ValueError("AdaLN projection width must split into multiples of 32 columns per rank")
+            n = rows // world
+            for w in self.weights:
+                w.w_adaln = w.w_adaln[rank * n:(rank + 1) * n].contiguous()
+                w.b_adaln = w.b_adaln[rank * n:(rank + 1) * n].contiguous()
         self.time = random_time_embedder(bc.hidden, self.device, seed=seed + 7)
         # per-token tables of the local rows; padded rows reuse row 0 (:1706-1710)
         pos = joint_positions(cfg)
@@ -88,8 +102,20 @@ class DiTStep:
         self.graph, self.graph_out = None, None
 
     def modulations(self, timestep: torch.Tensor) -> list[torch.Tensor]:
+        """Every block's modulation rows [timesteps*modalities, 6*Hd], computed up
+        front (the reference's batched AdaLN)."""
         temb = time_embedding(timestep, self.time)
-        return [adaln_modulation(temb, w, self.cfg.block) for w in self.weights]
+        if self.world == 1:
+            return [adaln_modulation(temb, w, self.cfg.block) for w in self.weights]
+        import torch.distributed as dist
+        activated = torch.nn.functional.silu(temb).to(torch.bfloat16)
+        local = torch.stack([ops.linear(activated, w.w_adaln) + w.b_adaln for w in self.weights])  # [B, t, n]
+        gathered = torch.empty((self.world,) + tuple(local.shape), dtype=local.dtype, device=local.device)
+        dist.all_gather_into_tensor(gathered, local, group=self.group)
+        blocks, t, n = local.shape
+        full = gathered.permute(1, 2, 0, 3).reshape(blocks, t * self.world * n)   # rank-major columns
+        rows = t * self.cfg.block.modalities
+        return [full[i].view(rows, 6 * self.cfg.block.hidden) for i in range(blocks)]
 
     def forward(self, x: torch.Tensor, timestep: torch.Tensor | None = None) -> torch.Tensor:
         ts = self.timestep if timestep is None else timestep

@@ -3,17 +3,27 @@ all-to-all), after ``MiniMaxH3Attention`` in patches/InfiniLM.patch:895-1137.
 
 Rank r owns tokens [r*T, (r+1)*T) of the sequence (zero-padded to W*T rows,
 padding only after the real tokens, :1676-1716).  For attention each rank
-needs H/W heads over the whole sequence:
+needs its Hl = H/W heads over the whole sequence:
 
-  send block p   = heads [p*Hl, (p+1)*Hl) of my T tokens      (gather_sequence :895-910)
+  send block p   = heads p*Hl + off_g + j of my T tokens    (gather_sequence :895-910)
   recv block q   = rank q's tokens, so the token axis is global order
-  attention      on [W*T, Hl, D] queries, keys/values narrowed to the real length
-  return block q = my output rows for rank q's tokens;  back home, block q holds
-                   heads q*Hl + h of the local tokens           (scatter_sequence :1127-1137)
+  attention      on [W*T, Hs_g, D] queries, keys/values narrowed to the real length
+  return block q = my output rows for rank q's tokens; back home block q holds
+                   heads q*Hl + off_g + h of the local tokens  (:1006-1014)
 
-The q/k RMSNorm + RoPE kernel writes straight into the permuted view of the
-send buffer ([T, W, Hl, D] view of [W, T, Hl, D]), as the reference's
-h3_qk_norm_rope_ does (:1092-1103), so no separate pack pass is needed for q/k.
+Heads can be processed in groups (``pipelined_sequence_attention`` :1047-1125,
+``attend_exchanged_groups`` :960-1018): the QKV projection of group g+1 runs on
+the compute stream while group g's all-to-all runs on a side stream, and group
+g's output travels home while group g+1 attends.  The default is one group: on
+B200 the NCCL all-to-all kernels need SMs that the attention and GEMM kernels
+(one ~200 KB shared-memory CTA per SM) do not leave free, so the exchange does
+not overlap anyway, and whole-wave attention calls matter more (measured:
+8 GPUs 0.1204 s/step with two groups vs 0.1202 with one).  The QKV weight rows are
+regrouped once so each group's projection is one contiguous GEMM (like the
+reference's ``group_qkv_weight`` :1020-1045; same dot products, so the result is
+bitwise the ungrouped one).  The q/k RMSNorm + RoPE kernel writes straight into
+the permuted view of the send buffer ([T, W, Hs, D] view of [W, T, Hs, D]), so
+no separate pack pass is needed for q/k.
 
 The exchange logic is written against a small ``kernels`` interface so the same
 host code runs with the CUDA ops on NCCL and, in the CPU tests, with the oracle
@@ -21,6 +31,7 @@ on gloo ranks.
 """
 from __future__ import annotations
 
+import contextlib
 import math
 from dataclasses import dataclass
 from typing import Callable
@@ -31,8 +42,9 @@ import torch.distributed as dist
 
 @dataclass
 class Kernels:
-    """The three device ops the exchange needs.
-    qk_norm_rope(out, x, weight, cos, sin, eps); mha(out, q, k, v, scale); copy(dst, src)."""
+    """Device ops the exchange needs: linear(out, x, w), qk_norm_rope(out, x,
+    weight, cos, sin, eps), mha(out, q, k, v, scale), copy(dst, src)."""
+    linear: Callable
     qk_norm_rope: Callable
     mha: Callable
     copy: Callable = lambda dst, src: dst.copy_(src)
@@ -40,24 +52,7 @@ class Kernels:
 
 def cuda_kernels() -> Kernels:
     from . import ops
-    return Kernels(qk_norm_rope=ops.h3_qk_norm_rope_, mha=ops.mha_)
-
-
-@dataclass
-class ExchangeBuffers:
-    send: list          # 3 x [W, T, Hl, D]  (q, k, v)
-    recv: list          # 3 x [W, T, Hl, D]
-    attn: torch.Tensor  # [W*T, Hl, D]
-    back: torch.Tensor  # [W, T, Hl, D]
-
-    @staticmethod
-    def allocate(world, tokens, heads_local, head_dim, device, dtype=torch.bfloat16):
-        e = dict(device=device, dtype=dtype)
-        return ExchangeBuffers(
-            send=[torch.empty(world, tokens, heads_local, head_dim, **e) for _ in range(3)],
-            recv=[torch.empty(world, tokens, heads_local, head_dim, **e) for _ in range(3)],
-            attn=torch.empty(world * tokens, heads_local, head_dim, **e),
-            back=torch.empty(world, tokens, heads_local, head_dim, **e))
+    return Kernels(linear=ops.linear_, qk_norm_rope=ops.h3_qk_norm_rope_, mha=ops.mha_)
 
 
 def local_rows(total_tokens: int, world: int, rank: int) -> tuple[int, int, int]:
@@ -66,9 +61,23 @@ def local_rows(total_tokens: int, world: int, rank: int) -> tuple[int, int, int]
     return t, rank * t, t * world
 
 
+def head_groups(heads_local: int, groups: int) -> list[int]:
+    """Split Hl heads into `groups` nearly equal groups (uneven allowed, larger
+    first), as the reference's sp_head_groups (:452-479) does for H3_SP_GROUPS.
+    Even group sizes are preferred: the attention kernel runs two 128-row query
+    tiles per CTA, so an even head count keeps each call's CTAs a whole number of
+    waves when the sequence is a multiple of 2*128*148/2 rows."""
+    groups = max(1, min(groups, heads_local))
+    if heads_local % 2 == 0 and heads_local // 2 >= groups:
+        base, extra = divmod(heads_local // 2, groups)
+        return [2 * (base + (1 if g < extra else 0)) for g in range(groups)]
+    base, extra = divmod(heads_local, groups)
+    return [base + (1 if g < extra else 0) for g in range(groups)]
+
+
 class SequenceParallel:
     def __init__(self, world: int, rank: int, group, valid_tokens: int, local_tokens: int, heads: int,
-                 head_dim: int, device, kernels: Kernels | None = None):
+                 head_dim: int, device, kernels: Kernels | None = None, groups: int = 1):
         if heads % world != 0:
             # same constraint as the reference (patches/InfiniLM.patch:717-721)
             raise ValueError("heads must be divisible by the sequence-parallel size")
@@ -80,33 +89,96 @@ class SequenceParallel:
         self.heads, self.head_dim = heads, head_dim
         self.heads_local = heads // world
         self.kernels = kernels or cuda_kernels()
-        self.bufs = ExchangeBuffers.allocate(world, local_tokens, self.heads_local, head_dim, device)
+        self.group_heads = head_groups(self.heads_local, groups)
+        self.device = torch.device(device)
+        e = dict(device=device, dtype=torch.bfloat16)
+        w, t, d = world, local_tokens, head_dim
+        self.send = [[torch.empty(w, t, hs, d, **e) for _ in range(3)] for hs in self.group_heads]
+        self.recv = [[torch.empty(w, t, hs, d, **e) for _ in range(3)] for hs in self.group_heads]
+        self.attn = [torch.empty(w * t, hs, d, **e) for hs in self.group_heads]
+        self.back = [torch.empty(w, t, hs, d, **e) for hs in self.group_heads]
+        self.qkv = torch.empty(t * 3 * w * max(self.group_heads) * d, **e)
+        self.out = torch.empty(t, w, self.heads_local, d, **e)
+        cuda = self.device.type == "cuda"
+        self.side = torch.cuda.Stream(self.device) if cuda else None
+        self._weights = {}
+
+    # -- weight layout --------------------------------------------------------
+    def group_weights(self, w_qkv: torch.Tensor) -> list[torch.Tensor]:
+        """Rows [q|k|v][head p*Hl + j][D] -> per group g one block of rows
+        [q|k|v][p][j in g][D] (computed once per weight tensor)."""
+        if len(self.group_heads) == 1:
+            return [w_qkv]          # one group: the regrouped order is the original order
+        key = w_qkv.data_ptr()
+        if key not in self._weights:
+            w, hl, d = self.world, self.heads_local, self.head_dim
+            by_head = w_qkv.view(3, w, hl, d, w_qkv.shape[1])
+            out, off = [], 0
+            for hs in self.group_heads:
+                out.append(by_head[:, :, off:off + hs].reshape(3 * w * hs * d, w_qkv.shape[1]).contiguous())
+                off += hs
+            self._weights[key] = out
+        return self._weights[key]
+
+    # -- streams ----------------------------------------------------------------
+    def _on_side(self):
+        return torch.cuda.stream(self.side) if self.side is not None else contextlib.nullcontext()
+
+    def _side_waits_compute(self):
+        if self.side is not None:
+            self.side.wait_stream(torch.cuda.current_stream(self.device))
+
+    def _event_on_side(self):
+        if self.side is None:
+            return None
+        ev = torch.cuda.Event()
+        ev.record(self.side)
+        return ev
 
     def _all_to_all(self, outs, ins):
         for o, i in zip(outs, ins):
             dist.all_to_all_single(o, i, group=self.group)
 
-    def attention_from_qkv(self, qkv: torch.Tensor, norm_q, norm_k, cos, sin, qk_eps: float) -> torch.Tensor:
-        """qkv [T, 3*H*D] (rows [q|k|v] head-major) of this rank's tokens ->
-        attention output [T, H*D] of the same tokens (all heads)."""
-        t, w, hl, d = self.tokens, self.world, self.heads_local, self.head_dim
+    # -- the exchange -----------------------------------------------------------
+    def attention(self, normalized: torch.Tensor, w_qkv: torch.Tensor, norm_q, norm_k, cos, sin,
+                  qk_eps: float) -> torch.Tensor:
+        """normalized [T, Hd] tokens of this rank -> attention output [T, H*D] of
+        the same tokens (all heads, head-major), before the output projection."""
         k = self.kernels
-        b = self.bufs
-        parts = qkv.view(t, 3, w, hl, d)
-        # tokens -> heads: q/k normalised + rotated straight into the send layout
-        k.qk_norm_rope(b.send[0].permute(1, 0, 2, 3), parts[:, 0], norm_q, cos, sin, qk_eps)
-        k.qk_norm_rope(b.send[1].permute(1, 0, 2, 3), parts[:, 1], norm_k, cos, sin, qk_eps)
-        k.copy(b.send[2].permute(1, 0, 2, 3), parts[:, 2])
-        self._all_to_all(b.recv, b.send)
-        q = b.recv[0].view(1, w * t, hl, d)
-        kk = b.recv[1].view(1, w * t, hl, d)[:, :self.valid]
-        v = b.recv[2].view(1, w * t, hl, d)[:, :self.valid]
-        k.mha(b.attn.unsqueeze(0), q, kk, v, 1.0 / math.sqrt(d))
-        # heads -> tokens
-        self._all_to_all([b.back], [b.attn.view(w, t, hl, d)])
-        return b.back.permute(1, 0, 2, 3).reshape(t, w * hl * d)
-
-    def attention(self, ws, weights, cos, sin, cfg) -> torch.Tensor:
-        from . import ops
-        ops.linear_(ws.qkv, ws.normalized, weights.w_qkv)
-        return self.attention_from_qkv(ws.qkv, weights.norm_q, weights.norm_k, cos, sin, cfg.qk_eps)
+        w, t, d, hl = self.world, self.tokens, self.head_dim, self.heads_local
+        compute = torch.cuda.current_stream(self.device) if self.side is not None else None
+        weights = self.group_weights(w_qkv)
+        arrived = []
+        # tokens -> heads, group by group: project, normalise/rotate into the send
+        # layout, exchange on the side stream while the next group projects
+        for g, hs in enumerate(self.group_heads):
+            qkv = self.qkv[:t * 3 * w * hs * d].view(t, 3 * w * hs * d)
+            k.linear(qkv, normalized, weights[g])
+            parts = qkv.view(t, 3, w, hs, d)
+            send = self.send[g]
+            k.qk_norm_rope(send[0].permute(1, 0, 2, 3), parts[:, 0], norm_q, cos, sin, qk_eps)
+            k.qk_norm_rope(send[1].permute(1, 0, 2, 3), parts[:, 1], norm_k, cos, sin, qk_eps)
+            k.copy(send[2].permute(1, 0, 2, 3), parts[:, 2])
+            self._side_waits_compute()
+            with self._on_side():
+                self._all_to_all(self.recv[g], send)
+            arrived.append(self._event_on_side())
+        # attention per group; each group's output goes home while the next attends
+        off = 0
+        for g, hs in enumerate(self.group_heads):
+            if arrived[g] is not None:
+                compute.wait_event(arrived[g])
+            recv = self.recv[g]
+            q = recv[0].view(1, w * t, hs, d)
+            kk = recv[1].view(1, w * t, hs, d)[:, :self.valid]
+            v = recv[2].view(1, w * t, hs, d)[:, :self.valid]
+            k.mha(self.attn[g].unsqueeze(0), q, kk, v, 1.0 / math.sqrt(d))
+            self._side_waits_compute()
+            with self._on_side():
+                self._all_to_all([self.back[g]], [self.attn[g].view(w, t, hs, d)])
+        if self.side is not None:
+            compute.wait_stream(self.side)
+        for g, hs in enumerate(self.group_heads):
+            k.copy(self.out[:, :, off:off + hs], self.back[g].permute(1, 0, 2, 3))
+            off += hs
+        return self.out.view(t, w * hl * d)

@@ -29,23 +29,25 @@ def _free_port():
 
 def _inputs():
     torch.manual_seed(0)
-    qkv = torch.randn(SEQ, 3 * HEADS * D).bfloat16()
+    x = torch.randn(SEQ, HEADS * D).bfloat16()
+    w_qkv = (torch.randn(3 * HEADS * D, HEADS * D) * 0.05).bfloat16()
     wq = (torch.randn(D) * 0.1 + 1).bfloat16()
     wk = (torch.randn(D) * 0.1 + 1).bfloat16()
     table = O.rotary_cache(O.grid_positions(1, 3, 3))
-    return qkv, wq, wk, table[:, :48], table[:, 48:]
+    return x, w_qkv, wq, wk, table[:, :48], table[:, 48:]
 
 
 def _oracle_kernels():
     import h3b200.ulysses as U
     return U.Kernels(
+        linear=lambda out, x, w: out.copy_(O.linear(x, w)),
         qk_norm_rope=lambda out, x, w, cos, sin, eps: out.copy_(O.qk_norm_rope(x, w, cos, sin, eps)),
         mha=lambda out, q, k, v, scale: out.copy_(O.attention_fp32(q, k, v, scale).bfloat16()))
 
 
 def _single_rank_reference():
-    qkv, wq, wk, cos, sin = _inputs()
-    parts = qkv.view(SEQ, 3, HEADS, D)
+    x, w_qkv, wq, wk, cos, sin = _inputs()
+    parts = O.linear(x, w_qkv).view(SEQ, 3, HEADS, D)
     q = O.qk_norm_rope(parts[:, 0], wq, cos, sin, 1e-6)
     k = O.qk_norm_rope(parts[:, 1], wk, cos, sin, 1e-6)
     v = parts[:, 2]
@@ -59,15 +61,16 @@ def _worker(rank, port, result_path):
     dist.init_process_group("gloo", rank=rank, world_size=WORLD)
     import h3b200.ulysses as U
     t, start, padded = U.local_rows(SEQ, WORLD, rank)
-    qkv, wq, wk, cos, sin = _inputs()
-    pad = torch.zeros(padded - SEQ, qkv.shape[1], dtype=qkv.dtype)
-    qkv_p = torch.cat([qkv, pad])
+    x, w_qkv, wq, wk, cos, sin = _inputs()
+    pad = torch.zeros(padded - SEQ, x.shape[1], dtype=x.dtype)
+    x_p = torch.cat([x, pad])
     cos_p = torch.cat([cos, cos[:1].expand(padded - SEQ, -1)])     # padded rows reuse row 0
     sin_p = torch.cat([sin, sin[:1].expand(padded - SEQ, -1)])
     rows = slice(start, start + t)
-    sp = U.SequenceParallel(WORLD, rank, None, SEQ, t, HEADS, D, "cpu", kernels=_oracle_kernels())
-    out = sp.attention_from_qkv(qkv_p[rows].contiguous(), wq, wk, cos_p[rows], sin_p[rows], 1e-6)
-    torch.save({"out": out.clone(), "recv": [r.clone() for r in sp.bufs.recv]}, f"{result_path}.{rank}")
+    sp = U.SequenceParallel(WORLD, rank, None, SEQ, t, HEADS, D, "cpu", kernels=_oracle_kernels(), groups=2)
+    out = sp.attention(x_p[rows].contiguous(), w_qkv, wq, wk, cos_p[rows], sin_p[rows], 1e-6)
+    torch.save({"out": out.clone(), "groups": sp.group_heads,
+                "recv": [[r.clone() for r in grp] for grp in sp.recv]}, f"{result_path}.{rank}")
     dist.barrier()
     dist.destroy_process_group()
 
@@ -83,11 +86,15 @@ def test_ulysses_world2_matches_single_rank(tmp_path):
     for rank in range(WORLD):
         res = torch.load(f"{path}.{rank}")
         outs.append(res["out"])
-        # received blocks = this rank's heads over the global token order (bit-exact layout)
-        heads = slice(rank * hl, (rank + 1) * hl)
-        for got, full in zip(res["recv"], (q, k, v)):
-            glob = got.reshape(WORLD * t, hl, D)[:SEQ]
-            assert torch.equal(glob, full[:, heads])
+        # received blocks = this rank's heads of each group over the global token
+        # order (bit-exact integer layout)
+        off = 0
+        for hs, grp in zip(res["groups"], res["recv"]):
+            heads = slice(rank * hl + off, rank * hl + off + hs)
+            for got, full in zip(grp, (q, k, v)):
+                glob = got.reshape(WORLD * t, hs, D)[:SEQ]
+                assert torch.equal(glob, full[:, heads])
+            off += hs
     gathered = torch.cat(outs)[:SEQ]
     assert O.max_abs_rel(gathered, ref) <= 1e-2
 
@@ -104,11 +111,11 @@ def _dropout_worker(rank, port, result_path):
         dist.destroy_process_group()
         return
     t, start, padded = U.local_rows(SEQ, WORLD, rank)
-    qkv, wq, wk, cos, sin = _inputs()
+    x, w_qkv, wq, wk, cos, sin = _inputs()
     sp = U.SequenceParallel(WORLD, rank, None, SEQ, t, HEADS, D, "cpu", kernels=_oracle_kernels())
     outcome = "no error"
     try:
-        sp.attention_from_qkv(qkv[:t].contiguous(), wq, wk, cos[:t], sin[:t], 1e-6)
+        sp.attention(x[:t].contiguous(), w_qkv, wq, wk, cos[:t], sin[:t], 1e-6)
     except Exception as exc:  # noqa: BLE001 - any collective error is the expected outcome
         outcome = f"error: {type(exc).__name__}"
     with open(result_path, "w") as f:
