@@ -550,12 +550,39 @@ def run_pointwise(args):
     launches = _lib.CALLS["n"] - c0
     mean = statistics.mean(v["GB/s"] for v in res.values())
     top = max(res, key=lambda n: res[n]["us"])
+
+    # the same kernels at the step's shapes (18944 tokens, hidden 5120, FFN 13824,
+    # 40 heads): per-launch fixed costs matter less there (informative)
+    S2, C2, F2, H2 = 18944, 5120, 13824, 40
+    big = {}
+    torch.cuda.empty_cache()
+    xq, xo = r(S2, H2, D), torch.empty(S2, H2, D, dtype=torch.bfloat16, device=device)
+    tb = ops.h3_rope_cache(O.grid_positions(37, 16, 32).to(device), ops.rope_powers(device=device)[:16].contiguous())
+    xs, ys = r(S2, C2), r(S2, C2)
+    o1, o2 = torch.empty_like(xs), torch.empty_like(xs)
+    sc2, sh2, g2, w2 = (r(C2) * 0.1).bfloat16(), (r(C2) * 0.1).bfloat16(), (r(C2) * 0.1).bfloat16(), r(C2)
+    ua, ub = r(S2, F2), r(S2, F2)
+    uo = torch.empty_like(ua)
+    cases = {
+        "qk_norm_rope": (2 * 2 * S2 * H2 * D + S2 * 96 * 2 // 1,
+                         lambda: ops.h3_qk_norm_rope_(xo.unsqueeze(1), xq.unsqueeze(1), qw, tb[:, :48], tb[:, 48:], 1e-6)),
+        "rms_modulate": (2 * 2 * S2 * C2, lambda: ops.h3_rms_modulate_(o1, xs, w2, sc2, sh2, 1e-6)),
+        "swiglu": (3 * 2 * S2 * F2, lambda: ops.h3_swiglu_(uo, ua, ub)),
+        "gated_residual": (3 * 2 * S2 * C2, lambda: ops.h3_gated_residual_(o1, xs, g2, ys)),
+        "gated_residual_rms_modulate": (4 * 2 * S2 * C2,
+                                        lambda: ops.h3_gated_residual_rms_modulate_(o1, o2, xs, g2, ys, w2, sc2, sh2,
+                                                                                    1e-6)),
+    }
+    for name, (nbytes, fn) in cases.items():
+        ms = _timed(fn, max(args.steps, 10), stream)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        big[name] = {"us": round(ms * 1e3, 1), "GB/s": round(gbs, 1), "frac": round(gbs / pk["hbm_gbs"], 3)}
     return {"metric": "pointwise GB/s (config 1 op set, mean over ops)", "value": round(mean, 1), "unit": "GB/s",
             "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "config1: q/k [8192,14,128] norm+RoPE, AdaLN [8192,1792], SwiGLU [8192,4864], "
                                    "gated residual [8192,1792]", "l2": "rotating input sets totalling > 3x L2, back-to-back launches (steady state)"},
-            "gpu_launches": launches, "ops": res,
+            "gpu_launches": launches, "ops": res, "ops_at_step_shapes": big,
             "roofline": {"kernel": top, "bound": "hbm", "achieved": res[top]["GB/s"], "peak": pk["hbm_gbs"],
                          "unit": "GB/s", "frac": res[top]["frac"], "peak_source": f"{kind} hbm_gbs",
                          "traffic": _ncu_traffic(top)}}

@@ -60,7 +60,10 @@ struct EwArgs {
 };
 
 enum { EW_GATED_RESIDUAL = 0, EW_SWIGLU = 1 };
-constexpr int EW_THREADS = 256, EW_VPT = 2;   // vectors of 8 per thread
+#ifndef H3_EW_VPT
+#define H3_EW_VPT 4
+#endif
+constexpr int EW_THREADS = 256, EW_VPT = H3_EW_VPT;   // vectors of 8 per thread
 
 // 8 elements (one 16-byte vector) of either op
 template <int OP>
@@ -81,30 +84,35 @@ __device__ __forceinline__ uint4 ew_apply8(uint4 a, uint4 b, uint4 c) {
     return o;
 }
 
+// Flat index over the rows x vectors of the tensor (row = v / nvec by an
+// invariant-integer division), EW_VPT vectors per thread with all loads issued
+// before any arithmetic; narrow rows no longer leave most of a CTA idle.
 template <int OP, bool VEC>
-__global__ void __launch_bounds__(EW_THREADS) ew_kernel(EwArgs args) {
+__global__ void __launch_bounds__(EW_THREADS) ew_kernel(EwArgs args, FastDiv div_nvec, uint32_t total) {
     const int64_t nvec = (args.C + 7) >> 3;
-    for (int64_t row = blockIdx.y; row < args.rows; row += gridDim.y) {
-        const __nv_bfloat16 *pa = args.a.p + row_offset(args.a.s0, args.a.s1, row, args.n1);
-        const __nv_bfloat16 *pb = args.b.p + row_offset(args.b.s0, args.b.s1, row, args.n1);
-        const __nv_bfloat16 *pc = args.c.p + row_offset(args.c.s0, args.c.s1, row, args.n1);
-        __nv_bfloat16 *po = args.o.p + row_offset(args.o.s0, args.o.s1, row, args.n1);
-        uint4 va[EW_VPT], vb[EW_VPT], vc[EW_VPT];
+    uint4 va[EW_VPT], vb[EW_VPT], vc[EW_VPT];
+    uint32_t rows[EW_VPT], cols[EW_VPT];
+    const uint32_t base = blockIdx.x * (uint32_t)(EW_THREADS * EW_VPT) + threadIdx.x;
 #pragma unroll
-        for (int k = 0; k < EW_VPT; ++k) {
-            const int64_t vi = (int64_t)blockIdx.x * (EW_THREADS * EW_VPT) + k * EW_THREADS + threadIdx.x;
-            vc[k] = make_uint4(0, 0, 0, 0);
-            if (vi < nvec) {
-                va[k] = load8p<VEC>(pa, args.a.sc, vi * 8, args.C);
-                vb[k] = load8p<VEC>(pb, args.b.sc, vi * 8, args.C);
-                if (OP == EW_GATED_RESIDUAL) vc[k] = load8p<VEC>(pc, args.c.sc, vi * 8, args.C);
-            }
+    for (int k = 0; k < EW_VPT; ++k) {
+        const uint32_t v = base + k * EW_THREADS;
+        const uint32_t row = div_nvec.div(v);
+        rows[k] = row;
+        cols[k] = v - row * (uint32_t)nvec;
+        vc[k] = make_uint4(0, 0, 0, 0);
+        if (v < total) {
+            const int64_t col = (int64_t)cols[k] * 8;
+            va[k] = load8p<VEC>(args.a.p + row_offset(args.a.s0, args.a.s1, row, args.n1), args.a.sc, col, args.C);
+            vb[k] = load8p<VEC>(args.b.p + row_offset(args.b.s0, args.b.s1, row, args.n1), args.b.sc, col, args.C);
+            if (OP == EW_GATED_RESIDUAL)
+                vc[k] = load8p<VEC>(args.c.p + row_offset(args.c.s0, args.c.s1, row, args.n1), args.c.sc, col, args.C);
         }
+    }
 #pragma unroll
-        for (int k = 0; k < EW_VPT; ++k) {
-            const int64_t vi = (int64_t)blockIdx.x * (EW_THREADS * EW_VPT) + k * EW_THREADS + threadIdx.x;
-            if (vi < nvec) store8p<VEC>(po, args.o.sc, vi * 8, args.C, ew_apply8<OP>(va[k], vb[k], vc[k]));
-        }
+    for (int k = 0; k < EW_VPT; ++k) {
+        if (base + k * EW_THREADS < total)
+            store8p<VEC>(args.o.p + row_offset(args.o.s0, args.o.s1, rows[k], args.n1), args.o.sc,
+                         (int64_t)cols[k] * 8, args.C, ew_apply8<OP>(va[k], vb[k], vc[k]));
     }
 }
 
@@ -124,16 +132,13 @@ struct RowArgs {
 
 constexpr int ROW_WARPS = 4;            // rows per CTA (one warp each)
 
+// Phase 1 of a row: its input vectors into registers (for the fused residual
+// op, the residual itself, which is also written out).
 template <int MODE, bool VEC, int VPT>
-__global__ void __launch_bounds__(ROW_WARPS * 32) row_kernel(RowArgs args) {
-    const int lane = threadIdx.x & 31;
-    const int64_t row = (int64_t)blockIdx.x * ROW_WARPS + (threadIdx.x >> 5);
-    if (row >= args.rows) return;  // whole warp leaves together
+__device__ __forceinline__ void row_load(const RowArgs &args, int64_t row, int lane, uint4 (&v)[VPT]) {
     const int64_t C = args.C;
     const int64_t nvec = (C + 7) >> 3;
     const __nv_bfloat16 *xrow = args.x.p + row_offset(args.x.s0, args.x.s1, row, args.n1);
-
-    uint4 v[VPT];
     if (MODE == ROW_RES_RMS_MOD) {
         // residual = bf16(x + bf16(gate * y)), written out and normalised
         const __nv_bfloat16 *grow = args.gate.p + row_offset(args.gate.s0, args.gate.s1, row, args.n1);
@@ -160,6 +165,13 @@ __global__ void __launch_bounds__(ROW_WARPS * 32) row_kernel(RowArgs args) {
         }
     }
 
+}
+
+// Phase 2: statistics, normalise, weight, modulate, store.
+template <int MODE, bool VEC, int VPT>
+__device__ __forceinline__ void row_finish(const RowArgs &args, int64_t row, int lane, const uint4 (&v)[VPT]) {
+    const int64_t C = args.C;
+    const int64_t nvec = (C + 7) >> 3;
     // ---- statistics (padding lanes hold zeros) ----
     float r = 0.f, shift_ln = 0.f;
     if (MODE == ROW_LN_MOD) {
@@ -250,6 +262,22 @@ __global__ void __launch_bounds__(ROW_WARPS * 32) row_kernel(RowArgs args) {
     }
 }
 
+// One warp per row, RPW rows per warp with every row's loads issued before the
+// first row's arithmetic (more bytes in flight for narrow rows).
+template <int MODE, bool VEC, int VPT, int RPW>
+__global__ void __launch_bounds__(ROW_WARPS * 32) row_kernel(RowArgs args) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row0 = ((int64_t)blockIdx.x * ROW_WARPS + (threadIdx.x >> 5)) * RPW;
+    if (row0 >= args.rows) return;  // whole warp leaves together
+    uint4 v[RPW][VPT];
+#pragma unroll
+    for (int u = 0; u < RPW; ++u)
+        if (row0 + u < args.rows) row_load<MODE, VEC, VPT>(args, row0 + u, lane, v[u]);
+#pragma unroll
+    for (int u = 0; u < RPW; ++u)
+        if (row0 + u < args.rows) row_finish<MODE, VEC, VPT>(args, row0 + u, lane, v[u]);
+}
+
 // ===========================================================================
 // per-head q/k RMSNorm + RoPE: a half-warp per 128-wide head row
 // ===========================================================================
@@ -268,14 +296,20 @@ struct HeadArgs {
     float eps;
 };
 
+#ifndef H3_HEAD_ROWS
+#define H3_HEAD_ROWS 4
+#endif
+#ifndef H3_HEAD_MINB
+#define H3_HEAD_MINB 1
+#endif
 constexpr int HEAD_THREADS = 128;                                      // 8 half-warps
-constexpr int HEAD_ROWS_PER_HW = 4;                                    // rows in flight per half-warp
+constexpr int HEAD_ROWS_PER_HW = H3_HEAD_ROWS;                         // rows in flight per half-warp
 constexpr int HEAD_ROWS_PER_CTA = (HEAD_THREADS / 16) * HEAD_ROWS_PER_HW;
 
 // Flat head rows r = (t * P + p) * Hs + h; a CTA takes HEAD_ROWS_PER_CTA
 // consecutive rows, each half-warp HEAD_ROWS_PER_HW of them (loads first).
 template <bool NORM, bool VEC>
-__global__ void __launch_bounds__(HEAD_THREADS) head_kernel(HeadArgs a) {
+__global__ void __launch_bounds__(HEAD_THREADS, H3_HEAD_MINB) head_kernel(HeadArgs a) {
     const int lane = threadIdx.x & 31;
     const int hl = lane & 15;                    // lane within the half-warp: elements [8hl, 8hl+8)
     const int hw_base = lane & 16;
@@ -451,10 +485,12 @@ static int launch_ew(const h3_tensor *o, const h3_tensor *a, const h3_tensor *b,
     const bool vec = rows_vectorizable(o, 8) && rows_vectorizable(a, 8) && rows_vectorizable(b, 8) &&
                      (!c || rows_vectorizable(c, 8));
     const int64_t nvec = (args.C + 7) / 8;
-    const dim3 grid((unsigned)((nvec + EW_THREADS * EW_VPT - 1) / (EW_THREADS * EW_VPT)),
-                    (unsigned)(args.rows < 65535 ? args.rows : 65535));
-    if (vec) ew_kernel<OP, true><<<grid, EW_THREADS, 0, stream>>>(args);
-    else ew_kernel<OP, false><<<grid, EW_THREADS, 0, stream>>>(args);
+    const int64_t total = args.rows * nvec;
+    if (total > 0x7fffffffLL) return H3_ERR_UNSUPPORTED;
+    const unsigned grid = (unsigned)((total + EW_THREADS * EW_VPT - 1) / (EW_THREADS * EW_VPT));
+    const FastDiv dn = FastDiv::make((uint32_t)nvec);
+    if (vec) ew_kernel<OP, true><<<grid, EW_THREADS, 0, stream>>>(args, dn, (uint32_t)total);
+    else ew_kernel<OP, false><<<grid, EW_THREADS, 0, stream>>>(args, dn, (uint32_t)total);
     return launch_status();
 }
 
@@ -463,21 +499,20 @@ static int launch_row(RowArgs &args, bool vec, cudaStream_t stream) {
     if (args.rows == 0 || args.C == 0) return H3_OK;
     const int64_t nvec = (args.C + 7) / 8;
     const int vpt = (int)((nvec + 31) / 32);
-    const int64_t blocks = (args.rows + ROW_WARPS - 1) / ROW_WARPS;
-    if (blocks > 0x7fffffffLL) return H3_ERR_UNSUPPORTED;
-    const dim3 grid((unsigned)blocks);
-    // vectorised path: row widths up to 8192 in steps of 4 vectors per lane (extra
-    // iterations are masked); strided path: coarser steps (rarely used, same bits)
-#define H3_ROW_VEC(V)                                                                   \
-    if (vec && vpt <= V) {                                                              \
-        row_kernel<MODE, true, V><<<grid, ROW_WARPS * 32, 0, stream>>>(args);           \
-        return launch_status();                                                         \
+    // rows per warp follow the instantiated width bucket: 2 for buckets <= 8 vectors
+    // per lane, else 1; the grid is sized from the same constant
+#define H3_ROW_LAUNCH(VEC_, V)                                                              \
+    {                                                                                       \
+        constexpr int R = (V) <= 8 ? 2 : 1;                                                 \
+        const int64_t blocks = (args.rows + ROW_WARPS * R - 1) / (ROW_WARPS * R);           \
+        if (blocks > 0x7fffffffLL) return H3_ERR_UNSUPPORTED;                               \
+        row_kernel<MODE, VEC_, V, R><<<(unsigned)blocks, ROW_WARPS * 32, 0, stream>>>(args); \
+        return launch_status();                                                             \
     }
-#define H3_ROW_STRIDED(V)                                                               \
-    if (!vec && vpt <= V) {                                                             \
-        row_kernel<MODE, false, V><<<grid, ROW_WARPS * 32, 0, stream>>>(args);          \
-        return launch_status();                                                         \
-    }
+#define H3_ROW_VEC(V) \
+    if (vec && vpt <= V) H3_ROW_LAUNCH(true, V)
+#define H3_ROW_STRIDED(V) \
+    if (!vec && vpt <= V) H3_ROW_LAUNCH(false, V)
     H3_ROW_VEC(1)
     H3_ROW_VEC(2)
     H3_ROW_VEC(4)
@@ -492,6 +527,7 @@ static int launch_row(RowArgs &args, bool vec, cudaStream_t stream) {
     H3_ROW_STRIDED(32)
 #undef H3_ROW_VEC
 #undef H3_ROW_STRIDED
+#undef H3_ROW_LAUNCH
     return H3_ERR_UNSUPPORTED;  // rows wider than 8192 elements
 }
 
