@@ -5,32 +5,42 @@
 //   logits = (Q K^T) * scale * log2(e)  (fp32),  online max,  P = exp2(logits - max),
 //   O = sum P_bf16 V / sum P  (fp32 accumulation), keys masked by K's length.
 //
-// One CTA owns two 128-row Q tiles of one (batch, head) and streams the K/V tiles
-// of 128 keys through a 5-slot TMA ring (no multicast).  Warp roles (384 threads):
-//   warp 0        TMA producer (one elected lane)
-//   warp 1        tcgen05.mma issuer (one lane) and TMEM owner
+// One CTA owns two 128-row Q tiles of one (batch, head) and streams K/V tiles of
+// 128 keys by TMA (no multicast).  Warp roles (384 threads):
+//   warp 0        TMA producer for Q and K (one lane)
+//   warp 1        tcgen05.mma issuer for S = Q K^T (one lane) and TMEM owner
+//   warp 2        tcgen05.mma issuer for O += P V (one lane)
+//   warp 3        TMA producer for V (one lane)
 //   warps 4..7    softmax + correction + epilogue for Q tile 0
 //   warps 8..11   softmax + correction + epilogue for Q tile 1
-// TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512), fp32,
-// one query row per TMEM lane.  The two tiles ping-pong: while one softmax
-// warpgroup exponentiates its S, the tensor core computes the other tile's S or
-// P V.  P is written by the softmax threads as packed BF16 pairs back into the
-// first 64 columns of their own S region (tcgen05.st) and consumed from TMEM by
-// a TS MMA (A operand in tensor memory); V is the MN-major B operand in shared
-// memory.  Before S_t(j+1) overwrites that region the MMA warp waits for the
-// commit of P_t(j) V_j, which is already in flight behind the other tile's PV,
-// so the tensor pipe does not drain.  A configurable share of the exponentials
-// (H3_ATTN_POLY_PAIRS of every 8 key pairs of a full tile) can be computed on the
-// FMA pipe with a Cody-Waite split 2^x = 2^round(x) * 2^f, f in [-1/2, 1/2], and
-// a degree-3 polynomial for 2^f fitted by Lawson's minimax iteration (max
-// relative error 7.5e-5, far below the BF16 rounding P receives); on B200 the
-// sweep 0/2/3/4/5 measured 1054/942/948/904/876 TFLOP/s at [1,40,18432,128],
-// so the default keeps every exponential on the MUFU ex2 unit (the softmax is
-// issue-bound, not MUFU-bound).  The running max is updated lazily (only when it grows by more than
-// 2^8 in the exp2 domain), so O is rescaled rarely; the normalisation uses the
-// same stale max in numerator and denominator, so the result is unchanged up to
-// fp32 rounding.  The epilogue divides by the row sum, rounds to BF16 and writes
-// through a swizzled shared tile with a TMA store (rows past Sq are clipped).
+// TMEM (512 columns, fp32, one query row per lane): S_0 [0,128) S_1 [128,256)
+// O_0 [256,384) O_1 [384,512).  The softmax warps write P_t(j) in BF16 to a
+// 128B-swizzled shared tile per Q tile (the layout TMA gives Q), and P V is a
+// shared x shared MMA with V as the MN-major B operand.  Shared memory: Q 64 KB,
+// P 64 KB, a two-slot K ring 64 KB, one V buffer 32 KB.  K_j is read early in
+// step j (by S_t(j)) and V_j late (by P_t(j) V_j); a 32 KB tile takes about 2000
+// cycles to arrive, so K keeps one tile in flight and V reloads within the step.
+//
+// With P outside tensor memory nothing ties S_t(j+1) to P_t(j) V_j: the softmax
+// warps release S_t as soon as their tcgen05.ld of it has completed, and the
+// tensor core computes S_t(j+1) while they exponentiate tile j.  The waits left
+// on a tile's path are the softmax itself and, before P_t(j+1) overwrites the P
+// tile (and before a rescale of O_t), the commit of P_t(j) V_j, which by then
+// has normally landed.  The two products have separate issuing threads (each
+// thread's commits track only its own MMAs), so one thread's barrier waits
+// overlap the other's issue; the tensor pipe's instruction queue is shallow.
+// Measured on B200 at [1,40,18432,128] this layout runs at ~1220 TFLOP/s against
+// ~1100 for P aliased into S in TMEM; 64-key tiles with double-buffered S (N=64
+// MMAs run at half rate), a shared P tile, alternating the two softmax groups'
+// exponentials, and moving exponentials to the FMA pipe were all slower.
+//
+// The running max is updated lazily (only when it grows by more than 2^8 in the
+// exp2 domain), so O is rescaled rarely; the normalisation uses the same stale
+// max in numerator and denominator, so the result is unchanged up to fp32
+// rounding.  H3_ATTN_POLY_PAIRS of every 8 key pairs of a full tile can be
+// exponentiated on the FMA pipe instead of the MUFU.  The epilogue divides by
+// the row sum, rounds to BF16 and writes through a swizzled shared tile with a
+// TMA store (rows past Sq are clipped).
 #include <math.h>
 #include <stdint.h>
 
@@ -46,23 +56,38 @@ constexpr int BM = 128;                       // query rows per tile
 constexpr int BN = 128;                       // keys per K/V tile
 constexpr int HD = 128;                       // head dim
 constexpr int NQ = 2;                         // Q tiles per CTA
-constexpr int STAGES = 5;                     // K/V ring slots
-constexpr int TILE = BM * HD * 2;             // 32 KB: one 128x128 BF16 tile
-constexpr int HALF = TILE / 2;                // 16 KB: 64 columns (one 128B swizzle span)
+#ifndef H3_ATTN_KSLOTS
+#define H3_ATTN_KSLOTS 2
+#endif
+#ifndef H3_ATTN_VSLOTS
+#define H3_ATTN_VSLOTS 1
+#endif
+constexpr int KSLOTS = H3_ATTN_KSLOTS;        // K ring slots
+constexpr int VSLOTS = H3_ATTN_VSLOTS;        // V ring slots
+#ifndef H3_ATTN_L2_AHEAD
+#define H3_ATTN_L2_AHEAD 4
+#endif
+constexpr int L2_AHEAD = H3_ATTN_L2_AHEAD;    // key tiles between an L2 prefetch and the load
+constexpr int TILE = 128 * 128 * 2;           // 32 KB: one 128x128 BF16 tile (Q, P, K or V)
+constexpr int HALF = TILE / 2;                // 16 KB: its 64-column (128B swizzle span) half
 constexpr int THREADS = 384;
 constexpr uint32_t TMEM_COLS = 512;
+constexpr int O_COL = NQ * BN;                // first O column
 constexpr float RESCALE_THRESHOLD = 8.0f;     // log2 domain
 
 #ifndef H3_ATTN_POLY_PAIRS
-#define H3_ATTN_POLY_PAIRS 0   // measured fastest on B200: the MUFU is not the limit here
+#define H3_ATTN_POLY_PAIRS 0   // measured fastest on B200 (the softmax warps are latency-bound)
 #endif
 constexpr int POLY_PAIRS = H3_ATTN_POLY_PAIRS; // of every 8 key pairs, exponentiated on the FMA pipe
 
 constexpr int OFF_Q = 0;
-constexpr int OFF_KV = OFF_Q + NQ * TILE;
-constexpr int OFF_BAR = OFF_KV + STAGES * TILE;
-constexpr int NUM_BARS = 1 + 2 * STAGES + 3 * NQ;
+constexpr int OFF_P = OFF_Q + NQ * TILE;
+constexpr int OFF_K = OFF_P + NQ * TILE;
+constexpr int OFF_V = OFF_K + KSLOTS * TILE;
+constexpr int OFF_BAR = OFF_V + VSLOTS * TILE;
+constexpr int NUM_BARS = 1 + 2 * KSLOTS + 2 * VSLOTS + 4 * NQ;
 constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 16 + 1024;  // + tmem slot, abort flag, alignment slack
+static_assert(SMEM_BYTES <= 232448, "shared memory over the sm_100 per-block limit");
 
 struct Params {
     int Sq, Sk, H, B;
@@ -70,24 +95,11 @@ struct Params {
     float scale_log2;
 };
 
+
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
-}
-
-// 2^x on the FMA pipe: x = n + f with n = round(x) (the 1.5*2^23 addition
-// leaves n in the low mantissa bits), 2^f by a degree-3 polynomial on
-// [-1/2, 1/2], then n is added to the exponent field.  x is clamped at -126 so
-// the exponent never wraps (the result is then a tiny non-negative number).
-__device__ __forceinline__ float exp2_poly(float x) {
-    x = fmaxf(x, -126.0f);
-    const float t = __fadd_rn(x, 12582912.0f);
-    const float f = __fsub_rn(x, __fsub_rn(t, 12582912.0f));
-    float p = fmaf(0.0551716685295105f, f, 0.2426111251115799f);
-    p = fmaf(p, f, 0.6932609677314758f);
-    p = fmaf(p, f, 0.9999280571937561f);
-    return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
 // Blackwell packed fp32 pairs (fma.rn.f32x2 / add.rn.f32x2) and the 3-input
@@ -116,6 +128,27 @@ __device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
     return d;
 }
 
+// 2^x for a pair of values on the FMA pipe (packed fp32x2): x = n + f with
+// n = round(x) (the 1.5*2^23 addition leaves n in the low mantissa bits), 2^f by
+// a degree-3 polynomial on [-1/2, 1/2] (Lawson minimax fit, max relative error
+// 7.5e-5), then n is added to the exponent field.  x is clamped at -126 so the
+// exponent never wraps (the result is then a tiny non-negative number).
+__device__ __forceinline__ void exp2_poly2(float x0, float x1, float &p0, float &p1) {
+    const uint64_t x = pk2(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));
+    const uint64_t t = fadd2(x, pk2(12582912.0f, 12582912.0f));
+    const uint64_t r = fadd2(t, pk2(-12582912.0f, -12582912.0f));  // round(x), exact
+    const uint64_t f = ffma2(r, pk2(-1.0f, -1.0f), x);               // x - round(x), exact
+    uint64_t q = ffma2(pk2(0.0551716685295105f, 0.0551716685295105f), f,
+                       pk2(0.2426111251115799f, 0.2426111251115799f));
+    q = ffma2(q, f, pk2(0.6932609677314758f, 0.6932609677314758f));
+    q = ffma2(q, f, pk2(0.9999280571937561f, 0.9999280571937561f));
+    float q0, q1, t0, t1;
+    up2(q, q0, q1);
+    up2(t, t0, t1);
+    p0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
+    p1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t *>(&v);
@@ -136,14 +169,19 @@ __global__ void __launch_bounds__(THREADS, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sQ = smem + OFF_Q;
-    uint8_t *sKV = smem + OFF_KV;
+    uint8_t *sP = smem + OFF_P;
+    uint8_t *sK = smem + OFF_K;
+    uint8_t *sV = smem + OFF_V;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
     uint64_t *q_full = bars;
-    uint64_t *kv_full = bars + 1;
-    uint64_t *kv_empty = kv_full + STAGES;
-    uint64_t *s_full = kv_empty + STAGES;
-    uint64_t *p_ready = s_full + NQ;
-    uint64_t *o_done = p_ready + NQ;
+    uint64_t *k_full = bars + 1;
+    uint64_t *k_empty = k_full + KSLOTS;
+    uint64_t *v_full = k_empty + KSLOTS;
+    uint64_t *v_empty = v_full + VSLOTS;
+    uint64_t *s_full = v_empty + VSLOTS;    // [t]: S_t(j) in TMEM
+    uint64_t *s_free = s_full + NQ;         // [t]: softmax t has read S_t(j)
+    uint64_t *p_ready = s_free + NQ;        // [t]: P_t(j) in shared memory, O_t rescaled
+    uint64_t *o_done = p_ready + NQ;        // [t]: P_t(j) V_j has landed in O_t
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + NUM_BARS);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
@@ -151,15 +189,21 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int lane = threadIdx.x & 31;
     const int h = blockIdx.y, b = blockIdx.z;
     const int q0 = blockIdx.x * (NQ * BM);
+    const int nkv = p.nkv;
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&kv_full[s], 1);
-            mbar_init(&kv_empty[s], 1);
+        for (int i = 0; i < KSLOTS; ++i) {
+            mbar_init(&k_full[i], 1);
+            mbar_init(&k_empty[i], 1);
+        }
+        for (int i = 0; i < VSLOTS; ++i) {
+            mbar_init(&v_full[i], 1);
+            mbar_init(&v_empty[i], 1);
         }
         for (int t = 0; t < NQ; ++t) {
             mbar_init(&s_full[t], 1);
+            mbar_init(&s_free[t], 128);
             mbar_init(&p_ready[t], 128);
             mbar_init(&o_done[t], 1);
         }
@@ -175,122 +219,131 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 0) {
-        // ------------------------------------------------------------ TMA producer
-        if (lane == 0) {
-            tma_prefetch_desc(&tq);
-            tma_prefetch_desc(&tk);
-            tma_prefetch_desc(&tv);
-            mbar_expect_tx(q_full, NQ * TILE);
-            for (int t = 0; t < NQ; ++t)
-                for (int hf = 0; hf < 2; ++hf)
-                    tma_load_4d(sQ + t * TILE + hf * HALF, &tq, q_full, hf * 64, q0 + t * BM, h, b);
-            for (int j = 0; j < p.nkv; ++j) {
-                bool ok = true;
-                for (int kv = 0; kv < 2 && ok; ++kv) {
-                    const int i = 2 * j + kv, slot = i % STAGES, use = i / STAGES;
-                    ok = mbar_wait(&kv_empty[slot], (use & 1) ^ 1, abort_flag);
-                    if (!ok) break;
-                    mbar_expect_tx(&kv_full[slot], TILE);
-                    const CUtensorMap *m = kv ? &tv : &tk;
+    if (warp < 4) {
+        if ((warp == 0 || warp == 3) && lane == 0) {
+            // -------------------------------------------------------- TMA producers
+            const bool kq = warp == 0;   // warp 0: Q and K; warp 3: V
+            if (kq) {
+                tma_prefetch_desc(&tq);
+                tma_prefetch_desc(&tk);
+                mbar_expect_tx(q_full, NQ * TILE);
+                for (int t = 0; t < NQ; ++t)
                     for (int hf = 0; hf < 2; ++hf)
-                        tma_load_4d(sKV + slot * TILE + hf * HALF, m, &kv_full[slot], hf * 64, j * BN, h, b);
-                }
-                if (!ok) break;
+                        tma_load_4d(sQ + t * TILE + hf * HALF, &tq, q_full, hf * 64, q0 + t * BM, h, b);
+            } else {
+                tma_prefetch_desc(&tv);
             }
-        }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
+            // use u of a slot waits for the release of use u - 1
+            auto load_tile = [&](const CUtensorMap *m, uint8_t *dst, uint64_t *full, uint64_t *empty, int use,
+                                 int row0) -> bool {
+                if (!mbar_wait(empty, (use & 1) ^ 1, abort_flag)) return false;
+                mbar_expect_tx(full, TILE);
+                for (int hf = 0; hf < 2; ++hf) tma_load_4d(dst + hf * HALF, m, full, hf * 64, row0, h, b);
+                return true;
+            };
+            // K/V tiles are requested L2_AHEAD key tiles before their load, so the load
+            // itself hits in L2 rather than waiting for HBM (or the other die)
+            auto prefetch = [&](int j) {
+                for (int hf = 0; hf < 2; ++hf) tma_prefetch_l2_4d(kq ? &tk : &tv, hf * 64, j * BN, h, b);
+            };
+            for (int j = 1; j < L2_AHEAD && j < nkv; ++j) prefetch(j);
+            bool ok = true;
+            for (int j = 0; j < nkv && ok; ++j) {
+                if (j + L2_AHEAD < nkv) prefetch(j + L2_AHEAD);
+                if (kq) {
+                    const int ks = j % KSLOTS;
+                    ok = load_tile(&tk, sK + ks * TILE, &k_full[ks], &k_empty[ks], j / KSLOTS, j * BN);
+                } else {
+                    const int vs = j % VSLOTS;
+                    ok = load_tile(&tv, sV + vs * TILE, &v_full[vs], &v_empty[vs], j / VSLOTS, j * BN);
+                }
+            }
+        } else if ((warp == 1 || warp == 2) && lane == 0) {
+            // -------------------------------------------------------- MMA issuers
             constexpr uint32_t ID_S = idesc_bf16_f32(BM, BN, false);  // Q (K-major) x K (K-major)
             constexpr uint32_t ID_PV = idesc_bf16_f32(BM, HD, true);  // P (K-major) x V (MN-major)
-            bool ok = mbar_wait(q_full, 0, abort_flag);
-            tc_fence_after();
-            const uint32_t q_base = smem_u32(sQ), kv_base = smem_u32(sKV);
-            // S_t(j) = Q_t K_j^T into TMEM columns [t*BN, t*BN+BN)
-            auto issue_s = [&](int t, uint32_t kaddr) {
-                const uint32_t qaddr = q_base + t * TILE;
+            const uint32_t q_base = smem_u32(sQ), p_base = smem_u32(sP), k_base = smem_u32(sK),
+                           v_base = smem_u32(sV);
+            // D[t] = A_t (128 x 128, K-major, 128B swizzle) x B (128 x 128)
+            auto issue = [&](uint32_t d, uint32_t a, uint32_t bsrc, bool pv, bool acc) {
 #pragma unroll
-                for (int kk = 0; kk < HD / 16; ++kk) {
-                    const uint32_t off = (kk >> 2) * HALF + (kk & 3) * 32;
-                    umma_ss(tmem + t * BN, smem_desc_sw128(qaddr + off, 16, 1024),
-                            smem_desc_sw128(kaddr + off, 16, 1024), ID_S, kk > 0);
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint32_t ka = (kk >> 2) * HALF + (kk & 3) * 32;
+                    const uint64_t bdesc = pv ? smem_desc_sw128(bsrc + kk * 2048, HALF, 1024)
+                                              : smem_desc_sw128(bsrc + ka, 16, 1024);
+                    umma_ss(d, smem_desc_sw128(a + ka, 16, 1024), bdesc, pv ? ID_PV : ID_S,
+                            (acc || kk > 0) ? 1u : 0u);
                 }
-                umma_commit(&s_full[t]);
             };
-            // prologue: S_0(0), S_1(0)
-            if (ok) ok = mbar_wait(&kv_full[0], 0, abort_flag);
-            if (ok) {
-                tc_fence_after();
-                for (int t = 0; t < NQ; ++t) issue_s(t, kv_base);
-                umma_commit(&kv_empty[0]);
-            }
-            // steady state, ping-pong order: PV_0(j), S_0(j+1), PV_1(j), S_1(j+1).  S_t(j+1)
-            // overwrites P_t(j) (aliased in TMEM), so it waits for the commit of PV_t(j);
-            // meanwhile the tensor pipe is busy with PV_t(j) itself, and softmax t can start
-            // on tile j+1 while the other warpgroup still works on tile j.
-            for (int j = 0; j < p.nkv && ok; ++j) {
-                const int iv = 2 * j + 1, sv = iv % STAGES;
-                const int ik = 2 * j + 2, sk = ik % STAGES;
-                const bool more = j + 1 < p.nkv;
-                ok = mbar_wait(&kv_full[sv], (iv / STAGES) & 1, abort_flag);
-                if (!ok) break;
-                const uint32_t vaddr = kv_base + sv * TILE;
-                const uint32_t kaddr = kv_base + sk * TILE;
-                for (int t = 0; t < NQ && ok; ++t) {
-                    ok = mbar_wait(&p_ready[t], j & 1, abort_flag);
-                    if (!ok) break;
-                    tc_fence_after();
-#pragma unroll
-                    for (int kk = 0; kk < BN / 16; ++kk)  // P: 16 keys = 8 packed columns per step
-                        umma_ts(tmem + 2 * BN + t * HD, tmem + t * BN + kk * 8,
-                                smem_desc_sw128(vaddr + kk * 2048, HALF, 1024), ID_PV, (j > 0 || kk > 0) ? 1u : 0u);
-                    umma_commit(&o_done[t]);
-                    if (more) {
-                        if (t == 0) ok = mbar_wait(&kv_full[sk], (ik / STAGES) & 1, abort_flag);
-                        if (ok) ok = mbar_wait(&o_done[t], j & 1, abort_flag);
+            bool ok = true;
+            if (warp == 1) {
+                // S_t(j) = Q_t K_j^T, issued as soon as softmax t has read S_t(j-1)
+                ok = mbar_wait(q_full, 0, abort_flag);
+                for (int j = 0; j < nkv && ok; ++j) {
+                    const int ks = j % KSLOTS;
+                    ok = mbar_wait(&k_full[ks], (j / KSLOTS) & 1, abort_flag);
+                    for (int t = 0; t < NQ && ok; ++t) {
+                        if (j > 0) ok = mbar_wait(&s_free[t], (j - 1) & 1, abort_flag);
                         if (!ok) break;
                         tc_fence_after();
-                        issue_s(t, kaddr);
+                        issue(tmem + t * BN, q_base + t * TILE, k_base + ks * TILE, false, false);
+                        umma_commit(&s_full[t]);
                     }
+                    if (!ok) break;
+                    umma_commit(&k_empty[ks]);
                 }
-                if (!ok) break;
-                umma_commit(&kv_empty[sv]);
-                if (more) umma_commit(&kv_empty[sk]);
+            } else {
+                // O_t += P_t(j) V_j once softmax t has written P_t(j)
+                for (int j = 0; j < nkv && ok; ++j) {
+                    const int vs = j % VSLOTS;
+                    ok = mbar_wait(&v_full[vs], (j / VSLOTS) & 1, abort_flag);
+                    for (int t = 0; t < NQ && ok; ++t) {
+                        ok = mbar_wait(&p_ready[t], j & 1, abort_flag);
+                        if (!ok) break;
+                        tc_fence_after();
+                        issue(tmem + O_COL + t * HD, p_base + t * TILE, v_base + vs * TILE, true, j > 0);
+                        umma_commit(&o_done[t]);
+                    }
+                    if (!ok) break;
+                    umma_commit(&v_empty[vs]);
+                }
             }
             if (!ok) drain_in_flight();
         }
-    } else if (warp >= 4) {
+    } else {
         // ------------------------------------------------------------ softmax / epilogue
         const int t = (warp - 4) >> 2;
         const int row = (warp & 3) * 32 + lane;
         const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
         const uint32_t s_addr = tmem + t * BN + lane_off;
-        const uint32_t o_addr = tmem + 2 * BN + t * HD + lane_off;
+        const uint32_t o_addr = tmem + O_COL + t * HD + lane_off;
+        const uint32_t p_tile = smem_u32(sP + t * TILE);
         const float c = p.scale_log2;
         float m = -INFINITY, l = 0.f;
         bool ok = true;
-        for (int j = 0; j < p.nkv; ++j) {
-            // s_full(j) implies P_t(j-1) V_{j-1} has landed: S_t(j) was issued after its commit
+        for (int j = 0; j < nkv; ++j) {
             ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, abort_flag));
             if (!ok) break;
             tc_fence_after();
-            uint32_t s[128];
+            uint32_t s[BN];
             tmem_ld32(s_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
             tmem_ld32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
             tmem_ld32(s_addr + 64, *reinterpret_cast<uint32_t(*)[32]>(&s[64]));
             tmem_ld32(s_addr + 96, *reinterpret_cast<uint32_t(*)[32]>(&s[96]));
             tmem_ld_wait();
+            // S_t(j) is in registers: the tensor core may overwrite it with S_t(j+1)
+            tc_fence_before();
+            mbar_arrive(&s_free[t]);
             const int valid = p.Sk - j * BN;
             const bool full = valid >= BN;
             if (!full) {
 #pragma unroll
-                for (int i = 0; i < 128; ++i)
+                for (int i = 0; i < BN; ++i)
                     if (i >= valid) s[i] = __float_as_uint(-INFINITY);
             }
             float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
-            for (int i = 0; i < 128; i += 8) {
+            for (int i = 0; i < BN; i += 8) {
                 mx0 = max3f(mx0, __uint_as_float(s[i]), __uint_as_float(s[i + 1]));
                 mx1 = max3f(mx1, __uint_as_float(s[i + 2]), __uint_as_float(s[i + 3]));
                 mx2 = max3f(mx2, __uint_as_float(s[i + 4]), __uint_as_float(s[i + 5]));
@@ -306,8 +359,38 @@ __global__ void __launch_bounds__(THREADS, 1)
                 m = mnew;
                 rescale = true;
             }
+            const float neg_m = -m;
+            const uint64_t c2 = pk2(c, c), nm2 = pk2(neg_m, neg_m);
+            uint64_t rs0 = pk2(0.f, 0.f), rs1 = pk2(0.f, 0.f);
+            uint32_t w[BN / 2];
+#pragma unroll
+            for (int i = 0; i < BN / 2; ++i) {
+                float x0, x1;   // s * c - m for a key pair, one packed FMA
+                up2(ffma2(pk2(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])), c2, nm2), x0, x1);
+                float p0, p1;
+                if (full && (i & 7) < POLY_PAIRS) {
+                    exp2_poly2(x0, x1, p0, p1);
+                } else {
+                    p0 = ex2(x0);
+                    p1 = ex2(x1);
+                }
+                if (i & 1) rs1 = fadd2(rs1, pk2(p0, p1));
+                else rs0 = fadd2(rs0, pk2(p0, p1));
+                w[i] = pack_bf16x2(p0, p1);
+            }
+            float r0, r1, r2, r3;
+            up2(rs0, r0, r1);
+            up2(rs1, r2, r3);
+            l = l * alpha + ((r0 + r1) + (r2 + r3));
+            // P_t(j-1) V_{j-1} must have read the P tile (and landed in O_t) before P_t(j)
+            // overwrites it or O_t is rescaled
+            if (j > 0) {
+                ok = __all_sync(0xffffffffu, mbar_wait(&o_done[t], (j - 1) & 1, abort_flag));
+                if (!ok) break;
+            }
             // tcgen05.ld/st are warp-collective: rescale the whole warp's rows if any needs it
             if (__any_sync(0xffffffffu, rescale)) {
+                tc_fence_after();
 #pragma unroll 1
                 for (int cc = 0; cc < 4; ++cc) {
                     uint32_t o[32];
@@ -317,42 +400,20 @@ __global__ void __launch_bounds__(THREADS, 1)
                     for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
                     tmem_st32(o_addr + cc * 32, o);
                 }
+                tmem_st_wait();
             }
-            const float neg_m = -m;
-            const uint64_t c2 = pk2(c, c), nm2 = pk2(neg_m, neg_m);
-            uint64_t rs0 = pk2(0.f, 0.f), rs1 = pk2(0.f, 0.f);
-            // P overwrites columns [0, 64) of this tile's S region (S is already in registers)
+            // P_t(j): this thread's row, keys [64 hf + 8 q, +8) in 16-byte chunk q of half hf
 #pragma unroll
-            for (int hf = 0; hf < 2; ++hf) {
-                uint32_t w[32];
+            for (int hf = 0; hf < 2; ++hf)
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    float x0, x1;   // s * c - m for a key pair, one packed FMA
-                    up2(ffma2(pk2(__uint_as_float(s[64 * hf + 2 * i]), __uint_as_float(s[64 * hf + 2 * i + 1])),
-                              c2, nm2), x0, x1);
-                    float p0, p1;
-                    if (full && (i & 7) < POLY_PAIRS) {
-                        p0 = exp2_poly(x0);
-                        p1 = exp2_poly(x1);
-                    } else {
-                        p0 = ex2(x0);
-                        p1 = ex2(x1);
-                    }
-                    if (i & 1) rs1 = fadd2(rs1, pk2(p0, p1));
-                    else rs0 = fadd2(rs0, pk2(p0, p1));
-                    w[i] = pack_bf16x2(p0, p1);
-                }
-                tmem_st32(s_addr + 32 * hf, w);
-            }
-            float r0, r1, r2, r3;
-            up2(rs0, r0, r1);
-            up2(rs1, r2, r3);
-            l = l * alpha + ((r0 + r1) + (r2 + r3));
-            tmem_st_wait();
+                for (int q = 0; q < 8; ++q)
+                    st_shared_v4(p_tile + hf * HALF + swz(row, q), w[32 * hf + 4 * q], w[32 * hf + 4 * q + 1],
+                                 w[32 * hf + 4 * q + 2], w[32 * hf + 4 * q + 3]);
+            fence_proxy_async_smem();
             tc_fence_before();
             mbar_arrive(&p_ready[t]);
         }
-        if (ok && p.nkv > 0) ok = mbar_wait(&o_done[t], (p.nkv - 1) & 1, abort_flag);
+        if (ok) ok = mbar_wait(&o_done[t], (nkv - 1) & 1, abort_flag);
         ok = __all_sync(0xffffffffu, ok);
         if (ok) {
             tc_fence_after();
@@ -402,15 +463,15 @@ using namespace h3;
 
 namespace {
 
-// [B, S, H, 128] BF16 view -> 4-D tensor map (D, S, H, B), box (64, 128, 1, 1)
-int attn_tmap(CUtensorMap *map, const h3_tensor *t) {
+// [B, S, H, 128] BF16 view -> 4-D tensor map (D, S, H, B), box (64, rows, 1, 1)
+int attn_tmap(CUtensorMap *map, const h3_tensor *t, unsigned rows) {
     const cuuint64_t dims[4] = {(cuuint64_t)t->shape[3], (cuuint64_t)t->shape[1], (cuuint64_t)t->shape[2],
                                 (cuuint64_t)t->shape[0]};
     // a size-1 batch dim may carry any stride; give TMA a legal one
     const int64_t sb = t->shape[0] == 1 ? t->strides[1] * t->shape[1] : t->strides[0];
     const int64_t sh = t->shape[2] == 1 ? 128 : t->strides[2];
     const cuuint64_t strides[3] = {(cuuint64_t)t->strides[1] * 2, (cuuint64_t)sh * 2, (cuuint64_t)sb * 2};
-    const cuuint32_t box[4] = {64, attn::BM, 1, 1};
+    const cuuint32_t box[4] = {64, rows, 1, 1};
     return make_tmap_bf16(map, t->data, 4, dims, strides, box);
 }
 
@@ -439,10 +500,10 @@ extern "C" int h3_mha(const h3_tensor *out, const h3_tensor *q, const h3_tensor 
     if (B == 0 || Sq == 0 || H == 0) return H3_OK;
     if (Sk == 0) return H3_ERR_BAD_SHAPE;
     CUtensorMap tq, tk, tv, to;
-    H3_CHECK(attn_tmap(&tq, q));
-    H3_CHECK(attn_tmap(&tk, k));
-    H3_CHECK(attn_tmap(&tv, v));
-    H3_CHECK(attn_tmap(&to, out));
+    H3_CHECK(attn_tmap(&tq, q, attn::BM));
+    H3_CHECK(attn_tmap(&tk, k, attn::BN));
+    H3_CHECK(attn_tmap(&tv, v, attn::BN));
+    H3_CHECK(attn_tmap(&to, out, attn::BM));
     attn::Params p;
     p.Sq = Sq;
     p.Sk = Sk;

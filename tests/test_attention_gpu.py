@@ -41,12 +41,27 @@ def _check(out, q, k, v, rows=None, max_err=None, mean_err=2e-4):
 
 
 @pytest.mark.parametrize("B,Sq,Sk,H", [(1, 128, 128, 1), (1, 200, 136, 3), (2, 333, 333, 2),
-                                       (1, 256, 1000, 4), (1, 1000, 777, 2), (1, 600, 129, 1)])
+                                       (1, 256, 1000, 4), (1, 1000, 777, 2), (1, 600, 129, 1),
+                                       (1, 130, 40, 2), (1, 64, 100, 1), (1, 300, 64, 1), (1, 257, 192, 3)])
 def test_small_shapes(h3, B, Sq, Sk, H):
     torch.manual_seed(B * 1000 + Sq + Sk + H)
     q = torch.randn(B, Sq, H, 128, dtype=torch.bfloat16, device=DEV)
     k = torch.randn(B, Sk, H, 128, dtype=torch.bfloat16, device=DEV)
     v = torch.randn(B, Sk, H, 128, dtype=torch.bfloat16, device=DEV)
+    out = h3.mha(q, k, v)
+    _check(out, q, k, v, mean_err=1e-3)
+
+
+def test_growing_logits_rescale(h3):
+    """Keys whose logits grow along the sequence: the running row max rises past
+    the lazy-rescale threshold many times, so O is rescaled between key tiles."""
+    torch.manual_seed(21)
+    Sq, Sk, H = 256, 1100, 2
+    q = torch.randn(1, Sq, H, 128, device=DEV).abs()
+    ramp = torch.linspace(0.0, 3.0, Sk, device=DEV).view(1, Sk, 1, 1)
+    k = (torch.rand(1, Sk, H, 128, device=DEV) * ramp).bfloat16()
+    q = q.bfloat16()
+    v = torch.randn(1, Sk, H, 128, dtype=torch.bfloat16, device=DEV)
     out = h3.mha(q, k, v)
     _check(out, q, k, v, mean_err=1e-3)
 
