@@ -21,6 +21,12 @@
  *   h3_timestep_embedding          InfiniCore.patch:223-252 (infiniopTimestepEmbedding C API)
  *   h3_linear*                     InfiniCore.patch:1231-1292 (linear.cc) + the fused
  *                                  epilogues of InfiniLM.patch:1172-1179, 1377-1394
+ *   h3_linear_f32                  linear_forward on the F32 modules (proj_in, audio_proj_in,
+ *                                  proj_out, audio_proj_out, time embedder),
+ *                                  InfiniLM.patch:1501-1517, 1662-1664, 1812-1814
+ *   h3_gather_rows                 gather_rows -> op::embedding, InfiniLM.patch:587-590
+ *   h3_index_copy_rows             op::index_copy of the packed sequence, InfiniLM.patch:1685-1690
+ *   h3_silu                        op::silu + cast_to, InfiniLM.patch:1267-1268, 1511, 1535
  */
 #ifndef H3_B200_H
 #define H3_B200_H
@@ -50,7 +56,8 @@ typedef enum h3_status {
     H3_ERR_UNSUPPORTED = 5,   /* valid request outside what this build supports  */
     H3_ERR_LAUNCH = 6,        /* the CUDA launch reported an error               */
     H3_ERR_DRIVER = 7,        /* a driver entry point could not be resolved      */
-    H3_ERR_TIMEOUT = 8        /* a bounded device-side wait gave up              */
+    H3_ERR_TIMEOUT = 8,       /* a bounded device-side wait gave up              */
+    H3_ERR_INDEX = 9          /* a row index was outside the indexed tensor      */
 } h3_status;
 
 /* A strided view.  strides are in ELEMENTS (not bytes); stride 0 broadcasts.
@@ -67,9 +74,10 @@ int h3_abi_version(void);
 const char *h3_status_string(int status);
 
 /* Synchronises the current device and reports (then clears) whether any bounded
- * device-side wait gave up since the last call: H3_ERR_TIMEOUT in that case,
- * H3_ERR_LAUNCH if the device reports an error, else H3_OK.  No reference
- * counterpart (the reference's waits are unbounded). */
+ * device-side wait gave up since the last call (H3_ERR_TIMEOUT), else whether a
+ * row gather/scatter met an index outside its table (H3_ERR_INDEX; that row was
+ * left untouched), H3_ERR_LAUNCH if the device reports an error, else H3_OK.
+ * No reference counterpart (the reference's waits are unbounded). */
 int h3_device_error(void);
 
 /* Failure-detection self test: launches one CTA that waits, with a limit of
@@ -161,6 +169,29 @@ int h3_linear_gated_residual(const h3_tensor *out, const h3_tensor *x, const h3_
 /* Reorder the [up; gate] rows of a gate_up weight [2F,K] into 128-row blocks
  * [up_0 | gate_0 | up_1 | gate_1 ...] consumed by h3_linear_swiglu. */
 int h3_pack_gate_up(const h3_tensor *dst, const h3_tensor *src, void *stream);
+
+/* ---------------- model wrapper ops (outside the block loop) ---------------- */
+
+/* y [M,N] = x [M,K] * w[N,K]^T (+ bias[N]); x BF16 or F32 (BF16 is widened
+ * exactly, as cast_to F32 does), w and bias F32, fp32 accumulation in k order;
+ * y F32, or BF16 rounded once from the fp32 result (cast_to after the F32
+ * linear).  bias may be NULL.  Rows contiguous (inner stride 1). */
+int h3_linear_f32(const h3_tensor *y, const h3_tensor *x, const h3_tensor *w, const h3_tensor *bias,
+                  void *stream);
+
+/* out [n,C] = table[indices[r], :]; table [T,C]; BF16 or F32; indices [n] I64.
+ * An index outside [0,T) leaves its row untouched; h3_device_error() then
+ * returns H3_ERR_INDEX. */
+int h3_gather_rows(const h3_tensor *out, const h3_tensor *table, const h3_tensor *indices, void *stream);
+
+/* out[indices[r], :] = src[r, :]; out [T,C], src [n,C]; BF16 or F32; indices
+ * [n] I64, distinct (as for index_copy, repeated indices race).  Out-of-range
+ * indices as for h3_gather_rows. */
+int h3_index_copy_rows(const h3_tensor *out, const h3_tensor *indices, const h3_tensor *src, void *stream);
+
+/* y = x / (1 + exp(-x)) computed in fp32 from x F32; y F32 or BF16 (rounded
+ * once).  Contiguous. */
+int h3_silu(const h3_tensor *y, const h3_tensor *x, void *stream);
 
 #ifdef __cplusplus
 }

@@ -2,8 +2,11 @@
 
 Host side in Python/PyTorch over the C-ABI library ``libh3b200.so``
 (include/h3_b200.h).  ``ops`` mirrors the reference operator API (h3_* fused
-pointwise ops, mha, linear); ``block`` composes one DiT block and the 40-block
-step; ``ulysses`` shards the block over GPUs with the head<->sequence all-to-all.
+pointwise ops, mha, linear, and the fp32 linear / row gather / SiLU ops of the
+model wrapper); ``block`` composes one DiT block, ``step`` the 40-block
+denoising step, ``model`` the whole transformer forward around it (input
+projections, token refiner, packing, output norm and projections);
+``ulysses`` shards the block over GPUs with the head<->sequence all-to-all.
 """
 from . import ops  # noqa: F401
 from .ops import *  # noqa: F401,F403

@@ -23,6 +23,7 @@ _STATUS = {
     6: "CUDA launch error",
     7: "driver entry point unavailable",
     8: "bounded device wait timed out",
+    9: "row index outside the indexed tensor",
 }
 _DTYPES = {torch.bfloat16: 0, torch.float32: 1, torch.float64: 2, torch.int64: 3}
 
@@ -64,6 +65,10 @@ SIGNATURES = {
     "h3_linear_swiglu": [P, P, P, _V],
     "h3_linear_gated_residual": [P, P, P, P, P, _V],
     "h3_pack_gate_up": [P, P, _V],
+    "h3_linear_f32": [P, P, P, P, _V],
+    "h3_gather_rows": [P, P, P, _V],
+    "h3_index_copy_rows": [P, P, P, _V],
+    "h3_silu": [P, P, _V],
 }
 
 _lib = None

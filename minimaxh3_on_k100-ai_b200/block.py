@@ -72,9 +72,10 @@ class BlockConfig:
 
 
 def random_block_weights(cfg: BlockConfig, device, seed: int = 0, std: float = 0.02,
-                         adaln: bool = True) -> BlockWeights:
+                         adaln: bool = True, temb_dim: int | None = None) -> BlockWeights:
     """Random-init weights ~N(0, std), norm weights ones,
-    qk-norm weights ones.  Generated on the device (no checkpoint is used)."""
+    qk-norm weights ones.  Generated on the device (no checkpoint is used).  The
+    AdaLN projection reads a time embedding of ``temb_dim`` (default: hidden)."""
     g = torch.Generator(device=device)
     g.manual_seed(seed)
     hd, f, d = cfg.hidden, cfg.ffn, cfg.head_dim
@@ -89,7 +90,7 @@ def random_block_weights(cfg: BlockConfig, device, seed: int = 0, std: float = 0
         norm1=torch.ones(hd, dtype=torch.bfloat16, device=device),
         norm2=torch.ones(hd, dtype=torch.bfloat16, device=device))
     if adaln:
-        w.w_adaln = rnd(cfg.modalities * 6 * hd, hd)
+        w.w_adaln = rnd(cfg.modalities * 6 * hd, temb_dim or hd)
         w.b_adaln = rnd(cfg.modalities * 6 * hd)
     return w.prepare()
 
@@ -170,27 +171,51 @@ class TimeEmbedderWeights:
     b2: torch.Tensor
 
 
-def random_time_embedder(hidden: int, device, in_dim: int = 256, seed: int = 1) -> TimeEmbedderWeights:
+def random_time_embedder(hidden: int, device, in_dim: int = 256, seed: int = 1,
+                         out_dim: int | None = None) -> TimeEmbedderWeights:
+    """fp32 time MLP in_dim -> hidden -> out_dim (default hidden), ~N(0, 0.02)."""
     g = torch.Generator(device=device)
     g.manual_seed(seed)
     r = lambda *s: torch.randn(*s, generator=g, device=device) * 0.02  # noqa: E731
-    return TimeEmbedderWeights(r(hidden, in_dim), r(hidden), r(hidden, hidden), r(hidden))
+    out_dim = out_dim or hidden
+    return TimeEmbedderWeights(r(hidden, in_dim), r(hidden), r(out_dim, hidden), r(out_dim))
 
 
 def time_embedding(t: torch.Tensor, tw: TimeEmbedderWeights, in_dim: int = 256) -> torch.Tensor:
-    """temb [N, Hd] fp32 = linear_2(silu(linear_1(sinusoid(t))))  (fp32 linears are
-    library GEMMs: two tiny matrix-vector products once per step)."""
+    """temb [N, out] fp32 = linear_2(silu(linear_1(sinusoid(t))))
+    (MiniMaxH3TimeEmbedder::forward, patches/InfiniLM.patch:1494-1517): the fp32
+    linears and the SiLU are the h3_linear_f32 / h3_silu kernels."""
     emb = ops.timestep_embedding(t, in_dim)
-    hidden = torch.nn.functional.silu(emb @ tw.w1.t() + tw.b1)
-    return hidden @ tw.w2.t() + tw.b2
+    hidden = ops.silu(ops.linear_f32(emb, tw.w1, tw.b1))
+    return ops.linear_f32(hidden, tw.w2, tw.b2)
+
+
+_UNIT: dict = {}
+
+
+def unit_gate(width: int, device) -> torch.Tensor:
+    """A BF16 row of ones [width] (cached), the gate that turns a gated residual
+    into a plain add: bf16(x + bf16(1 * y)) = bf16(x + y)."""
+    key = (width, str(device))
+    if key not in _UNIT:
+        _UNIT[key] = torch.ones(width, dtype=torch.bfloat16, device=device)
+    return _UNIT[key]
+
+
+def add_bias(y: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+    """y + bias in BF16 (one rounding), in place: the gated-residual kernel with a
+    unit gate."""
+    flat = y.reshape(-1, y.shape[-1])
+    ops.h3_gated_residual_(flat, flat, unit_gate(flat.shape[-1], y.device), bias.expand(flat.shape))
+    return y
 
 
 def adaln_modulation(temb: torch.Tensor, w: BlockWeights, cfg: BlockConfig) -> torch.Tensor:
     """[N*modalities, 6*Hd] BF16 modulation rows of one block: silu(temb) -> bf16,
     projected by the block's AdaLN linear (tcgen05 GEMM) plus bias
     (MiniMaxH3AdaLNProjection::forward, patches/InfiniLM.patch:1260-1279)."""
-    activated = torch.nn.functional.silu(temb).to(torch.bfloat16)
-    mod = ops.linear(activated, w.w_adaln) + w.b_adaln
+    activated = ops.silu(temb, dtype=torch.bfloat16)
+    mod = add_bias(ops.linear(activated, w.w_adaln), w.b_adaln)
     return mod.view(temb.shape[0] * cfg.modalities, 6 * cfg.hidden)
 
 

@@ -4,6 +4,7 @@
 
 extern "C" unsigned int h3_attention_device_error_read_and_clear(void);
 extern "C" unsigned int h3_gemm_device_error_read_and_clear(void);
+extern "C" unsigned int h3_model_ops_device_error_read_and_clear(void);
 
 extern "C" int h3_abi_version(void) { return H3_ABI_VERSION; }
 
@@ -18,20 +19,24 @@ extern "C" const char *h3_status_string(int status) {
         case H3_ERR_LAUNCH: return "CUDA launch error";
         case H3_ERR_DRIVER: return "driver entry point unavailable";
         case H3_ERR_TIMEOUT: return "bounded device wait timed out";
+        case H3_ERR_INDEX: return "row index outside the indexed tensor";
         default: return "unknown status";
     }
 }
 
 // Synchronises the current device, then reads and clears the device error words
-// of the kernels with bounded waits.  Returns H3_ERR_TIMEOUT if any wait expired
-// since the last call, H3_ERR_LAUNCH if the device reports an error, else H3_OK.
+// of the kernels with bounded waits or index checks.  Returns H3_ERR_TIMEOUT if
+// any wait expired since the last call, else H3_ERR_INDEX if a row index was out
+// of range, H3_ERR_LAUNCH if the device reports an error, else H3_OK.
 extern "C" int h3_device_error(void) {
     if (cudaDeviceSynchronize() != cudaSuccess) return H3_ERR_LAUNCH;
     unsigned int own = 0, zero = 0;
     cudaMemcpyFromSymbol(&own, h3::g_h3_device_error, sizeof(own));
     cudaMemcpyToSymbol(h3::g_h3_device_error, &zero, sizeof(zero));
-    const unsigned int w = own | h3_attention_device_error_read_and_clear() | h3_gemm_device_error_read_and_clear();
-    return w ? H3_ERR_TIMEOUT : H3_OK;
+    const unsigned int w = own | h3_attention_device_error_read_and_clear() | h3_gemm_device_error_read_and_clear() |
+                           h3_model_ops_device_error_read_and_clear();
+    if (w & 1u) return H3_ERR_TIMEOUT;
+    return (w & 2u) ? H3_ERR_INDEX : H3_OK;
 }
 
 namespace {

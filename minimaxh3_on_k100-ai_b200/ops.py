@@ -27,6 +27,7 @@ __all__ = [
     "h3_gated_residual_rms_modulate", "h3_gated_residual_rms_modulate_", "h3_qk_norm_rope_",
     "h3_rope_cache", "h3_rope_cache_sectioned", "rope_powers", "timestep_embedding", "mha", "mha_",
     "linear", "linear_", "linear_swiglu", "linear_gated_residual", "pack_gate_up",
+    "linear_f32", "linear_f32_", "gather_rows", "gather_rows_", "index_copy_rows_", "silu", "silu_",
 ]
 
 
@@ -227,6 +228,52 @@ def linear_gated_residual(x, weight, residual, gate, out=None):
     call("h3_linear_gated_residual", desc(_flat(out)), desc(_flat(x)), desc(weight), desc(r2), desc(g2),
          stream_of(x))
     return out
+
+
+# ---------------------------------------------------------------------------
+# model wrapper ops (outside the block loop)
+# ---------------------------------------------------------------------------
+def linear_f32_(out, x, weight, bias=None):
+    """out [M,N] = x [M,K] (BF16 or F32) * weight[N,K]^T (+ bias) in fp32, stored as out's dtype
+    (F32, or BF16 rounded once) -- linear_forward on the F32 modules of MiniMaxH3Transformer."""
+    require_cuda(out, x, weight, bias)
+    call("h3_linear_f32", desc(_flat(out)), desc(_flat(x)), desc(weight), desc(bias), stream_of(x))
+    return out
+
+
+def linear_f32(x, weight, bias=None, out_dtype=torch.float32):
+    out = torch.empty(*x.shape[:-1], weight.shape[0], dtype=out_dtype, device=x.device)
+    return linear_f32_(out, x, weight, bias)
+
+
+def gather_rows_(out, table, indices):
+    """out[r] = table[indices[r]] (gather_rows / op::embedding)."""
+    require_cuda(out, table, indices)
+    call("h3_gather_rows", desc(out), desc(table), desc(indices), stream_of(table))
+    return out
+
+
+def gather_rows(table, indices):
+    out = torch.empty(indices.shape[0], table.shape[1], dtype=table.dtype, device=table.device)
+    return gather_rows_(out, table, indices)
+
+
+def index_copy_rows_(out, indices, src):
+    """out[indices[r]] = src[r] in place (op::index_copy along the token dim)."""
+    require_cuda(out, src, indices)
+    call("h3_index_copy_rows", desc(out), desc(indices), desc(src), stream_of(src))
+    return out
+
+
+def silu_(out, x):
+    """out = silu(x) in fp32, stored as out's dtype (F32 or BF16)."""
+    require_cuda(out, x)
+    call("h3_silu", desc(out), desc(x), stream_of(x))
+    return out
+
+
+def silu(x, dtype=torch.float32):
+    return silu_(torch.empty(x.shape, dtype=dtype, device=x.device), x)
 
 
 def library_loaded() -> bool:

@@ -19,11 +19,12 @@ from dataclasses import dataclass, field
 import torch
 
 from . import ops
-from .block import (BlockConfig, Segment, Workspace, adaln_modulation, block_forward, random_block_weights,
-                    random_time_embedder, segments_from_indices, time_embedding)
+from .block import (BlockConfig, Segment, Workspace, adaln_modulation, add_bias, block_forward,
+                    random_block_weights, random_time_embedder, segments_from_indices, time_embedding)
 from .ulysses import SequenceParallel, local_rows
 
-VIDEO_TAG, TEXT_TAG = 0, 2   # token tags; adaln row = 3 * timestep_index + tag (:1695-1697)
+# token tags video 0, text 1, audio 2 (patches/InfiniLM.patch:137); adaln row = 3 * timestep_index + tag (:1695-1697)
+VIDEO_TAG, TEXT_TAG, AUDIO_TAG = 0, 1, 2
 
 
 @dataclass
@@ -55,20 +56,19 @@ def joint_positions(cfg: StepConfig) -> torch.Tensor:
     return torch.cat([video, cond]).double()
 
 
-class DiTStep:
-    """One denoising step of the block stack.  ``forward`` takes this rank's
-    tokens [T, Hd] on the device; ``__call__`` is the end-to-end entry point
-    (host tensor in, host tensor out)."""
+class BlockStack:
+    """The block loop shared by ``DiTStep`` and ``model.H3Transformer``: the
+    blocks' weights (AdaLN projections column-split across ranks), the batched
+    AdaLN of every block, the Ulysses exchange state and the per-shape
+    activation buffers."""
 
-    def __init__(self, cfg: StepConfig, device, world: int = 1, rank: int = 0, group=None, seed: int = 0):
-        self.cfg = cfg
+    def __init__(self, bc: BlockConfig, blocks: int, device, world: int = 1, rank: int = 0, group=None,
+                 seed: int = 0, temb_dim: int | None = None):
+        self.cfg = bc
         self.device = torch.device(device)
-        bc = cfg.block
-        self.world, self.rank = world, rank
-        self.local, start, padded = local_rows(cfg.tokens, world, rank)
-        self.start = start
-        self.weights = [random_block_weights(bc, self.device, seed=seed + 1000 * i) for i in range(cfg.blocks)]
-        self.group = group
+        self.world, self.rank, self.group = world, rank, group
+        self.weights = [random_block_weights(bc, self.device, seed=seed + 1000 * i, temb_dim=temb_dim)
+                        for i in range(blocks)]
         if world > 1:
             # AdaLN projections stay column-parallel (as the reference keeps them,
             # patches/InfiniLM.patch:1286-1292, 1740-1761): rank r holds output columns
@@ -82,6 +82,65 @@ class DiTStep:
             for w in self.weights:
                 w.w_adaln = w.w_adaln[rank * n:(rank + 1) * n].contiguous()
                 w.b_adaln = w.b_adaln[rank * n:(rank + 1) * n].contiguous()
+        self._ws: dict[int, Workspace] = {}
+        self._sp: dict[tuple[int, int], SequenceParallel] = {}
+
+    def workspace(self, tokens: int) -> Workspace:
+        if tokens not in self._ws:
+            self._ws[tokens] = Workspace(tokens, self.cfg, self.device)
+        return self._ws[tokens]
+
+    def sequence_parallel(self, valid_tokens: int, local_tokens: int) -> SequenceParallel | None:
+        if self.world == 1:
+            return None
+        key = (valid_tokens, local_tokens)
+        if key not in self._sp:
+            self._sp[key] = SequenceParallel(self.world, self.rank, self.group, valid_tokens, local_tokens,
+                                             self.cfg.heads, self.cfg.head_dim, self.device)
+        return self._sp[key]
+
+    def modulations(self, temb: torch.Tensor) -> list[torch.Tensor]:
+        """Every block's modulation rows [timesteps*modalities, 6*Hd], computed up
+        front (the reference's batched AdaLN, patches/InfiniLM.patch:1718-1761)."""
+        bc = self.cfg
+        if self.world == 1:
+            return [adaln_modulation(temb, w, bc) for w in self.weights]
+        import torch.distributed as dist
+        activated = ops.silu(temb, dtype=torch.bfloat16)
+        local = torch.stack([add_bias(ops.linear(activated, w.w_adaln), w.b_adaln) for w in self.weights])
+        gathered = torch.empty((self.world,) + tuple(local.shape), dtype=local.dtype, device=local.device)
+        dist.all_gather_into_tensor(gathered, local, group=self.group)
+        blocks, t, n = local.shape
+        full = gathered.permute(1, 2, 0, 3).reshape(blocks, t * self.world * n)   # rank-major columns
+        rows = t * bc.modalities
+        return [full[i].view(rows, 6 * bc.hidden) for i in range(blocks)]
+
+    def run(self, h: torch.Tensor, mods: list[torch.Tensor], segments: list[Segment], cos: torch.Tensor,
+            sin: torch.Tensor, valid_tokens: int) -> torch.Tensor:
+        """The block loop on this rank's tokens h [T, Hd]; returns one of the two
+        workspace output buffers."""
+        ws = self.workspace(h.shape[0])
+        sp = self.sequence_parallel(valid_tokens, h.shape[0])
+        for i, w in enumerate(self.weights):
+            h = block_forward(h, mods[i], segments, w, cos, sin, self.cfg, ws, out=ws.out[i % 2], sp=sp)
+        return h
+
+
+class DiTStep:
+    """One denoising step of the block stack.  ``forward`` takes this rank's
+    tokens [T, Hd] on the device; ``__call__`` is the end-to-end entry point
+    (host tensor in, host tensor out)."""
+
+    def __init__(self, cfg: StepConfig, device, world: int = 1, rank: int = 0, group=None, seed: int = 0):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        bc = cfg.block
+        self.world, self.rank = world, rank
+        self.local, start, padded = local_rows(cfg.tokens, world, rank)
+        self.start = start
+        self.group = group
+        self.stack = BlockStack(bc, cfg.blocks, self.device, world, rank, group, seed)
+        self.weights = self.stack.weights
         self.time = random_time_embedder(bc.hidden, self.device, seed=seed + 7)
         # per-token tables of the local rows; padded rows reuse row 0 (:1706-1710)
         pos = joint_positions(cfg)
@@ -92,11 +151,8 @@ class DiTStep:
         table = ops.h3_rope_cache(pos[idx].to(self.device), power)
         self.cos, self.sin = table[:, :48], table[:, 48:]
         self.segments: list[Segment] = segments_from_indices((3 * 0 + tags[idx]).tolist())
-        self.ws = Workspace(self.local, bc, self.device)
-        self.sp = None
-        if world > 1:
-            self.sp = SequenceParallel(world, rank, group, cfg.tokens, self.local, bc.heads, bc.head_dim,
-                                       self.device)
+        self.ws = self.stack.workspace(self.local)
+        self.sp = self.stack.sequence_parallel(cfg.tokens, self.local)
         self.timestep = torch.full((1,), cfg.timestep, dtype=torch.float32, device=self.device)
         self.x_dev = torch.empty(self.local, bc.hidden, dtype=torch.bfloat16, device=self.device)
         self.graph, self.graph_out = None, None
@@ -104,27 +160,11 @@ class DiTStep:
     def modulations(self, timestep: torch.Tensor) -> list[torch.Tensor]:
         """Every block's modulation rows [timesteps*modalities, 6*Hd], computed up
         front (the reference's batched AdaLN)."""
-        temb = time_embedding(timestep, self.time)
-        if self.world == 1:
-            return [adaln_modulation(temb, w, self.cfg.block) for w in self.weights]
-        import torch.distributed as dist
-        activated = torch.nn.functional.silu(temb).to(torch.bfloat16)
-        local = torch.stack([ops.linear(activated, w.w_adaln) + w.b_adaln for w in self.weights])  # [B, t, n]
-        gathered = torch.empty((self.world,) + tuple(local.shape), dtype=local.dtype, device=local.device)
-        dist.all_gather_into_tensor(gathered, local, group=self.group)
-        blocks, t, n = local.shape
-        full = gathered.permute(1, 2, 0, 3).reshape(blocks, t * self.world * n)   # rank-major columns
-        rows = t * self.cfg.block.modalities
-        return [full[i].view(rows, 6 * self.cfg.block.hidden) for i in range(blocks)]
+        return self.stack.modulations(time_embedding(timestep, self.time))
 
     def forward(self, x: torch.Tensor, timestep: torch.Tensor | None = None) -> torch.Tensor:
         ts = self.timestep if timestep is None else timestep
-        mods = self.modulations(ts)
-        h = x
-        for i, w in enumerate(self.weights):
-            h = block_forward(h, mods[i], self.segments, w, self.cos, self.sin, self.cfg.block, self.ws,
-                              out=self.ws.out[i % 2], sp=self.sp)
-        return h
+        return self.stack.run(x, self.modulations(ts), self.segments, self.cos, self.sin, self.cfg.tokens)
 
     def capture(self) -> None:
         """Record ``forward(self.x_dev)`` -- every kernel of the step and, under

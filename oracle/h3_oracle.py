@@ -26,6 +26,8 @@ line number inside the patch file):
 * MLP:                         patches/InfiniLM.patch:1172-1179 ([up; gate] rows, :5775-5784)
 * Ulysses permutations:        patches/InfiniLM.patch:895-1137
 * timestep embedding:          patches/InfiniCore.patch:2115-2137 (kernel), :2834-2845 (test formula)
+* model forward around blocks: patches/InfiniLM.patch:1626-1826 (packing, output norm/projections),
+                               :1198-1241 (token refiner), :1494-1538 (time embedder, output norm)
 """
 from __future__ import annotations
 
@@ -273,6 +275,96 @@ def block_forward(x: torch.Tensor, modulation: torch.Tensor, weights: dict, cos:
     hidden = swiglu(gate_up[:, :f], gate_up[:, f:])
     mlp = linear(hidden, weights["w_down"])
     return gated_residual(residual, gate_mlp, mlp)
+
+
+# --------------------------------------------------------------------------
+# Model forward around the block stack (patches/InfiniLM.patch:1626-1826)
+# --------------------------------------------------------------------------
+def linear_f32(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """fp32 linear of the F32 modules (proj_in/out, audio, time MLP), x widened to fp32."""
+    y = x.float() @ weight.float().t()
+    return y if bias is None else y + bias.float()
+
+
+def silu(x: torch.Tensor) -> torch.Tensor:
+    """op::silu in fp32."""
+    return torch.nn.functional.silu(x.float())
+
+
+def add_bias(y: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+    """bias of a BF16 linear: bf16(y + b) after the BF16 GEMM output."""
+    return _r(y.float() + bias.float())
+
+
+def time_embedder(t: torch.Tensor, w1, b1, w2, b2, in_dim: int = 256) -> torch.Tensor:
+    """MiniMaxH3TimeEmbedder::forward (:1494-1517): sinusoid -> linear_1 -> silu -> linear_2, fp32."""
+    return linear_f32(silu(linear_f32(timestep_embedding(t, in_dim), w1, b1)), w2, b2)
+
+
+def adaln_rows(temb: torch.Tensor, w: torch.Tensor, b: torch.Tensor, hidden: int, modalities: int = 3):
+    """MiniMaxH3AdaLNProjection::forward (:1260-1279): [timesteps*modalities, 6*Hd]."""
+    mod = add_bias(linear(_r(silu(temb)), w), b)
+    return mod.view(temb.shape[0] * modalities, 6 * hidden)
+
+
+def refiner_block_forward(x: torch.Tensor, w: dict, heads: int, eps: float, qk_eps: float) -> torch.Tensor:
+    """MiniMaxH3TokenRefinerBlock::forward (:1210-1216): plain RMSNorm, attention with
+    q/k RMSNorm over the head dim and no RoPE, residual adds; SwiGLU MLP."""
+    n, hd = x.shape
+    d = hd // heads
+    qkv = linear(rms_norm(x, w["norm1"], eps), w["w_qkv"]).view(n, 3, heads, d)
+    q = rms_norm(qkv[:, 0], w["norm_q"], qk_eps)
+    k = rms_norm(qkv[:, 1], w["norm_k"], qk_eps)
+    attn = _r(attention_fp32(q[None], k[None], qkv[:, 2][None], d ** -0.5)[0]).reshape(n, hd)
+    out = _r(x.float() + linear(attn, w["w_o"]).float())
+    gate_up = linear(rms_norm(out, w["norm2"], eps), w["w_gate_up"])
+    f = gate_up.shape[1] // 2
+    mlp = linear(swiglu(gate_up[:, :f], gate_up[:, f:]), w["w_down"])
+    return _r(out.float() + mlp.float())
+
+
+def model_forward(inputs: dict, weights: dict, blocks: Sequence[dict], heads: int, eps: float = 1e-6,
+                  qk_eps: float = 1e-6, final_eps: float = 1e-6, sections: Sequence[int] = (16, 16, 16),
+                  time_in: int = 256):
+    """The whole transformer forward on one device (:1626-1826); returns
+    (video [1, Nv, patch], audio [1, Na, audio]) in fp32.  ``weights`` holds the
+    non-block modules, ``blocks`` the per-block dicts of ``block_forward`` plus
+    ``w_adaln`` / ``b_adaln``."""
+    w = weights
+    hd = w["ctx_w"].shape[0]
+    video_embeds = _r(linear_f32(inputs["video"][0], w["proj_in_w"], w["proj_in_b"]))
+    audio_embeds = _r(linear_f32(inputs["audio"][0], w["audio_in_w"], w["audio_in_b"]))
+    x = add_bias(linear(inputs["text"][0].to(BF16), w["ctx_w"]), w["ctx_b"])
+    for rb in w["refiner"]:
+        x = refiner_block_forward(x, rb, heads, eps, qk_eps)
+    text_embeds = rms_norm(x, w["refiner_norm"], final_eps)
+    seq = inputs["position_ids"].shape[0]
+    hidden = torch.zeros(seq, hd, dtype=BF16)
+    hidden[inputs["text_indices"]] = text_embeds
+    hidden[inputs["video_indices"]] = video_embeds
+    hidden[inputs["audio_indices"]] = audio_embeds
+    temb = time_embedder(inputs["timestep"].float(), w["time_w1"], w["time_b1"], w["time_w2"], w["time_b2"],
+                         time_in)
+    adaln_idx = (3 * inputs["timestep_indices"] + inputs["token_tags"]).tolist()
+    segments = []
+    for i, row in enumerate(adaln_idx):
+        if segments and segments[-1][2] == row:
+            segments[-1][1] += 1
+        else:
+            segments.append([i, 1, row])
+    table = rotary_cache(inputs["position_ids"], sections)
+    half = table.shape[1] // 2
+    cos, sin = table[:, :half], table[:, half:]
+    h = hidden
+    for bw in blocks:
+        mod = adaln_rows(temb, bw["w_adaln"], bw["b_adaln"], hd)
+        h = block_forward(h, mod, bw, cos, sin, heads, eps, qk_eps, segments=segments)
+    out_mod = add_bias(linear(_r(silu(temb)), w["norm_out_w"]), w["norm_out_b"])
+    tok = out_mod[inputs["timestep_indices"]]
+    normalized = rms_modulate(h, w["norm_out"], tok[:, hd:], tok[:, :hd], final_eps)
+    video_all = linear_f32(normalized, w["proj_out_w"], w["proj_out_b"])
+    audio_all = linear_f32(normalized, w["audio_out_w"], w["audio_out_b"])
+    return video_all[inputs["video_indices"]][None], audio_all[inputs["audio_indices"]][None]
 
 
 # --------------------------------------------------------------------------
