@@ -67,3 +67,43 @@ def test_ulysses_two_gpus_bitwise_equal_to_one(tmp_path):
     ref = one.forward(_x(cfg).to("cuda:0")).cpu()
     sp = torch.cat([torch.load(f"{path}.{r}") for r in range(WORLD)])[:cfg.tokens]
     assert torch.equal(sp, ref), "W-GPU output differs from the 1-GPU run"
+
+
+def _model_worker(rank, port, path):
+    import datetime
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    from h3b200.model import H3Transformer, packed_inputs
+    cfg = _model_cfg()
+    model = H3Transformer(cfg, f"cuda:{rank}", world=WORLD, rank=rank, group=dist.group.WORLD, seed=11)
+    inputs = packed_inputs(cfg, video_grid=(2, 6, 10), audio_tokens=13, text_tokens=30, seed=2)
+    video, audio = model(**{k: v.to(f"cuda:{rank}") for k, v in inputs.items()})
+    torch.save((video.cpu(), audio.cpu()), f"{path}.{rank}")
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _model_cfg():
+    from h3b200.block import BlockConfig
+    from h3b200.model import H3ModelConfig
+    return H3ModelConfig(block=BlockConfig(hidden=512, heads=4, ffn=1536), blocks=2, refiner_blocks=2, text_dim=512)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+def test_model_forward_two_gpus_bitwise_equal_to_one(tmp_path):
+    """The whole transformer forward (refiner replicated, blocks sequence-parallel,
+    output rows all-gathered): 163 tokens, so one rank carries a padding row."""
+    path = str(tmp_path / "model")
+    mp.start_processes(_model_worker, args=(_free_port(), path), nprocs=WORLD, start_method="spawn")
+    from h3b200.model import H3Transformer, packed_inputs
+    cfg = _model_cfg()
+    model = H3Transformer(cfg, "cuda:0", seed=11)
+    inputs = packed_inputs(cfg, video_grid=(2, 6, 10), audio_tokens=13, text_tokens=30, seed=2)
+    video, audio = model(**{k: v.to("cuda:0") for k, v in inputs.items()})
+    for r in range(WORLD):
+        v, a = torch.load(f"{path}.{r}")
+        assert torch.equal(v, video.cpu()) and torch.equal(a, audio.cpu()), f"rank {r} differs from the 1-GPU run"
