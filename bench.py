@@ -44,9 +44,9 @@ def parse():
     p.add_argument("--blocks", type=int, default=40)
     p.add_argument("--no-graph", action="store_true", help="eager launches instead of one CUDA graph per step")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--workload", choices=["step", "attention", "pointwise"], default="step",
+    p.add_argument("--workload", choices=["step", "attention", "pointwise", "gemm"], default="step",
                    help="step: BASELINE config 5 (default, the headline); attention: config 2; "
-                        "pointwise: config 1 op set")
+                        "pointwise: config 1 op set; gemm: the block's four projections at config 3")
     return p.parse_args()
 
 
@@ -423,6 +423,90 @@ def _timed(fn, reps, stream):
     return a.elapsed_time(b) / reps
 
 
+def run_gemm(args):
+    """The block's four projections at BASELINE config 3 (18432 tokens, hidden 5120,
+    FFN 13824) with their fused epilogues: QKV, out-proj, gate_up + SwiGLU,
+    down + gated residual.  About 1.7 GB on the device; every operand set is read
+    once per launch and the weights alone exceed L2."""
+    import h3b200
+    from h3b200 import _lib, ops
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    h3b200.load()
+    n, hd, f = 18432, 5120, 13824
+    g = torch.Generator(device=device).manual_seed(0)
+    rnd = lambda *s: (torch.randn(*s, generator=g, device=device) * 0.02).bfloat16()  # noqa: E731
+    x = rnd(n, hd) * 50
+    w_qkv, w_o, w_gu, w_down = rnd(3 * hd, hd), rnd(hd, hd), rnd(2 * f, hd), rnd(hd, f)
+    w_gu_packed = ops.pack_gate_up(w_gu)
+    qkv = torch.empty(n, 3 * hd, dtype=torch.bfloat16, device=device)
+    o = torch.empty(n, hd, dtype=torch.bfloat16, device=device)
+    hidden = rnd(n, f) * 50
+    res = torch.empty(n, hd, dtype=torch.bfloat16, device=device)
+    gate = rnd(hd)
+    gemms = {
+        "qkv": (lambda: ops.linear_(qkv, x, w_qkv), 2.0 * n * 3 * hd * hd),
+        "out": (lambda: ops.linear_(o, x, w_o), 2.0 * n * hd * hd),
+        "gate_up_swiglu": (lambda: ops.linear_swiglu(x, w_gu_packed, out=hidden), 2.0 * n * 2 * f * hd),
+        "down_gated_residual": (lambda: ops.linear_gated_residual(hidden, w_down, x, gate, out=res),
+                                2.0 * n * hd * f),
+    }
+    stream = torch.cuda.current_stream(device)
+    for fn, _ in gemms.values():
+        for _ in range(args.warmup):
+            fn()
+    sampler = ClockSampler()
+    sampler.start()
+    time.sleep(0.3)
+    c0 = _lib.CALLS["n"]
+    per = {}
+    total_ms, total_flop = 0.0, 0.0
+    for name, (fn, flop) in gemms.items():
+        ms = _timed(fn, args.steps, stream)
+        per[name] = {"ms": round(ms, 3), "tflops": round(flop / (ms * 1e-3) / 1e12, 1)}
+        total_ms += ms
+        total_flop += flop
+    launches = _lib.CALLS["n"] - c0
+    clocks = sampler.stop()
+    pk, kind = peaks()
+    achieved = total_flop / (total_ms * 1e-3) / 1e12
+    hx = x.cpu().pin_memory()
+    hq = torch.empty(n, 3 * hd, dtype=torch.bfloat16).pin_memory()
+
+    def e2e():
+        ops.linear_(qkv, hx.to(device, non_blocking=True), w_qkv)
+        hq.copy_(qkv, non_blocking=True)
+        stream.synchronize()
+    e2e_ms = _timed(e2e, args.steps, stream)
+    line = {"metric": "block GEMM TFLOP/s (config 3: QKV, out, gate_up+SwiGLU, down+gated residual)",
+            "value": round(achieved, 1), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(total_ms, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "config3 projections: 18432 tokens, hidden 5120, FFN 13824, random bf16 "
+                                   "weights; a step = the four GEMMs once each",
+                       "l2": "weights 157-283 MB per GEMM and activations 189-510 MB exceed the 126 MB L2"},
+            "e2e": {"value": round(gemms["qkv"][1] / (e2e_ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s (QKV GEMM)",
+                    "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": qkv.numel() * 2},
+            "gpu_launches": launches, "gemms": per,
+            "roofline": {"kernel": "gemm_kernel (tcgen05, 128x256 tiles)", "bound": "tensor",
+                         "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": round(achieved / pk["bf16_tflops"], 4),
+                         "peak_source": f"{kind} bf16_tflops (burst)", "traffic": _ncu_traffic("gemm_kernel")},
+            "clocks": clocks}
+    if not args.no_cpu_baseline:
+        from oracle import h3_oracle as O
+        torch.set_num_threads(os.cpu_count() or 1)
+        xc, wc = hx[:256], w_qkv.cpu()
+        O.linear(xc[:16], wc)
+        t0 = time.perf_counter()
+        O.linear(xc, wc)
+        spent = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": round(2.0 * 256 * 3 * hd * hd / spent / 1e12, 4), "unit": "TFLOP/s",
+                                "cores": torch.get_num_threads(), "kind": "port",
+                                "sample": f"oracle QKV linear (fp32 accumulate) on 256 of 18432 tokens ({spent:.2f} s)"}
+    return line
+
+
 def run_attention(args):
     """non-causal attention, Q,K,V [1, 40, 18432, 128] (passed in
     the mha [B, S, H, D] layout), scale 1/sqrt(128).  Inputs (3 x 189 MB) exceed L2."""
@@ -620,7 +704,8 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.workload != "step" and args.impl == "ours":
         if rank == 0:
-            _emit(out, run_attention(args) if args.workload == "attention" else run_pointwise(args))
+            runner = {"attention": run_attention, "pointwise": run_pointwise, "gemm": run_gemm}[args.workload]
+            _emit(out, runner(args))
         return 0
     if args.impl == "reference":
         _emit(out, run_reference(args, rank))
