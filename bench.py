@@ -279,9 +279,10 @@ def run_ours(args, rank, world, local_rank, group):
     else:
         sp = step.sp
         w_, hs = world, sp.group_heads[0]
-        attn_call = lambda: ops.mha_(sp.attn[0].unsqueeze(0), sp.recv[0][0].view(1, w_ * t, hs, bc.head_dim),  # noqa: E731
-                                     sp.recv[0][1].view(1, w_ * t, hs, bc.head_dim)[:, :cfg.tokens],
-                                     sp.recv[0][2].view(1, w_ * t, hs, bc.head_dim)[:, :cfg.tokens],
+        rq, rk, rv = sp.recv_p2p if sp.exchange == "p2p" else sp.recv[0]
+        attn_call = lambda: ops.mha_(sp.attn[0].unsqueeze(0), rq.view(1, w_ * t, hs, bc.head_dim),  # noqa: E731
+                                     rk.view(1, w_ * t, hs, bc.head_dim)[:, :cfg.tokens],
+                                     rv.view(1, w_ * t, hs, bc.head_dim)[:, :cfg.tokens],
                                      1.0 / math.sqrt(bc.head_dim))
         sq, sk, hh = w_ * t, cfg.tokens, hs
     for _ in range(2):
@@ -325,9 +326,11 @@ def run_ours(args, rank, world, local_rank, group):
         torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX, group=group)
     dev_s, e2e_s, attn_ms = vals.tolist()
 
-    # a graph holding NCCL calls must be released before destroy_process_group
+    # a graph holding NCCL calls must be released before destroy_process_group; the
+    # peer buffers are unmapped once every rank has finished writing into them
     step.release_graph()
-    torch.cuda.synchronize(device)
+    sync_all()
+    step.close()
     if rank != 0:
         return None
     pk, pk_kind = peaks()

@@ -27,6 +27,10 @@
  *   h3_gather_rows                 gather_rows -> op::embedding, InfiniLM.patch:587-590
  *   h3_index_copy_rows             op::index_copy of the packed sequence, InfiniLM.patch:1685-1690
  *   h3_silu                        op::silu + cast_to, InfiniLM.patch:1267-1268, 1511, 1535
+ *   h3_ipc_* , h3_exchange_*       the Ulysses all-to-alls all_to_all_[on_stream_]
+ *                                  (InfiniCore.patch:526-577) as used by gather_sequence /
+ *                                  scatter_sequence (InfiniLM.patch:895-910, 1127-1137): peer
+ *                                  receive buffers + epoch flags instead of a collective
  */
 #ifndef H3_B200_H
 #define H3_B200_H
@@ -39,6 +43,9 @@ extern "C" {
 
 #define H3_ABI_VERSION 1
 #define H3_MAX_DIMS 4
+#define H3_EXCHANGE_MAX_RANKS 8
+#define H3_EXCHANGE_SLOTS 4
+#define H3_IPC_HANDLE_BYTES 64
 
 typedef enum h3_dtype {
     H3_BF16 = 0,
@@ -192,6 +199,32 @@ int h3_index_copy_rows(const h3_tensor *out, const h3_tensor *indices, const h3_
 /* y = x / (1 + exp(-x)) computed in fp32 from x F32; y F32 or BF16 (rounded
  * once).  Contiguous. */
 int h3_silu(const h3_tensor *y, const h3_tensor *x, void *stream);
+
+/* ---------------- peer-memory exchange (sequence parallelism) ---------------- */
+
+/* Persistent buffers a peer process can map: cudaMalloc of `bytes` (zeroed) and
+ * its CUDA IPC handle (H3_IPC_HANDLE_BYTES bytes written to `handle`).  Allocated
+ * once at set-up, freed with h3_ipc_free; no other entry point allocates. */
+int h3_ipc_alloc(uint64_t bytes, void **ptr, void *handle);
+/* Map a peer's buffer from its handle (peer access enabled lazily); unmap with h3_ipc_close. */
+int h3_ipc_open(const void *handle, void **ptr);
+int h3_ipc_close(void *ptr);
+int h3_ipc_free(void *ptr);
+
+/* After the kernels that stored this rank's blocks into the peers' receive buffers
+ * (earlier on `stream`): increment this rank's epoch[slot] and write the new value
+ * into flags[slot][rank] of every peer.  peer_flags[p] is rank p's flag array
+ * (uint64 [H3_EXCHANGE_SLOTS][H3_EXCHANGE_MAX_RANKS]) as mapped in this process
+ * (own entry: the local array). */
+int h3_exchange_signal(void *const *peer_flags, uint64_t *epoch, int32_t slot, int32_t rank, int32_t world,
+                       void *stream);
+
+/* Wait (on the device, bounded by timeout_ns) until every peer's flags[slot][q]
+ * has reached this rank's epoch[slot]; later work on `stream` then sees the
+ * peers' data.  A wait that gives up ends the kernel normally and
+ * h3_device_error() returns H3_ERR_TIMEOUT. */
+int h3_exchange_wait(const void *flags, const uint64_t *epoch, int32_t slot, int32_t rank, int32_t world,
+                     uint64_t timeout_ns, void *stream);
 
 #ifdef __cplusplus
 }

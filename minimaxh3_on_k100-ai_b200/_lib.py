@@ -69,6 +69,12 @@ SIGNATURES = {
     "h3_gather_rows": [P, P, P, _V],
     "h3_index_copy_rows": [P, P, P, _V],
     "h3_silu": [P, P, _V],
+    "h3_ipc_alloc": [ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p],
+    "h3_ipc_open": [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)],
+    "h3_ipc_close": [ctypes.c_void_p],
+    "h3_ipc_free": [ctypes.c_void_p],
+    "h3_exchange_signal": [ctypes.POINTER(ctypes.c_void_p), _V, _I, _I, _I, _V],
+    "h3_exchange_wait": [_V, _V, _I, _I, _I, ctypes.c_uint64, _V],
 }
 
 _lib = None

@@ -5,6 +5,7 @@
 extern "C" unsigned int h3_attention_device_error_read_and_clear(void);
 extern "C" unsigned int h3_gemm_device_error_read_and_clear(void);
 extern "C" unsigned int h3_model_ops_device_error_read_and_clear(void);
+extern "C" unsigned int h3_exchange_device_error_read_and_clear(void);
 
 extern "C" int h3_abi_version(void) { return H3_ABI_VERSION; }
 
@@ -34,7 +35,7 @@ extern "C" int h3_device_error(void) {
     cudaMemcpyFromSymbol(&own, h3::g_h3_device_error, sizeof(own));
     cudaMemcpyToSymbol(h3::g_h3_device_error, &zero, sizeof(zero));
     const unsigned int w = own | h3_attention_device_error_read_and_clear() | h3_gemm_device_error_read_and_clear() |
-                           h3_model_ops_device_error_read_and_clear();
+                           h3_model_ops_device_error_read_and_clear() | h3_exchange_device_error_read_and_clear();
     if (w & 1u) return H3_ERR_TIMEOUT;
     return (w & 2u) ? H3_ERR_INDEX : H3_OK;
 }

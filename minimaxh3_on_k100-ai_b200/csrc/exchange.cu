@@ -1,0 +1,154 @@
+// Peer-memory exchange for the Ulysses all-to-alls (patches/InfiniLM.patch:895-1137,
+// all_to_all_* InfiniCore.patch:526-577): the sending kernels (q/k RMSNorm + RoPE,
+// row copies of v and of the attention output) store straight into the peers'
+// receive buffers over NVLink, then one thread per rank raises an epoch flag in
+// every peer's flag array and the receiver waits for its peers' flags before the
+// next kernel reads the data.  Receive buffers are plain cudaMalloc allocations
+// shared through CUDA IPC handles (no multicast objects, no NVLS).
+//
+// Flag array of a rank: uint64 flags[slot][H3_EXCHANGE_MAX_RANKS]; flags[s][q] is
+// written only by rank q.  Every rank also keeps uint64 epoch[slot] locally: the
+// signal kernel increments it and sends the new value, the wait kernel waits
+// until every peer's flag has reached the local value.  All ranks run the same
+// sequence of exchanges, so their epochs advance together; a peer can be at
+// most one exchange ahead (it needs this rank's next message to go further),
+// hence the >= test.
+//
+// Buffer reuse needs no extra flags: a rank writes a peer's q/k/v receive buffer
+// for block i+1 only after it has received that peer's attention output of block i
+// (sent after the peer's attention read the buffer), and a peer writes this rank's
+// output-return buffer for block i+1 only after receiving this rank's q/k/v of
+// block i+1 (sent after this rank consumed block i's returns).
+#include <stdint.h>
+#include <string.h>
+
+#include "h3_abi_util.h"
+#include "sm100_ptx.cuh"
+
+namespace h3 {
+namespace xchg {
+
+struct PeerFlags {
+    uint64_t *flags[H3_EXCHANGE_MAX_RANKS];  // flag array of every rank (own entry included)
+};
+
+__device__ __forceinline__ void st_release_sys(uint64_t *p, uint64_t v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t *p) {
+    uint64_t v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__global__ void signal_kernel(PeerFlags peers, uint64_t *epoch, int slot, int rank, int world) {
+    if (threadIdx.x != 0) return;
+    const uint64_t e = epoch[slot] + 1;
+    epoch[slot] = e;
+    // the data stores of the preceding kernels on this stream are complete; order
+    // the flag after them for every observer in the system
+    __threadfence_system();
+    for (int p = 0; p < world; ++p)
+        if (p != rank) st_release_sys(peers.flags[p] + slot * H3_EXCHANGE_MAX_RANKS + rank, e);
+}
+
+__global__ void wait_kernel(const uint64_t *flags, const uint64_t *epoch, int slot, int rank, int world,
+                            uint64_t timeout_ns) {
+    const int q = threadIdx.x;
+    bool ok = true;
+    if (q < world && q != rank) {
+        const uint64_t target = epoch[slot];
+        const uint64_t *f = flags + slot * H3_EXCHANGE_MAX_RANKS + q;
+        const uint64_t start = globaltimer();
+        while (ld_acquire_sys(f) < target) {
+            if (globaltimer() - start > timeout_ns) {
+                ok = false;
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    if (!ok) atomicOr(&g_h3_device_error, 1u);
+    __syncwarp();
+    __threadfence_system();
+}
+
+}  // namespace xchg
+}  // namespace h3
+
+using namespace h3;
+
+extern "C" int h3_ipc_alloc(uint64_t bytes, void **ptr, void *handle) {
+    if (!ptr || !handle) return H3_ERR_NULL;
+    *ptr = nullptr;
+    if (bytes == 0) return H3_ERR_BAD_SHAPE;
+    void *p = nullptr;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) return H3_ERR_LAUNCH;
+    if (cudaMemset(p, 0, bytes) != cudaSuccess) {
+        cudaFree(p);
+        return H3_ERR_LAUNCH;
+    }
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+        cudaFree(p);
+        return H3_ERR_DRIVER;
+    }
+    static_assert(sizeof(cudaIpcMemHandle_t) == H3_IPC_HANDLE_BYTES, "IPC handle size");
+    memcpy(handle, &h, sizeof(h));
+    *ptr = p;
+    return H3_OK;
+}
+
+extern "C" int h3_ipc_open(const void *handle, void **ptr) {
+    if (!ptr || !handle) return H3_ERR_NULL;
+    *ptr = nullptr;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    void *p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return H3_ERR_DRIVER;
+    *ptr = p;
+    return H3_OK;
+}
+
+extern "C" int h3_ipc_close(void *ptr) {
+    if (!ptr) return H3_ERR_NULL;
+    return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? H3_OK : H3_ERR_DRIVER;
+}
+
+extern "C" int h3_ipc_free(void *ptr) {
+    if (!ptr) return H3_ERR_NULL;
+    return cudaFree(ptr) == cudaSuccess ? H3_OK : H3_ERR_LAUNCH;
+}
+
+extern "C" int h3_exchange_signal(void *const *peer_flags, uint64_t *epoch, int32_t slot, int32_t rank,
+                                  int32_t world, void *stream) {
+    if (!peer_flags || !epoch) return H3_ERR_NULL;
+    if (world < 1 || world > H3_EXCHANGE_MAX_RANKS || rank < 0 || rank >= world) return H3_ERR_BAD_SHAPE;
+    if (slot < 0 || slot >= H3_EXCHANGE_SLOTS) return H3_ERR_BAD_SHAPE;
+    xchg::PeerFlags pf{};
+    for (int p = 0; p < world; ++p) {
+        if (!peer_flags[p]) return H3_ERR_NULL;
+        pf.flags[p] = static_cast<uint64_t *>(peer_flags[p]);
+    }
+    xchg::signal_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(pf, epoch, slot, rank, world);
+    return launch_status();
+}
+
+extern "C" int h3_exchange_wait(const void *flags, const uint64_t *epoch, int32_t slot, int32_t rank, int32_t world,
+                                uint64_t timeout_ns, void *stream) {
+    if (!flags || !epoch) return H3_ERR_NULL;
+    if (world < 1 || world > H3_EXCHANGE_MAX_RANKS || rank < 0 || rank >= world) return H3_ERR_BAD_SHAPE;
+    if (slot < 0 || slot >= H3_EXCHANGE_SLOTS) return H3_ERR_BAD_SHAPE;
+    if (timeout_ns == 0 || timeout_ns > 60000000000ull) return H3_ERR_UNSUPPORTED;
+    xchg::wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(static_cast<const uint64_t *>(flags), epoch, slot, rank,
+                                                          world, timeout_ns);
+    return launch_status();
+}
+
+// device error word of this translation unit (exchange waits that gave up)
+extern "C" unsigned int h3_exchange_device_error_read_and_clear(void) {
+    unsigned int v = 0, zero = 0;
+    cudaMemcpyFromSymbol(&v, h3::g_h3_device_error, sizeof(v));
+    cudaMemcpyToSymbol(h3::g_h3_device_error, &zero, sizeof(zero));
+    return v;
+}

@@ -26,8 +26,11 @@ namespace mops {
 // or BF16 (the fp32 result rounded once, as cast_to after an F32 linear).
 // 64x64 output tile per 256-thread CTA, 4x4 outputs per thread, K in steps of 16
 // through shared memory (transposed so the inner loop reads are conflict-free).
-// Each output accumulates its K products in increasing k with fmaf, so results
-// do not depend on the launch shape.
+// Each output accumulates its K products in increasing k with fmaf.  For at most
+// GEMV_ROWS rows (the time MLP runs on one timestep) a warp per output column
+// streams its weight row instead: lane-strided partial sums, then a fixed
+// butterfly reduction.  Either way the result of a row depends only on M's path,
+// not on the other rows.
 // ---------------------------------------------------------------------------
 constexpr int LT = 64, LK = 16;
 
@@ -86,6 +89,39 @@ __global__ void __launch_bounds__(256) linear_f32_kernel(LinArgs a) {
             const int64_t n = n0 + tx + 16 * j;
             if (n >= a.N) continue;
             const float v = a.b ? __fadd_rn(acc[i][j], a.b[n]) : acc[i][j];
+            if (a.y_bf16) static_cast<__nv_bfloat16 *>(a.y)[m * a.sy + n] = __float2bfloat16_rn(v);
+            else static_cast<float *>(a.y)[m * a.sy + n] = v;
+        }
+    }
+}
+
+constexpr int GEMV_ROWS = 8;
+
+__global__ void __launch_bounds__(256) linear_f32_gemv_kernel(LinArgs a) {
+    const int64_t n = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (n >= a.N) return;
+    float acc[GEMV_ROWS] = {};
+    const float *wr = a.w + n * a.sw;
+    for (int64_t k = lane; k < a.K; k += 32) {
+        const float wv = wr[k];
+#pragma unroll
+        for (int m = 0; m < GEMV_ROWS; ++m) {
+            if (m < a.M) {
+                const float xv = a.x_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16 *>(a.x)[m * a.sx + k])
+                                          : static_cast<const float *>(a.x)[m * a.sx + k];
+                acc[m] = fmaf(xv, wv, acc[m]);
+            }
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < GEMV_ROWS; ++m) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc[m] = __fadd_rn(acc[m], __shfl_xor_sync(0xffffffffu, acc[m], o));
+    }
+    if (lane == 0) {
+        for (int m = 0; m < GEMV_ROWS && m < a.M; ++m) {
+            const float v = a.b ? __fadd_rn(acc[m], a.b[n]) : acc[m];
             if (a.y_bf16) static_cast<__nv_bfloat16 *>(a.y)[m * a.sy + n] = __float2bfloat16_rn(v);
             else static_cast<float *>(a.y)[m * a.sy + n] = v;
         }
@@ -177,6 +213,11 @@ extern "C" int h3_linear_f32(const h3_tensor *y, const h3_tensor *x, const h3_te
     mops::LinArgs a{x->data, static_cast<const float *>(w->data), bias ? static_cast<const float *>(bias->data) : nullptr,
                     y->data, M, N, K, x->strides[0], w->strides[0], y->strides[0],
                     x->dtype == H3_BF16, y->dtype == H3_BF16};
+    if (M <= mops::GEMV_ROWS) {
+        if ((N + 7) / 8 > 0x7fffffff) return H3_ERR_UNSUPPORTED;
+        mops::linear_f32_gemv_kernel<<<(unsigned)((N + 7) / 8), 256, 0, (cudaStream_t)stream>>>(a);
+        return launch_status();
+    }
     const dim3 grid((unsigned)((N + mops::LT - 1) / mops::LT), (unsigned)((M + mops::LT - 1) / mops::LT));
     mops::linear_f32_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(a);
     return launch_status();

@@ -224,6 +224,10 @@ class H3Transformer:
 
     __call__ = forward
 
+    def close(self) -> None:
+        """Release the peer-exchange buffers (every rank, after the last forward)."""
+        self.stack.close()
+
     def _gather_rows_of_ranks(self, local: torch.Tensor) -> torch.Tensor:
         """All ranks' [T, C] blocks concatenated in rank (= token) order (:1815-1820)."""
         import torch.distributed as dist

@@ -115,6 +115,13 @@ class BlockStack:
         rows = t * bc.modalities
         return [full[i].view(rows, 6 * bc.hidden) for i in range(blocks)]
 
+    def close(self) -> None:
+        """Unmap and free the peer-exchange buffers (call on every rank, after a
+        barrier that follows the last step)."""
+        for sp in self._sp.values():
+            sp.close()
+        self._sp = {}
+
     def run(self, h: torch.Tensor, mods: list[torch.Tensor], segments: list[Segment], cos: torch.Tensor,
             sin: torch.Tensor, valid_tokens: int) -> torch.Tensor:
         """The block loop on this rank's tokens h [T, Hd]; returns one of the two
@@ -185,6 +192,12 @@ class DiTStep:
         """Drop the graph (required before destroying a process group whose
         collectives it holds)."""
         self.graph, self.graph_out = None, None
+
+    def close(self) -> None:
+        """Release the peer-exchange buffers (every rank, after the last step)."""
+        self.release_graph()
+        self.stack.close()
+        self.sp = None
 
     def run(self) -> torch.Tensor:
         """One step on ``self.x_dev`` (graph replay when captured)."""

@@ -25,19 +25,30 @@ bitwise the ungrouped one).  The q/k RMSNorm + RoPE kernel writes straight into
 the permuted view of the send buffer ([T, W, Hs, D] view of [W, T, Hs, D]), so
 no separate pack pass is needed for q/k.
 
+On GPUs the exchange is peer-to-peer (``PeerExchange``): the receive buffers of
+every rank live in CUDA-IPC-shared allocations, the q/k RMSNorm + RoPE kernel
+stores each destination's block straight into that rank's receive buffer over
+NVLink (no send buffer, no separate collective), row-copy kernels do the same for
+v and for the attention output, and an epoch flag per rank (bounded device wait)
+replaces the collective's synchronisation.  ``exchange="collective"`` keeps the
+torch.distributed all_to_all_single path (NCCL, or gloo in the CPU tests).
+
 The exchange logic is written against a small ``kernels`` interface so the same
-host code runs with the CUDA ops on NCCL and, in the CPU tests, with the oracle
-on gloo ranks.
+host code runs with the CUDA ops and, in the CPU tests, with the oracle on gloo
+ranks.
 """
 from __future__ import annotations
 
 import contextlib
+import ctypes
 import math
 from dataclasses import dataclass
 from typing import Callable
 
 import torch
 import torch.distributed as dist
+
+from . import _lib
 
 
 @dataclass
@@ -75,9 +86,103 @@ def head_groups(heads_local: int, groups: int) -> list[int]:
     return [base + (1 if g < extra else 0) for g in range(groups)]
 
 
+class _CudaBytes:
+    """A raw device allocation seen through __cuda_array_interface__ (int16 units,
+    reinterpreted as BF16 by the caller)."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes // 2,), "typestr": "<i2", "data": (ptr, False),
+                                         "version": 3}
+
+
+class PeerExchange:
+    """Receive buffers every peer can store into, plus epoch flags
+    (h3_ipc_* / h3_exchange_* of the C-ABI).  Layout of each rank's allocation:
+    flags [SLOTS][MAX_RANKS] uint64 (256 B), then the named regions, 256-byte
+    aligned.  Created collectively (every rank, same regions)."""
+
+    MAX_RANKS, SLOTS, HANDLE = 8, 4, 64
+    FLAGS_BYTES = 256
+
+    def __init__(self, world: int, rank: int, group, device, regions: dict, timeout_s: float = 5.0):
+        if world > self.MAX_RANKS:
+            raise ValueError(f"at most {self.MAX_RANKS} ranks")
+        self.world, self.rank, self.device = world, rank, torch.device(device)
+        self.timeout_ns = int(timeout_s * 1e9)
+        lib = _lib.load()
+        self.offsets, off = {}, self.FLAGS_BYTES
+        for name, nbytes in regions.items():
+            self.offsets[name] = off
+            off += (nbytes + 255) // 256 * 256
+        self.bytes = off
+        ptr, handle = ctypes.c_void_p(), (ctypes.c_char * self.HANDLE)()
+        with torch.cuda.device(self.device):
+            _lib.check(lib.h3_ipc_alloc(self.bytes, ctypes.byref(ptr), handle), "h3_ipc_alloc")
+        self.own = ptr.value
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.bases, self.opened = [], []
+        with torch.cuda.device(self.device):
+            for p in range(world):
+                if p == rank:
+                    self.bases.append(self.own)
+                    continue
+                peer = ctypes.c_void_p()
+                buf = (ctypes.c_char * self.HANDLE).from_buffer_copy(handles[p])
+                _lib.check(lib.h3_ipc_open(buf, ctypes.byref(peer)), "h3_ipc_open")
+                self.bases.append(peer.value)
+                self.opened.append(peer.value)
+        self.peer_flags = (ctypes.c_void_p * world)(*self.bases)
+        self.epoch = torch.zeros(self.SLOTS, dtype=torch.int64, device=self.device)
+        dist.barrier(group=group)
+
+    def local(self, name: str, shape) -> torch.Tensor:
+        """This rank's region as a BF16 tensor of ``shape``."""
+        n = math.prod(shape)
+        t = torch.as_tensor(_CudaBytes(self.own + self.offsets[name], 2 * n), device=self.device)
+        return t.view(torch.bfloat16).view(*shape)
+
+    def peer_desc(self, p: int, name: str, shape, elem_offset: int = 0) -> _lib.H3Tensor:
+        """Descriptor of a contiguous BF16 block inside rank p's region (as mapped here)."""
+        d = _lib.H3Tensor()
+        d.data = self.bases[p] + self.offsets[name] + 2 * elem_offset
+        stride = 1
+        for i in reversed(range(len(shape))):
+            d.shape[i] = shape[i]
+            d.strides[i] = stride
+            stride *= shape[i]
+        d.ndim, d.dtype = len(shape), 0
+        return d
+
+    def signal(self, slot: int, stream: int) -> None:
+        _lib.CALLS["n"] += 1
+        _lib.check(_lib.load().h3_exchange_signal(self.peer_flags, ctypes.c_void_p(self.epoch.data_ptr()), slot,
+                                                  self.rank, self.world, stream), "h3_exchange_signal")
+
+    def wait(self, slot: int, stream: int) -> None:
+        _lib.CALLS["n"] += 1
+        _lib.check(_lib.load().h3_exchange_wait(ctypes.c_void_p(self.own), ctypes.c_void_p(self.epoch.data_ptr()),
+                                                slot, self.rank, self.world, self.timeout_ns, stream),
+                   "h3_exchange_wait")
+
+    def close(self) -> None:
+        lib = _lib.load()
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize(self.device)
+            for p in self.opened:
+                lib.h3_ipc_close(ctypes.c_void_p(p))
+            self.opened = []
+            if self.own:
+                lib.h3_ipc_free(ctypes.c_void_p(self.own))
+                self.own = 0
+
+
 class SequenceParallel:
+    SLOT_QKV, SLOT_OUT = 0, 1
+
     def __init__(self, world: int, rank: int, group, valid_tokens: int, local_tokens: int, heads: int,
-                 head_dim: int, device, kernels: Kernels | None = None, groups: int = 1):
+                 head_dim: int, device, kernels: Kernels | None = None, groups: int = 1,
+                 exchange: str | None = None):
         if heads % world != 0:
             # same constraint as the reference (patches/InfiniLM.patch:717-721)
             raise ValueError("heads must be divisible by the sequence-parallel size")
@@ -93,15 +198,30 @@ class SequenceParallel:
         self.device = torch.device(device)
         e = dict(device=device, dtype=torch.bfloat16)
         w, t, d = world, local_tokens, head_dim
-        self.send = [[torch.empty(w, t, hs, d, **e) for _ in range(3)] for hs in self.group_heads]
-        self.recv = [[torch.empty(w, t, hs, d, **e) for _ in range(3)] for hs in self.group_heads]
+        cuda = self.device.type == "cuda"
+        self.exchange = exchange or ("p2p" if cuda else "collective")
+        if self.exchange not in ("p2p", "collective"):
+            raise ValueError("exchange must be 'p2p' or 'collective'")
         self.attn = [torch.empty(w * t, hs, d, **e) for hs in self.group_heads]
-        self.back = [torch.empty(w, t, hs, d, **e) for hs in self.group_heads]
         self.qkv = torch.empty(t * 3 * w * max(self.group_heads) * d, **e)
         self.out = torch.empty(t, w, self.heads_local, d, **e)
-        cuda = self.device.type == "cuda"
         self.side = torch.cuda.Stream(self.device) if cuda else None
         self._weights = {}
+        self.peers = None
+        if self.exchange == "p2p":
+            if len(self.group_heads) != 1:
+                raise ValueError("the peer-to-peer exchange runs the heads as one group")
+            hs = self.group_heads[0]
+            block = w * t * hs * d * 2
+            self.peers = PeerExchange(world, rank, group, self.device,
+                                      {"q": block, "k": block, "v": block, "back": block})
+            self.recv_p2p = [self.peers.local(n, (w, t, hs, d)) for n in ("q", "k", "v")]
+            self.back_p2p = self.peers.local("back", (w, t, hs, d))
+            self.rows = torch.arange(t, dtype=torch.int64, device=self.device)
+        else:
+            self.send = [[torch.empty(w, t, hs, d, **e) for _ in range(3)] for hs in self.group_heads]
+            self.recv = [[torch.empty(w, t, hs, d, **e) for _ in range(3)] for hs in self.group_heads]
+            self.back = [torch.empty(w, t, hs, d, **e) for hs in self.group_heads]
 
     # -- weight layout --------------------------------------------------------
     def group_weights(self, w_qkv: torch.Tensor) -> list[torch.Tensor]:
@@ -139,11 +259,56 @@ class SequenceParallel:
         for o, i in zip(outs, ins):
             dist.all_to_all_single(o, i, group=self.group)
 
+    def close(self) -> None:
+        if self.peers is not None:
+            self.peers.close()
+            self.peers = None
+
+    # -- peer-to-peer exchange (GPU) --------------------------------------------
+    def _attention_p2p(self, normalized, w_qkv, norm_q, norm_k, cos, sin, qk_eps):
+        from . import ops
+        w, t, d, hl, r = self.world, self.tokens, self.head_dim, self.heads_local, self.rank
+        px = self.peers
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        qkv = self.qkv[:t * 3 * w * hl * d].view(t, 3 * w * hl * d)
+        self.kernels.linear(qkv, normalized, w_qkv)
+        parts = qkv.view(t, 3, w, hl, d)
+        cos_d, sin_d = _lib.desc(cos), _lib.desc(sin)
+        wq, wk = _lib.desc(norm_q), _lib.desc(norm_k)
+        rows = _lib.desc(self.rows)
+        # tokens -> heads: block p (heads p*Hl..) of my tokens goes to slot r of rank p
+        for p in range(w):
+            shape4 = (t, 1, hl, d)
+            _lib.call("h3_qk_norm_rope", px.peer_desc(p, "q", shape4, r * t * hl * d),
+                      _lib.desc(parts[:, 0, p].unsqueeze(1)), wq, cos_d, sin_d, float(qk_eps), stream)
+            _lib.call("h3_qk_norm_rope", px.peer_desc(p, "k", shape4, r * t * hl * d),
+                      _lib.desc(parts[:, 1, p].unsqueeze(1)), wk, cos_d, sin_d, float(qk_eps), stream)
+            _lib.call("h3_gather_rows", px.peer_desc(p, "v", (t, hl * d), r * t * hl * d),
+                      _lib.desc(parts[:, 2, p].flatten(1)), rows, stream)
+        px.signal(self.SLOT_QKV, stream)
+        px.wait(self.SLOT_QKV, stream)
+        q = self.recv_p2p[0].view(1, w * t, hl, d)
+        kk = self.recv_p2p[1].view(1, w * t, hl, d)[:, :self.valid]
+        v = self.recv_p2p[2].view(1, w * t, hl, d)[:, :self.valid]
+        attn = self.attn[0]
+        self.kernels.mha(attn.unsqueeze(0), q, kk, v, 1.0 / math.sqrt(d))
+        # heads -> tokens: rows of rank q's tokens go back to slot r of rank q
+        flat = attn.view(w * t, hl * d)
+        for q_rank in range(w):
+            _lib.call("h3_gather_rows", px.peer_desc(q_rank, "back", (t, hl * d), r * t * hl * d),
+                      _lib.desc(flat[q_rank * t:(q_rank + 1) * t]), rows, stream)
+        px.signal(self.SLOT_OUT, stream)
+        px.wait(self.SLOT_OUT, stream)
+        self.kernels.copy(self.out, self.back_p2p.permute(1, 0, 2, 3))
+        return self.out.view(t, w * hl * d)
+
     # -- the exchange -----------------------------------------------------------
     def attention(self, normalized: torch.Tensor, w_qkv: torch.Tensor, norm_q, norm_k, cos, sin,
                   qk_eps: float) -> torch.Tensor:
         """normalized [T, Hd] tokens of this rank -> attention output [T, H*D] of
         the same tokens (all heads, head-major), before the output projection."""
+        if self.exchange == "p2p":
+            return self._attention_p2p(normalized, w_qkv, norm_q, norm_k, cos, sin, qk_eps)
         k = self.kernels
         w, t, d, hl = self.world, self.tokens, self.head_dim, self.heads_local
         compute = torch.cuda.current_stream(self.device) if self.side is not None else None

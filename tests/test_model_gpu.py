@@ -20,7 +20,9 @@ def h3():
 
 
 @pytest.mark.parametrize("M,K,N,xdt,bias", [(200, 96, 300, torch.float32, True), (1, 256, 512, torch.float32, True),
-                                            (333, 5120, 96, torch.bfloat16, True), (64, 32, 130, torch.float32, False)])
+                                            (333, 5120, 96, torch.bfloat16, True), (64, 32, 130, torch.float32, False),
+                                            (1, 5120, 5120, torch.float32, True), (8, 77, 33, torch.bfloat16, False),
+                                            (9, 64, 70, torch.float32, True)])
 def test_linear_f32(h3, M, K, N, xdt, bias):
     torch.manual_seed(M + K + N)
     x = torch.randn(M, K).to(xdt)

@@ -53,7 +53,9 @@ def _worker(rank, port, path):
     local[:rows.shape[0]] = rows
     out = step.forward(local.to(f"cuda:{rank}")).cpu()
     torch.save(out, f"{path}.{rank}")
+    assert step.sp.exchange == "p2p"
     dist.barrier()
+    step.close()
     dist.destroy_process_group()
 
 
@@ -83,7 +85,9 @@ def _model_worker(rank, port, path):
     inputs = packed_inputs(cfg, video_grid=(2, 6, 10), audio_tokens=13, text_tokens=30, seed=2)
     video, audio = model(**{k: v.to(f"cuda:{rank}") for k, v in inputs.items()})
     torch.save((video.cpu(), audio.cpu()), f"{path}.{rank}")
+    torch.cuda.synchronize()
     dist.barrier()
+    model.close()
     dist.destroy_process_group()
 
 
