@@ -291,23 +291,25 @@ struct HeadArgs {
     const __nv_bfloat16 *cos, *sin;
     int64_t cs0, cs1, ss0, ss1;
     int64_t T, P, Hs;
-    FastDiv div_ph, div_hs;        // by P*Hs and by Hs
+    FastDiv div_chunks, div_hs;    // by the head-row chunks per token and by Hs
+    uint32_t chunks;               // ceil(P*Hs / HEAD_ROWS_PER_HW)
     int half;                      // rotated pairs (48 or 64); 0 = no rotation
     float eps;
 };
 
 #ifndef H3_HEAD_ROWS
-#define H3_HEAD_ROWS 4
+#define H3_HEAD_ROWS 8
 #endif
 #ifndef H3_HEAD_MINB
 #define H3_HEAD_MINB 1
 #endif
 constexpr int HEAD_THREADS = 128;                                      // 8 half-warps
 constexpr int HEAD_ROWS_PER_HW = H3_HEAD_ROWS;                         // rows in flight per half-warp
-constexpr int HEAD_ROWS_PER_CTA = (HEAD_THREADS / 16) * HEAD_ROWS_PER_HW;
 
-// Flat head rows r = (t * P + p) * Hs + h; a CTA takes HEAD_ROWS_PER_CTA
-// consecutive rows, each half-warp HEAD_ROWS_PER_HW of them (loads first).
+// A half-warp task is a chunk of up to HEAD_ROWS_PER_HW consecutive head rows
+// ph = p * Hs + h of one token t: the token's cos/sin are loaded once per task,
+// and all the chunk's rows are loaded before the first is used, so a half-warp
+// keeps HEAD_ROWS_PER_HW x 256 B of q/k in flight.
 template <bool NORM, bool VEC>
 __global__ void __launch_bounds__(HEAD_THREADS, H3_HEAD_MINB) head_kernel(HeadArgs a) {
     const int lane = threadIdx.x & 31;
@@ -315,30 +317,31 @@ __global__ void __launch_bounds__(HEAD_THREADS, H3_HEAD_MINB) head_kernel(HeadAr
     const int hw_base = lane & 16;
     const int hw = threadIdx.x >> 4;             // half-warp index in the CTA
     const uint32_t PH = (uint32_t)(a.P * a.Hs), Hs = (uint32_t)a.Hs;
-    const uint32_t rows = (uint32_t)a.T * PH;
     const int d = a.half >> 3;                   // lanes per rotated half
     const int partner = hl < d ? hl + d : (hl < 2 * d ? hl - d : hl);
     const bool rot_lane = a.half > 0 && hl < 2 * d;
 
-    uint4 xv[HEAD_ROWS_PER_HW], cv[HEAD_ROWS_PER_HW], sv[HEAD_ROWS_PER_HW];
-    uint32_t rr[HEAD_ROWS_PER_HW], tt[HEAD_ROWS_PER_HW], pp[HEAD_ROWS_PER_HW], hh[HEAD_ROWS_PER_HW];
+    const uint32_t task = blockIdx.x * (uint32_t)(HEAD_THREADS / 16) + hw;
+    const uint32_t t = a.div_chunks.div(task), c = task - t * a.chunks;
+    const bool task_ok = t < (uint32_t)a.T;
+    uint4 cv = make_uint4(0, 0, 0, 0), sv = make_uint4(0, 0, 0, 0);
+    if (task_ok && rot_lane) {
+        const int j = 8 * (hl < d ? hl : hl - d);
+        cv = load8p<VEC>(a.cos + t * a.cs0 + j * a.cs1, a.cs1, 0, 8);
+        sv = load8p<VEC>(a.sin + t * a.ss0 + j * a.ss1, a.ss1, 0, 8);
+    }
+    uint4 xv[HEAD_ROWS_PER_HW];
+    uint32_t pp[HEAD_ROWS_PER_HW], hh[HEAD_ROWS_PER_HW];
+    bool ok[HEAD_ROWS_PER_HW];
 #pragma unroll
     for (int u = 0; u < HEAD_ROWS_PER_HW; ++u) {
-        const uint32_t r = blockIdx.x * (uint32_t)HEAD_ROWS_PER_CTA + u * (HEAD_THREADS / 16) + hw;
-        rr[u] = r;
-        xv[u] = cv[u] = sv[u] = make_uint4(0, 0, 0, 0);
-        const uint32_t t = a.div_ph.div(r), ph = r - t * PH, p = a.div_hs.div(ph), h = ph - p * Hs;
-        tt[u] = t;
+        const uint32_t ph = c * (uint32_t)HEAD_ROWS_PER_HW + u;
+        const uint32_t p = a.div_hs.div(ph), h = ph - p * Hs;
         pp[u] = p;
         hh[u] = h;
-        if (r < rows) {
-            xv[u] = load8p<VEC>(a.x + t * a.xs[0] + p * a.xs[1] + h * a.xs[2], a.xs[3], 8 * hl, 128);
-            if (rot_lane) {
-                const int j = 8 * (hl < d ? hl : hl - d);
-                cv[u] = load8p<VEC>(a.cos + t * a.cs0 + j * a.cs1, a.cs1, 0, 8);
-                sv[u] = load8p<VEC>(a.sin + t * a.ss0 + j * a.ss1, a.ss1, 0, 8);
-            }
-        }
+        ok[u] = task_ok && ph < PH;
+        xv[u] = make_uint4(0, 0, 0, 0);
+        if (ok[u]) xv[u] = load8p<VEC>(a.x + t * a.xs[0] + p * a.xs[1] + h * a.xs[2], a.xs[3], 8 * hl, 128);
     }
     uint4 w = make_uint4(0, 0, 0, 0);
     if (NORM) {
@@ -382,12 +385,12 @@ __global__ void __launch_bounds__(HEAD_THREADS, H3_HEAD_MINB) head_kernel(HeadAr
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     const uint32_t other = first ? bneg2(w32(pv, i)) : w32(pv, i);
-                    w32(o, i) = badd2(bmul2(w32(v, i), w32(cv[u], i)), bmul2(other, w32(sv[u], i)));
+                    w32(o, i) = badd2(bmul2(w32(v, i), w32(cv, i)), bmul2(other, w32(sv, i)));
                 }
             }
         }
-        if (rr[u] < rows)
-            store8p<VEC>(a.out + tt[u] * a.os[0] + pp[u] * a.os[1] + hh[u] * a.os[2], a.os[3], 8 * hl, 128, o);
+        if (ok[u])
+            store8p<VEC>(a.out + t * a.os[0] + pp[u] * a.os[1] + hh[u] * a.os[2], a.os[3], 8 * hl, 128, o);
     }
 }
 
@@ -654,7 +657,8 @@ static int head_launch(const h3_tensor *out, const h3_tensor *x, const h3_tensor
     a.ss0 = sin->strides[0]; a.ss1 = sin->strides[1];
     a.T = shp[0]; a.P = shp[1]; a.Hs = shp[2];
     if (a.P * a.Hs <= 0 || a.P * a.Hs > 0x7fffffffLL) return a.T == 0 || a.P * a.Hs == 0 ? H3_OK : H3_ERR_UNSUPPORTED;
-    a.div_ph = FastDiv::make((uint32_t)(a.P * a.Hs));
+    a.chunks = (uint32_t)((a.P * a.Hs + HEAD_ROWS_PER_HW - 1) / HEAD_ROWS_PER_HW);
+    a.div_chunks = FastDiv::make(a.chunks);
     a.div_hs = FastDiv::make((uint32_t)a.Hs);
     a.half = (int)cos->shape[1];
     a.eps = eps;
@@ -664,8 +668,9 @@ static int head_launch(const h3_tensor *out, const h3_tensor *x, const h3_tensor
                aligned16(out->data) && aligned16(cos->data) && aligned16(sin->data);
     for (int i = 0; i < 3; ++i) vec = vec && (xs[i] % 8 == 0) && (os[i] % 8 == 0);
     vec = vec && a.cs0 % 8 == 0 && a.ss0 % 8 == 0;
-    if (rows > 0x7fffffffLL) return H3_ERR_UNSUPPORTED;
-    const unsigned g = (unsigned)((rows + HEAD_ROWS_PER_CTA - 1) / HEAD_ROWS_PER_CTA);
+    const int64_t tasks = a.T * (int64_t)a.chunks;
+    if (rows > 0x7fffffffLL || tasks > 0x7fffffffLL) return H3_ERR_UNSUPPORTED;
+    const unsigned g = (unsigned)((tasks + HEAD_THREADS / 16 - 1) / (HEAD_THREADS / 16));
     if (norm) {
         if (vec) head_kernel<true, true><<<g, HEAD_THREADS, 0, stream>>>(a);
         else head_kernel<true, false><<<g, HEAD_THREADS, 0, stream>>>(a);
