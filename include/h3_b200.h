@@ -202,6 +202,17 @@ int h3_silu(const h3_tensor *y, const h3_tensor *x, void *stream);
 
 /* ---------------- peer-memory exchange (sequence parallelism) ---------------- */
 
+/* The q/k RMSNorm + RoPE of h3_qk_norm_rope for every destination block in one
+ * launch: x [T, n, Hs, 128] (the head blocks of the QKV output), outs[p] (an
+ * array of n descriptors, each [T, Hs, 128], same strides; typically slot r of
+ * rank p's receive buffer, mapped from a peer) receives block p.  n <= 8. */
+int h3_qk_norm_rope_multi(const h3_tensor *outs, int32_t n, const h3_tensor *x, const h3_tensor *weight,
+                          const h3_tensor *cos, const h3_tensor *sin, float eps, void *stream);
+
+/* dsts[b] [R, C] = src[b] for the n blocks of src [n, R, C] (strided, inner stride 1),
+ * BF16 or F32, one launch; n <= 8.  The v and attention-output legs of the exchange. */
+int h3_copy_blocks(const h3_tensor *dsts, int32_t n, const h3_tensor *src, void *stream);
+
 /* Persistent buffers a peer process can map: cudaMalloc of `bytes` (zeroed) and
  * its CUDA IPC handle (H3_IPC_HANDLE_BYTES bytes written to `handle`).  Allocated
  * once at set-up, freed with h3_ipc_free; no other entry point allocates. */

@@ -69,6 +69,8 @@ SIGNATURES = {
     "h3_gather_rows": [P, P, P, _V],
     "h3_index_copy_rows": [P, P, P, _V],
     "h3_silu": [P, P, _V],
+    "h3_qk_norm_rope_multi": [P, _I, P, P, P, P, _F, _V],
+    "h3_copy_blocks": [P, _I, P, _V],
     "h3_ipc_alloc": [ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p],
     "h3_ipc_open": [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)],
     "h3_ipc_close": [ctypes.c_void_p],

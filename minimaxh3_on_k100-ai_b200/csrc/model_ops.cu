@@ -166,6 +166,34 @@ __global__ void __launch_bounds__(256) row_move_kernel(RowMoveArgs a) {
 }
 
 // ---------------------------------------------------------------------------
+// Block copy: src [n, R, C] (strided) -> dst[b] [R, C], one launch for all n
+// blocks (the v and attention-output legs of the sequence-parallel exchange).
+// ---------------------------------------------------------------------------
+struct BlockCopyArgs {
+    const uint8_t *src;
+    uint8_t *dst[H3_EXCHANGE_MAX_RANKS];
+    int64_t n, rows, row_bytes;
+    int64_t s_blk, s_row, d_row;   // bytes
+    int vec16;
+};
+
+__global__ void __launch_bounds__(256) block_copy_kernel(BlockCopyArgs a) {
+    const int64_t g = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);   // global row = b * rows + r
+    const int lane = threadIdx.x & 31;
+    if (g >= a.n * a.rows) return;
+    const int64_t b = g / a.rows, r = g - b * a.rows;
+    const uint8_t *s = a.src + b * a.s_blk + r * a.s_row;
+    uint8_t *d = a.dst[b] + r * a.d_row;
+    if (a.vec16) {
+        for (int64_t o = (int64_t)lane * 16; o < a.row_bytes; o += 32 * 16)
+            *reinterpret_cast<uint4 *>(d + o) = *reinterpret_cast<const uint4 *>(s + o);
+    } else {
+        for (int64_t o = (int64_t)lane * 2; o < a.row_bytes; o += 32 * 2)
+            *reinterpret_cast<uint16_t *>(d + o) = *reinterpret_cast<const uint16_t *>(s + o);
+    }
+}
+
+// ---------------------------------------------------------------------------
 // SiLU in fp32, written as F32 or rounded to BF16: y = x / (1 + e^-x).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) silu_kernel(const float *x, void *y, int64_t n, int y_bf16) {
@@ -269,6 +297,42 @@ extern "C" int h3_gather_rows(const h3_tensor *out, const h3_tensor *table, cons
 extern "C" int h3_index_copy_rows(const h3_tensor *out, const h3_tensor *indices, const h3_tensor *src,
                                   void *stream) {
     return row_move(out, src, indices, true, stream);
+}
+
+extern "C" int h3_copy_blocks(const h3_tensor *dsts, int32_t n, const h3_tensor *src, void *stream) {
+    if (!dsts || !src) return H3_ERR_NULL;
+    const int eb = elem_bytes(src->dtype);
+    if (eb == 0) return H3_ERR_BAD_DTYPE;
+    H3_CHECK(check_desc(src, src->dtype));
+    if (n < 1 || n > H3_EXCHANGE_MAX_RANKS) return H3_ERR_BAD_SHAPE;
+    if (src->ndim != 3 || src->shape[0] != n) return H3_ERR_BAD_SHAPE;
+    if (src->strides[2] != 1 && src->shape[2] > 1) return H3_ERR_BAD_LAYOUT;
+    const int64_t rows = src->shape[1], C = src->shape[2];
+    mops::BlockCopyArgs a;
+    for (int i = 0; i < H3_EXCHANGE_MAX_RANKS; ++i) a.dst[i] = nullptr;
+    bool aligned = aligned16(src->data);
+    for (int i = 0; i < n; ++i) {
+        const h3_tensor *d = &dsts[i];
+        if (d->dtype != src->dtype) return H3_ERR_BAD_DTYPE;
+        H3_CHECK(check_desc(d, d->dtype));
+        if (d->ndim != 2 || d->shape[0] != rows || d->shape[1] != C) return H3_ERR_BAD_SHAPE;
+        if (!dense_rows_2d(d) || d->strides[0] != dsts[0].strides[0]) return H3_ERR_BAD_LAYOUT;
+        a.dst[i] = static_cast<uint8_t *>(d->data);
+        aligned = aligned && aligned16(d->data);
+    }
+    if (rows == 0 || C == 0) return H3_OK;
+    a.src = static_cast<const uint8_t *>(src->data);
+    a.n = n;
+    a.rows = rows;
+    a.row_bytes = C * eb;
+    a.s_blk = src->strides[0] * eb;
+    a.s_row = src->strides[1] * eb;
+    a.d_row = dsts[0].strides[0] * eb;
+    a.vec16 = (aligned && a.row_bytes % 16 == 0 && a.s_blk % 16 == 0 && a.s_row % 16 == 0 && a.d_row % 16 == 0) ? 1 : 0;
+    const int64_t blocks = (n * rows + 7) / 8;
+    if (blocks > 0x7fffffff) return H3_ERR_UNSUPPORTED;
+    mops::block_copy_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(a);
+    return launch_status();
 }
 
 extern "C" int h3_silu(const h3_tensor *y, const h3_tensor *x, void *stream) {

@@ -286,6 +286,8 @@ struct HeadArgs {
     int64_t xs[4];                 // [T, P, Hs, D] strides
     __nv_bfloat16 *out;
     int64_t os[4];
+    __nv_bfloat16 *outs[H3_EXCHANGE_MAX_RANKS];  // per-block outputs (nouts > 0): block p at outs[p]
+    int nouts;
     const __nv_bfloat16 *weight;   // [128] (norm only)
     int64_t wsc;
     const __nv_bfloat16 *cos, *sin;
@@ -389,8 +391,11 @@ __global__ void __launch_bounds__(HEAD_THREADS, H3_HEAD_MINB) head_kernel(HeadAr
                 }
             }
         }
-        if (ok[u])
-            store8p<VEC>(a.out + t * a.os[0] + pp[u] * a.os[1] + hh[u] * a.os[2], a.os[3], 8 * hl, 128, o);
+        if (ok[u]) {
+            __nv_bfloat16 *dst = a.nouts > 0 ? a.outs[pp[u]] + t * a.os[0] + hh[u] * a.os[2]
+                                             : a.out + t * a.os[0] + pp[u] * a.os[1] + hh[u] * a.os[2];
+            store8p<VEC>(dst, a.os[3], 8 * hl, 128, o);
+        }
     }
 }
 
@@ -635,19 +640,29 @@ extern "C" int h3_gated_residual_rms_modulate(const h3_tensor *residual, const h
 }
 
 static int head_launch(const h3_tensor *out, const h3_tensor *x, const h3_tensor *weight,
-                       const h3_tensor *cos, const h3_tensor *sin, float eps, bool norm, cudaStream_t stream) {
-    // x/out are [T, P, Hs, 128] (4-D) or [S, H, 128] (3-D, seen as P = 1)
+                       const h3_tensor *cos, const h3_tensor *sin, float eps, bool norm, cudaStream_t stream,
+                       const h3_tensor *outs = nullptr, int nouts = 0) {
+    // x/out are [T, P, Hs, 128] (4-D) or [S, H, 128] (3-D, seen as P = 1); with nouts > 0,
+    // x is [T, nouts, Hs, 128] and block p goes to outs[p], each [T, Hs, 128]
     HeadArgs a;
+    a.nouts = nouts;
+    for (int i = 0; i < H3_EXCHANGE_MAX_RANKS; ++i) a.outs[i] = nullptr;
     int64_t shp[4], xs[4], os[4];
     if (x->ndim == 4) {
-        for (int i = 0; i < 4; ++i) { shp[i] = x->shape[i]; xs[i] = x->strides[i]; os[i] = out->strides[i]; }
+        for (int i = 0; i < 4; ++i) { shp[i] = x->shape[i]; xs[i] = x->strides[i]; os[i] = out ? out->strides[i] : 0; }
     } else {
         shp[0] = x->shape[0]; shp[1] = 1; shp[2] = x->shape[1]; shp[3] = x->shape[2];
         xs[0] = x->strides[0]; xs[1] = 0; xs[2] = x->strides[1]; xs[3] = x->strides[2];
+        if (!out) return H3_ERR_NULL;
         os[0] = out->strides[0]; os[1] = 0; os[2] = out->strides[1]; os[3] = out->strides[2];
     }
+    if (nouts > 0) {
+        // per-block outputs: strides of outs[0] ([T, Hs, 128]) as (t, -, h, d)
+        os[0] = outs[0].strides[0]; os[1] = 0; os[2] = outs[0].strides[1]; os[3] = outs[0].strides[2];
+        for (int i = 0; i < nouts; ++i) a.outs[i] = static_cast<__nv_bfloat16 *>(outs[i].data);
+    }
     a.x = static_cast<const __nv_bfloat16 *>(x->data);
-    a.out = static_cast<__nv_bfloat16 *>(out->data);
+    a.out = nouts > 0 ? a.outs[0] : static_cast<__nv_bfloat16 *>(out->data);
     for (int i = 0; i < 4; ++i) { a.xs[i] = xs[i]; a.os[i] = os[i]; }
     a.weight = weight ? static_cast<const __nv_bfloat16 *>(weight->data) : nullptr;
     a.wsc = weight ? weight->strides[0] : 1;
@@ -665,7 +680,8 @@ static int head_launch(const h3_tensor *out, const h3_tensor *x, const h3_tensor
     const int64_t rows = a.T * a.P * a.Hs;
     if (rows == 0) return H3_OK;
     bool vec = xs[3] == 1 && os[3] == 1 && a.cs1 == 1 && a.ss1 == 1 && aligned16(x->data) &&
-               aligned16(out->data) && aligned16(cos->data) && aligned16(sin->data);
+               aligned16(a.out) && aligned16(cos->data) && aligned16(sin->data);
+    for (int i = 0; i < nouts; ++i) vec = vec && aligned16(a.outs[i]);
     for (int i = 0; i < 3; ++i) vec = vec && (xs[i] % 8 == 0) && (os[i] % 8 == 0);
     vec = vec && a.cs0 % 8 == 0 && a.ss0 % 8 == 0;
     const int64_t tasks = a.T * (int64_t)a.chunks;
@@ -697,6 +713,27 @@ extern "C" int h3_rope(const h3_tensor *y, const h3_tensor *x, const h3_tensor *
     H3_CHECK(check_same_shape(y, x));
     H3_CHECK(check_angles(cos, sin, x->shape[0]));
     return head_launch(y, x, nullptr, cos, sin, 0.f, false, (cudaStream_t)stream);
+}
+
+// One launch for every destination block of the sequence-parallel exchange:
+// x [T, n, Hs, 128], outs[p] [T, Hs, 128] (all the same shape and strides).
+extern "C" int h3_qk_norm_rope_multi(const h3_tensor *outs, int32_t n, const h3_tensor *x, const h3_tensor *weight,
+                                     const h3_tensor *cos, const h3_tensor *sin, float eps, void *stream) {
+    if (!outs) return H3_ERR_NULL;
+    H3_CHECK(check_bf16(x));
+    if (n < 1 || n > H3_EXCHANGE_MAX_RANKS) return H3_ERR_BAD_SHAPE;
+    if (x->ndim != 4 || x->shape[1] != n || x->shape[3] != 128) return H3_ERR_BAD_SHAPE;
+    for (int i = 0; i < n; ++i) {
+        H3_CHECK(check_bf16(&outs[i]));
+        if (outs[i].ndim != 3 || outs[i].shape[0] != x->shape[0] || outs[i].shape[1] != x->shape[2] ||
+            outs[i].shape[2] != 128)
+            return H3_ERR_BAD_SHAPE;
+        for (int j = 0; j < 3; ++j)
+            if (outs[i].strides[j] != outs[0].strides[j]) return H3_ERR_BAD_LAYOUT;
+    }
+    H3_CHECK(check_weight(weight, 128));
+    H3_CHECK(check_angles(cos, sin, x->shape[0]));
+    return head_launch(nullptr, x, weight, cos, sin, eps, true, (cudaStream_t)stream, outs, n);
 }
 
 extern "C" int h3_qk_norm_rope(const h3_tensor *out, const h3_tensor *x, const h3_tensor *weight,

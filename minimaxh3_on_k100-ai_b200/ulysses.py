@@ -217,7 +217,12 @@ class SequenceParallel:
                                       {"q": block, "k": block, "v": block, "back": block})
             self.recv_p2p = [self.peers.local(n, (w, t, hs, d)) for n in ("q", "k", "v")]
             self.back_p2p = self.peers.local("back", (w, t, hs, d))
-            self.rows = torch.arange(t, dtype=torch.int64, device=self.device)
+            # destination descriptors: slot `rank` of every rank's regions, as mapped here
+            slot = rank * t * hs * d
+            arr = lambda name, shape: (_lib.H3Tensor * w)(  # noqa: E731
+                *[self.peers.peer_desc(p, name, shape, slot) for p in range(w)])
+            self.dst_q, self.dst_k = arr("q", (t, hs, d)), arr("k", (t, hs, d))
+            self.dst_v, self.dst_back = arr("v", (t, hs * d)), arr("back", (t, hs * d))
         else:
             self.send = [[torch.empty(w, t, hs, d, **e) for _ in range(3)] for hs in self.group_heads]
             self.recv = [[torch.empty(w, t, hs, d, **e) for _ in range(3)] for hs in self.group_heads]
@@ -266,25 +271,20 @@ class SequenceParallel:
 
     # -- peer-to-peer exchange (GPU) --------------------------------------------
     def _attention_p2p(self, normalized, w_qkv, norm_q, norm_k, cos, sin, qk_eps):
-        from . import ops
-        w, t, d, hl, r = self.world, self.tokens, self.head_dim, self.heads_local, self.rank
+        w, t, d, hl = self.world, self.tokens, self.head_dim, self.heads_local
         px = self.peers
         stream = torch.cuda.current_stream(self.device).cuda_stream
         qkv = self.qkv[:t * 3 * w * hl * d].view(t, 3 * w * hl * d)
         self.kernels.linear(qkv, normalized, w_qkv)
         parts = qkv.view(t, 3, w, hl, d)
         cos_d, sin_d = _lib.desc(cos), _lib.desc(sin)
-        wq, wk = _lib.desc(norm_q), _lib.desc(norm_k)
-        rows = _lib.desc(self.rows)
-        # tokens -> heads: block p (heads p*Hl..) of my tokens goes to slot r of rank p
-        for p in range(w):
-            shape4 = (t, 1, hl, d)
-            _lib.call("h3_qk_norm_rope", px.peer_desc(p, "q", shape4, r * t * hl * d),
-                      _lib.desc(parts[:, 0, p].unsqueeze(1)), wq, cos_d, sin_d, float(qk_eps), stream)
-            _lib.call("h3_qk_norm_rope", px.peer_desc(p, "k", shape4, r * t * hl * d),
-                      _lib.desc(parts[:, 1, p].unsqueeze(1)), wk, cos_d, sin_d, float(qk_eps), stream)
-            _lib.call("h3_gather_rows", px.peer_desc(p, "v", (t, hl * d), r * t * hl * d),
-                      _lib.desc(parts[:, 2, p].flatten(1)), rows, stream)
+        # tokens -> heads: block p (heads p*Hl..) of my tokens goes to slot r of rank p,
+        # stored by the producing kernels themselves (one launch each for q, k, v)
+        _lib.call("h3_qk_norm_rope_multi", self.dst_q, w, _lib.desc(parts[:, 0]), _lib.desc(norm_q), cos_d, sin_d,
+                  float(qk_eps), stream)
+        _lib.call("h3_qk_norm_rope_multi", self.dst_k, w, _lib.desc(parts[:, 1]), _lib.desc(norm_k), cos_d, sin_d,
+                  float(qk_eps), stream)
+        _lib.call("h3_copy_blocks", self.dst_v, w, _lib.desc(parts[:, 2].permute(1, 0, 2, 3).flatten(2)), stream)
         px.signal(self.SLOT_QKV, stream)
         px.wait(self.SLOT_QKV, stream)
         q = self.recv_p2p[0].view(1, w * t, hl, d)
@@ -293,10 +293,7 @@ class SequenceParallel:
         attn = self.attn[0]
         self.kernels.mha(attn.unsqueeze(0), q, kk, v, 1.0 / math.sqrt(d))
         # heads -> tokens: rows of rank q's tokens go back to slot r of rank q
-        flat = attn.view(w * t, hl * d)
-        for q_rank in range(w):
-            _lib.call("h3_gather_rows", px.peer_desc(q_rank, "back", (t, hl * d), r * t * hl * d),
-                      _lib.desc(flat[q_rank * t:(q_rank + 1) * t]), rows, stream)
+        _lib.call("h3_copy_blocks", self.dst_back, w, _lib.desc(attn.view(w, t, hl * d)), stream)
         px.signal(self.SLOT_OUT, stream)
         px.wait(self.SLOT_OUT, stream)
         self.kernels.copy(self.out, self.back_p2p.permute(1, 0, 2, 3))
