@@ -131,6 +131,11 @@ struct RowArgs {
 };
 
 constexpr int ROW_WARPS = 4;            // rows per CTA (one warp each)
+#ifndef H3_ROW_PAIR_MAXV
+#define H3_ROW_PAIR_MAXV 2              // rows of at most this many 16-byte vectors per lane go two per warp
+                                        // (rows <= 512 elements; measured: wider rows run faster one per
+                                        // warp, e.g. K8 at [8192, 1792] 3031 -> 3360 GB/s)
+#endif
 
 // Phase 1 of a row: its input vectors into registers (for the fused residual
 // op, the residual itself, which is also written out).
@@ -511,7 +516,7 @@ static int launch_row(RowArgs &args, bool vec, cudaStream_t stream) {
     // per lane, else 1; the grid is sized from the same constant
 #define H3_ROW_LAUNCH(VEC_, V)                                                              \
     {                                                                                       \
-        constexpr int R = (V) <= 8 ? 2 : 1;                                                 \
+        constexpr int R = (V) <= H3_ROW_PAIR_MAXV ? 2 : 1;                                  \
         const int64_t blocks = (args.rows + ROW_WARPS * R - 1) / (ROW_WARPS * R);           \
         if (blocks > 0x7fffffffLL) return H3_ERR_UNSUPPORTED;                               \
         row_kernel<MODE, VEC_, V, R><<<(unsigned)blocks, ROW_WARPS * 32, 0, stream>>>(args); \
