@@ -24,6 +24,9 @@ residual add -> RMSNorm -> SwiGLU MLP -> residual add, then a final RMSNorm.
 Residual adds and biases of BF16 linears use the gated-residual kernels with a
 unit gate: bf16(x + bf16(1 * y)) = bf16(x + y).
 
+``MiniMaxH3DiffusersAdapter`` (below) gives it the reference's Diffusers-style
+surface: same forward signature, packed-input record and output record.
+
 Weights are random-init (no checkpoint in this environment); sizes follow the
 BASELINE block config (hidden 5120, 40 heads, FFN 13824) with the reference's
 patch (24 latent channels x (1,2,2) = 96), audio (32) and text (5120) widths.
@@ -263,3 +266,116 @@ def packed_inputs(cfg: H3ModelConfig, video_grid=(4, 8, 8), audio_tokens: int = 
                   timestep_indices=torch.zeros(s, dtype=torch.long), token_tags=tags, position_ids=pos,
                   video_indices=video_idx, audio_indices=audio_idx, text_indices=text_idx)
     return {k: v.to(device) for k, v in inputs.items()}
+
+
+# ---------------------------------------------------------------------------
+# Diffusers-style surface (patches/InfiniLM.patch:6536-6603, 7081-7131): the
+# packed-input record, the output record and the adapter module a Diffusers
+# pipeline calls in place of its transformer.
+# ---------------------------------------------------------------------------
+_INDEX_DTYPES = (torch.int32, torch.int64)
+
+
+@dataclass(frozen=True)
+class MiniMaxH3TransformerInputs:
+    """Packed FL2VA inputs (MiniMaxH3TransformerInputs, :6536-6586), same checks."""
+
+    video_hidden_states: torch.Tensor
+    audio_hidden_states: torch.Tensor
+    encoder_hidden_states: torch.Tensor
+    timestep: torch.Tensor
+    timestep_indices: torch.Tensor
+    token_tags: torch.Tensor
+    position_ids: torch.Tensor
+    video_indices: torch.Tensor
+    audio_indices: torch.Tensor
+    text_indices: torch.Tensor
+
+    def validate(self) -> None:
+        sequence_length = self.position_ids.shape[0]
+        if self.position_ids.ndim != 2 or self.position_ids.shape[1] != 3:
+            raise ValueError("position_ids must have shape [sequence_length, 3]")
+        if self.timestep.ndim != 1:
+            raise ValueError("timestep must have shape [num_timesteps]")
+        for name in ("timestep_indices", "token_tags"):
+            tensor = getattr(self, name)
+            if tensor.shape != (sequence_length,):
+                raise ValueError(f"{name} must have shape [{sequence_length}], got {tuple(tensor.shape)}")
+            if tensor.dtype not in _INDEX_DTYPES:
+                raise TypeError(f"{name} must use int32 or int64 indices")
+        for name in ("video_indices", "audio_indices", "text_indices"):
+            tensor = getattr(self, name)
+            if tensor.ndim != 1:
+                raise ValueError(f"{name} must be one-dimensional")
+            if tensor.dtype not in _INDEX_DTYPES:
+                raise TypeError(f"{name} must use int32 or int64 indices")
+        if not (self.position_ids.is_floating_point() or self.position_ids.dtype in _INDEX_DTYPES):
+            raise TypeError("position_ids must use a floating-point or integer dtype")
+        for name in ("video_hidden_states", "audio_hidden_states", "encoder_hidden_states"):
+            tensor = getattr(self, name)
+            if tensor.ndim != 3 or tensor.shape[0] != 1:
+                raise ValueError(f"{name} must have shape [1, tokens, channels]")
+
+
+@dataclass(frozen=True)
+class MiniMaxH3TransformerOutput:
+    sample: torch.Tensor
+    audio_sample: torch.Tensor
+
+    @property
+    def video(self) -> torch.Tensor:
+        return self.sample
+
+    @property
+    def audio(self) -> torch.Tensor:
+        return self.audio_sample
+
+
+def run_packed(model: H3Transformer, inputs: MiniMaxH3TransformerInputs) -> MiniMaxH3TransformerOutput:
+    """The runner call (MiniMaxH3TransformerRunner.__call__): validate, move the
+    inputs to the model's device with int64 indices and fp64 positions (the
+    kernels' index and angle types), run the forward."""
+    inputs.validate()
+    dev = model.device
+    idx = lambda t: t.to(dev, torch.int64)  # noqa: E731
+    video, audio = model.forward(
+        inputs.video_hidden_states.to(dev), inputs.audio_hidden_states.to(dev),
+        inputs.encoder_hidden_states.to(dev), inputs.timestep.to(dev, torch.float32),
+        idx(inputs.timestep_indices), idx(inputs.token_tags), inputs.position_ids.to(dev, torch.float64),
+        idx(inputs.video_indices), idx(inputs.audio_indices), idx(inputs.text_indices))
+    return MiniMaxH3TransformerOutput(sample=video, audio_sample=audio)
+
+
+class MiniMaxH3DiffusersAdapter(torch.nn.Module):
+    """Diffusers-style facade (MiniMaxH3DiffusersAdapter, :7081-7131) around an
+    ``H3Transformer``: same forward signature, ``return_dict`` behaviour and
+    ``dtype`` / ``config`` attributes."""
+
+    def __init__(self, model: H3Transformer, *, dtype: torch.dtype = torch.bfloat16) -> None:
+        super().__init__()
+        self.model = model
+        self._dtype = dtype
+        bc = model.cfg.block
+        from types import SimpleNamespace
+        self.config = SimpleNamespace(
+            hidden_size=bc.hidden, num_attention_heads=bc.heads, attention_head_dim=bc.head_dim,
+            ffn_hidden_size=bc.ffn, num_layers=model.cfg.blocks, num_refiner_layers=model.cfg.refiner_blocks,
+            text_dim=model.cfg.text_dim, audio_latents_dim=model.cfg.audio_dim, patch_dim=model.cfg.patch_dim,
+            freq_dim=model.cfg.time_in, norm_eps=bc.eps, qk_norm_eps=bc.qk_eps, final_norm_eps=model.cfg.final_eps)
+
+    @property
+    def dtype(self) -> torch.dtype:
+        return self._dtype
+
+    def forward(self, hidden_states, audio_hidden_states, encoder_hidden_states, timestep, timestep_indices,
+                token_tags, position_ids, video_indices, audio_indices, text_indices, attention_kwargs=None,
+                return_dict: bool = True):
+        del attention_kwargs
+        output = run_packed(self.model, MiniMaxH3TransformerInputs(
+            video_hidden_states=hidden_states, audio_hidden_states=audio_hidden_states,
+            encoder_hidden_states=encoder_hidden_states, timestep=timestep, timestep_indices=timestep_indices,
+            token_tags=token_tags, position_ids=position_ids, video_indices=video_indices,
+            audio_indices=audio_indices, text_indices=text_indices))
+        if return_dict:
+            return output
+        return output.sample, output.audio_sample

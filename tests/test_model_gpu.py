@@ -128,3 +128,24 @@ def test_model_refiner_matches_oracle(h3):
         x = O.refiner_block_forward(x, rb, cfg.block.heads, cfg.block.eps, cfg.block.qk_eps)
     ref = O.rms_norm(x, weights["refiner_norm"], cfg.final_eps)
     assert O.max_abs_rel(out, ref) <= 1e-2
+
+
+def test_diffusers_adapter_equals_model_forward(h3):
+    """The Diffusers-style facade (int32 indices, integer positions, CPU inputs)
+    returns exactly the model forward's outputs, as a record or a tuple."""
+    from h3b200.model import H3Transformer, MiniMaxH3DiffusersAdapter, packed_inputs
+    cfg = _small_config(h3)
+    model = H3Transformer(cfg, DEV, seed=6)
+    inputs = packed_inputs(cfg, video_grid=(2, 4, 4), audio_tokens=8, text_tokens=12, seed=1)
+    video, audio = model(**{k: v.to(DEV) for k, v in inputs.items()})
+    adapter = MiniMaxH3DiffusersAdapter(model)
+    kwargs = dict(hidden_states=inputs["video"], audio_hidden_states=inputs["audio"],
+                  encoder_hidden_states=inputs["text"], timestep=inputs["timestep"],
+                  timestep_indices=inputs["timestep_indices"].int(), token_tags=inputs["token_tags"].int(),
+                  position_ids=inputs["position_ids"].long(), video_indices=inputs["video_indices"].int(),
+                  audio_indices=inputs["audio_indices"].int(), text_indices=inputs["text_indices"].int())
+    out = adapter(**kwargs)
+    assert torch.equal(out.sample, video) and torch.equal(out.audio, audio)
+    v2, a2 = adapter(**kwargs, return_dict=False)
+    assert torch.equal(v2, video) and torch.equal(a2, audio)
+    assert adapter.dtype == torch.bfloat16 and adapter.config.hidden_size == cfg.block.hidden
