@@ -23,6 +23,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import torch
@@ -84,7 +85,9 @@ class ClockSampler:
 
     def __init__(self, n_gpus: int = 1):
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+        # raw samples go to H3_CLOCK_LOG_DIR when set (kept for inspection), else a temp dir
+        log_dir = os.environ.get("H3_CLOCK_LOG_DIR") or tempfile.gettempdir()
+        self.path = os.path.join(log_dir, f"clocks_{os.getpid()}.csv")
         # the physical GPUs this job runs on (rank i uses visible device i)
         visible = os.environ.get("CUDA_VISIBLE_DEVICES")
         ids = visible.split(",")[:n_gpus] if visible else [str(i) for i in range(n_gpus)]

@@ -12,11 +12,10 @@ torch baselines are kept, never a kernel output.
 
 Every fixture is generated on the CPU with ``torch.manual_seed`` exactly as the
 reference harness seeds it (``bench_h3_ops.py:286,292``), at small sizes so the
-files stay small.  The reference tree is read from ``H3_REFERENCE_ROOT``
-(default: the mounted read-only checkout); it is needed only to regenerate the
-fixtures, never at test time.
+files stay small.  The reference tree is read from ``H3_REFERENCE_ROOT`` (the read-only
+checkout); it is needed only to regenerate the fixtures, never at test time.
 
-Run:  python tests/golden/make_golden.py
+Run:  H3_REFERENCE_ROOT=<reference checkout> python tests/golden/make_golden.py
 """
 from __future__ import annotations
 
@@ -79,7 +78,10 @@ class _Cfg:
 
 
 def main() -> int:
-    root = Path(os.environ.get("H3_REFERENCE_ROOT", "/root/reference"))
+    if "H3_REFERENCE_ROOT" not in os.environ:
+        print("set H3_REFERENCE_ROOT to the reference checkout")
+        return 1
+    root = Path(os.environ["H3_REFERENCE_ROOT"])
     if not (root / "tools" / "bench_h3_ops.py").exists():
         print(f"reference tree not found under {root}")
         return 1
