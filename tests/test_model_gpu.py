@@ -149,3 +149,21 @@ def test_diffusers_adapter_equals_model_forward(h3):
     v2, a2 = adapter(**kwargs, return_dict=False)
     assert torch.equal(v2, video) and torch.equal(a2, audio)
     assert adapter.dtype == torch.bfloat16 and adapter.config.hidden_size == cfg.block.hidden
+
+
+def test_model_forward_other_time_embedding_widths(h3):
+    """time_embed_hidden_size and time_embed_dim differ from hidden (the reference's
+    defaults are 5376 and 2688 at hidden 5376): the AdaLN and output-norm
+    projections read the narrower time embedding."""
+    from h3b200.block import BlockConfig
+    from h3b200.model import H3ModelConfig, H3Transformer, packed_inputs
+    cfg = H3ModelConfig(block=BlockConfig(hidden=256, heads=2, ffn=512), blocks=1, refiner_blocks=1,
+                        text_dim=192, time_hidden=384, time_embed_dim=128)
+    model = H3Transformer(cfg, DEV, seed=8)
+    assert model.stack.weights[0].w_adaln.shape == (18 * 256, 128)
+    inputs = packed_inputs(cfg, video_grid=(1, 4, 6), audio_tokens=3, text_tokens=9, seed=4)
+    video, audio = model(**{k: v.to(DEV) for k, v in inputs.items()})
+    weights, blocks = _oracle_weights(model)
+    ref_v, ref_a = O.model_forward(inputs, weights, blocks, heads=2)
+    assert O.max_abs_rel(video.cpu(), ref_v) <= 2e-2
+    assert O.max_abs_rel(audio.cpu(), ref_a) <= 2e-2
