@@ -45,6 +45,8 @@ def parse():
     p.add_argument("--blocks", type=int, default=40)
     p.add_argument("--no-graph", action="store_true", help="eager launches instead of one CUDA graph per step")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--parallel", choices=["sp", "tp"], default="sp",
+                   help="multi-GPU step: sp = Ulysses sequence parallelism (default), tp = tensor parallelism")
     p.add_argument("--workload", choices=["step", "attention", "pointwise", "gemm"], default="step",
                    help="step: BASELINE config 5 (default, the headline); attention: config 2; "
                         "pointwise: config 1 op set; gemm: the block's four projections at config 3")
@@ -70,7 +72,8 @@ def workload_config(args, world):
         "blocks": args.blocks,
         "global_batch": 1,
         "seq_len": 18944,
-        "parallelism": f"ulysses-sp{world}" if world > 1 else "single-gpu",
+        "parallelism": (f"ulysses-sp{world}" if getattr(args, "parallel", "sp") == "sp" else f"tensor-tp{world}")
+                       if world > 1 else "single-gpu",
         "l2": "no flush needed: each step streams ~63 GB of weights, far larger than the 126 MB L2",
     }
 
@@ -191,7 +194,7 @@ def run_ours(args, rank, world, local_rank, group):
     torch.cuda.set_device(device)
     h3b200.load()
     cfg = StepConfig(blocks=args.blocks)
-    step = DiTStep(cfg, device, world=world, rank=rank, group=group, seed=0)
+    step = DiTStep(cfg, device, world=world, rank=rank, group=group, seed=0, parallel=args.parallel)
     gen = torch.Generator(device="cpu")
     gen.manual_seed(1234)
     x_full = torch.randn(cfg.tokens, cfg.block.hidden, generator=gen).bfloat16()
@@ -274,11 +277,13 @@ def run_ours(args, rank, world, local_rank, group):
     ws = step.ws
     bc = cfg.block
     from h3b200 import ops
+    tp_mode = step.parallel == "tp"
+    heads_here = bc.heads // world if tp_mode else bc.heads
     if step.sp is None:
-        qkv = ws.qkv.view(t, 3, bc.heads, bc.head_dim)
+        qkv = ws.qkv.view(t, 3, heads_here, bc.head_dim)
         attn_call = lambda: ops.mha_(ws.attn.unsqueeze(0), ws.q.unsqueeze(0), ws.k.unsqueeze(0),  # noqa: E731
                                      qkv[:, 2].unsqueeze(0), 1.0 / math.sqrt(bc.head_dim))
-        sq, sk, hh = t, cfg.tokens, bc.heads
+        sq, sk, hh = t, cfg.tokens, heads_here
     else:
         sp = step.sp
         w_, hs = world, sp.group_heads[0]
@@ -314,14 +319,19 @@ def run_ours(args, rank, world, local_rank, group):
         return g0.elapsed_time(g1) / reps
 
     w0 = step.weights[0]
-    gemm = {
-        "qkv": (time_call(lambda: ops.linear_(ws.qkv, ws.normalized, w0.w_qkv)), 2.0 * t * 3 * bc.hidden * bc.hidden),
-        "out": (time_call(lambda: ops.linear_(ws.attn_out, ws.attn.view(t, -1), w0.w_o)), 2.0 * t * bc.hidden * bc.hidden),
-        "gate_up_swiglu": (time_call(lambda: ops.linear_swiglu(ws.normalized2, w0.w_gate_up_packed, out=ws.hidden)),
-                           2.0 * t * 2 * bc.ffn * bc.hidden),
-        "down_gated_residual": (time_call(lambda: ops.linear_gated_residual(
-            ws.hidden, w0.w_down, ws.residual, ws.residual[0], out=ws.out[1])), 2.0 * t * bc.ffn * bc.hidden),
-    }
+    if tp_mode:
+        # this rank's slices; the row-parallel products go to the all-reduce buffer
+        part = step.stack.tensor_parallel(t).part
+        hdq, fr = w0.w_qkv.shape[0], w0.w_down.shape[1]
+        gemm = {
+            "qkv": (time_call(lambda: ops.linear_(ws.qkv, ws.normalized, w0.w_qkv)), 2.0 * t * hdq * bc.hidden),
+            "out": (time_call(lambda: ops.linear_(part, ws.attn.view(t, -1), w0.w_o)), 2.0 * t * bc.hidden * hdq / 3),
+            "gate_up_swiglu": (time_call(lambda: ops.linear_swiglu(ws.normalized2, w0.w_gate_up_packed,
+                                                                   out=ws.hidden)), 2.0 * t * 2 * fr * bc.hidden),
+            "down": (time_call(lambda: ops.linear_(part, ws.hidden, w0.w_down)), 2.0 * t * fr * bc.hidden),
+        }
+    else:
+        gemm = _sp_gemms(ops, ws, w0, t, bc, time_call)
 
     # max over ranks
     vals = torch.tensor([dev_s, e2e_s, attn_ms], dtype=torch.float64, device=device)
@@ -427,6 +437,19 @@ def _timed(fn, reps, stream):
     b.record(stream)
     torch.cuda.synchronize()
     return a.elapsed_time(b) / reps
+
+
+def _sp_gemms(ops, ws, w0, t, bc, time_call):
+    """The block's four projections on this rank's tokens (one GPU or sequence
+    parallelism), each timed live: {name: (ms, flop)}."""
+    return {
+        "qkv": (time_call(lambda: ops.linear_(ws.qkv, ws.normalized, w0.w_qkv)), 2.0 * t * 3 * bc.hidden * bc.hidden),
+        "out": (time_call(lambda: ops.linear_(ws.attn_out, ws.attn.view(t, -1), w0.w_o)), 2.0 * t * bc.hidden * bc.hidden),
+        "gate_up_swiglu": (time_call(lambda: ops.linear_swiglu(ws.normalized2, w0.w_gate_up_packed, out=ws.hidden)),
+                           2.0 * t * 2 * bc.ffn * bc.hidden),
+        "down_gated_residual": (time_call(lambda: ops.linear_gated_residual(
+            ws.hidden, w0.w_down, ws.residual, ws.residual[0], out=ws.out[1])), 2.0 * t * bc.ffn * bc.hidden),
+    }
 
 
 def run_gemm(args):

@@ -213,6 +213,14 @@ int h3_qk_norm_rope_multi(const h3_tensor *outs, int32_t n, const h3_tensor *x, 
  * BF16 or F32, one launch; n <= 8.  The v and attention-output legs of the exchange. */
 int h3_copy_blocks(const h3_tensor *dsts, int32_t n, const h3_tensor *src, void *stream);
 
+/* The all-reduce step of the tensor-parallel block for the n ranks' rows this rank
+ * owns: every dsts[i] [R, C] BF16 (rank i's sum buffer rows, mapped here)
+ * receives bf16(sum over p = 0..n-1 of srcs[p]) (rank p's partial rows), summed
+ * in fp32 in rank order.  Rows 16-byte aligned, C a multiple of 8.  Replaces the
+ * reference's allreduce_on_stream_ after the row-parallel projections
+ * (InfiniLM.patch:1432-1436, 1455-1459). */
+int h3_peer_reduce_rows(const h3_tensor *dsts, const h3_tensor *srcs, int32_t n, void *stream);
+
 /* Persistent buffers a peer process can map: cudaMalloc of `bytes` (zeroed) and
  * its CUDA IPC handle (H3_IPC_HANDLE_BYTES bytes written to `handle`).  Allocated
  * once at set-up, freed with h3_ipc_free; no other entry point allocates. */

@@ -71,6 +71,7 @@ SIGNATURES = {
     "h3_silu": [P, P, _V],
     "h3_qk_norm_rope_multi": [P, _I, P, P, P, P, _F, _V],
     "h3_copy_blocks": [P, _I, P, _V],
+    "h3_peer_reduce_rows": [P, P, _I, _V],
     "h3_ipc_alloc": [ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p],
     "h3_ipc_open": [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)],
     "h3_ipc_close": [ctypes.c_void_p],

@@ -22,6 +22,8 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <cuda_bf16.h>
+
 #include "h3_abi_util.h"
 #include "sm100_ptx.cuh"
 
@@ -71,6 +73,43 @@ __global__ void wait_kernel(const uint64_t *flags, const uint64_t *epoch, int sl
     if (!ok) atomicOr(&g_h3_device_error, 1u);
     __syncwarp();
     __threadfence_system();
+}
+
+// All-reduce step of the tensor-parallel block (the reference's allreduce_on_stream_
+// after the row-parallel projections, InfiniLM.patch:1432-1436, 1455-1459): this
+// rank owns rows [r0, r0 + R) of the sum; it reads those rows of every rank's
+// partial (peer loads), adds them in fp32 in rank order, rounds once to BF16 and
+// stores the result into every rank's sum buffer (peer stores).  The fixed order
+// makes the sum identical on every rank and independent of timing.
+struct ReduceArgs {
+    const __nv_bfloat16 *src[H3_EXCHANGE_MAX_RANKS];
+    __nv_bfloat16 *dst[H3_EXCHANGE_MAX_RANKS];
+    int64_t s_row, d_row;   // row strides (elements), shared by all blocks
+    int64_t rows, vec_per_row;
+    int n;
+};
+
+__global__ void __launch_bounds__(256) reduce_rows_kernel(ReduceArgs a) {
+    const int64_t total = a.rows * a.vec_per_row;
+    for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < total; i += (int64_t)gridDim.x * 256) {
+        const int64_t r = i / a.vec_per_row, c = (i - r * a.vec_per_row) * 8;
+        float acc[8] = {};
+        for (int p = 0; p < a.n; ++p) {
+            const uint4 v = *reinterpret_cast<const uint4 *>(a.src[p] + r * a.s_row + c);
+            const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&v);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float2 f = __bfloat1622float2(h[k]);
+                acc[2 * k] = __fadd_rn(acc[2 * k], f.x);
+                acc[2 * k + 1] = __fadd_rn(acc[2 * k + 1], f.y);
+            }
+        }
+        uint4 o;
+        __nv_bfloat162 *oh = reinterpret_cast<__nv_bfloat162 *>(&o);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) oh[k] = __floats2bfloat162_rn(acc[2 * k], acc[2 * k + 1]);
+        for (int p = 0; p < a.n; ++p) *reinterpret_cast<uint4 *>(a.dst[p] + r * a.d_row + c) = o;
+    }
 }
 
 }  // namespace xchg
@@ -142,6 +181,34 @@ extern "C" int h3_exchange_wait(const void *flags, const uint64_t *epoch, int32_
     if (timeout_ns == 0 || timeout_ns > 60000000000ull) return H3_ERR_UNSUPPORTED;
     xchg::wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(static_cast<const uint64_t *>(flags), epoch, slot, rank,
                                                           world, timeout_ns);
+    return launch_status();
+}
+
+extern "C" int h3_peer_reduce_rows(const h3_tensor *dsts, const h3_tensor *srcs, int32_t n, void *stream) {
+    if (!dsts || !srcs) return H3_ERR_NULL;
+    if (n < 1 || n > H3_EXCHANGE_MAX_RANKS) return H3_ERR_BAD_SHAPE;
+    const int64_t R = srcs[0].shape[0], C = srcs[0].ndim == 2 ? srcs[0].shape[1] : 0;
+    xchg::ReduceArgs a;
+    for (int i = 0; i < n; ++i) {
+        for (const h3_tensor *t : {&srcs[i], &dsts[i]}) {
+            H3_CHECK(check_bf16(t));
+            if (t->ndim != 2 || t->shape[0] != R || t->shape[1] != C) return H3_ERR_BAD_SHAPE;
+            if ((t->strides[1] != 1 && C > 1) || !aligned16(t->data) || t->strides[0] % 8 != 0) return H3_ERR_BAD_LAYOUT;
+        }
+        if (srcs[i].strides[0] != srcs[0].strides[0] || dsts[i].strides[0] != dsts[0].strides[0]) return H3_ERR_BAD_LAYOUT;
+        a.src[i] = static_cast<const __nv_bfloat16 *>(srcs[i].data);
+        a.dst[i] = static_cast<__nv_bfloat16 *>(dsts[i].data);
+    }
+    if (C % 8 != 0) return H3_ERR_BAD_SHAPE;
+    if (R == 0 || C == 0) return H3_OK;
+    a.s_row = srcs[0].strides[0];
+    a.d_row = dsts[0].strides[0];
+    a.rows = R;
+    a.vec_per_row = C / 8;
+    a.n = n;
+    const int64_t total = R * a.vec_per_row;
+    const int64_t blocks = (total + 255) / 256;
+    xchg::reduce_rows_kernel<<<(unsigned)(blocks < 4 * 148 * 8 ? blocks : 4 * 148 * 8), 256, 0, (cudaStream_t)stream>>>(a);
     return launch_status();
 }
 

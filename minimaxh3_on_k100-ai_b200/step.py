@@ -63,10 +63,13 @@ class BlockStack:
     activation buffers."""
 
     def __init__(self, bc: BlockConfig, blocks: int, device, world: int = 1, rank: int = 0, group=None,
-                 seed: int = 0, temb_dim: int | None = None):
+                 seed: int = 0, temb_dim: int | None = None, parallel: str = "sp"):
+        if parallel not in ("sp", "tp"):
+            raise ValueError("parallel must be 'sp' (Ulysses sequence parallelism) or 'tp' (tensor parallelism)")
         self.cfg = bc
         self.device = torch.device(device)
         self.world, self.rank, self.group = world, rank, group
+        self.parallel = parallel if world > 1 else "sp"
         self.weights = [random_block_weights(bc, self.device, seed=seed + 1000 * i, temb_dim=temb_dim)
                         for i in range(blocks)]
         if world > 1:
@@ -82,16 +85,30 @@ class BlockStack:
             for w in self.weights:
                 w.w_adaln = w.w_adaln[rank * n:(rank + 1) * n].contiguous()
                 w.b_adaln = w.b_adaln[rank * n:(rank + 1) * n].contiguous()
-        self._ws: dict[int, Workspace] = {}
+        if self.parallel == "tp":
+            from .tp import shard_block_weights
+            self.weights = [shard_block_weights(w, bc, world, rank) for w in self.weights]
+        self._ws: dict = {}
         self._sp: dict[tuple[int, int], SequenceParallel] = {}
+        self._tp: dict = {}
 
-    def workspace(self, tokens: int) -> Workspace:
+    def workspace(self, tokens: int):
         if tokens not in self._ws:
-            self._ws[tokens] = Workspace(tokens, self.cfg, self.device)
+            if self.parallel == "tp":
+                from .tp import TPWorkspace
+                self._ws[tokens] = TPWorkspace(tokens, self.cfg, self.world, self.device)
+            else:
+                self._ws[tokens] = Workspace(tokens, self.cfg, self.device)
         return self._ws[tokens]
 
+    def tensor_parallel(self, tokens: int):
+        if tokens not in self._tp:
+            from .tp import TensorParallel
+            self._tp[tokens] = TensorParallel(self.world, self.rank, self.group, tokens, self.cfg.hidden, self.device)
+        return self._tp[tokens]
+
     def sequence_parallel(self, valid_tokens: int, local_tokens: int) -> SequenceParallel | None:
-        if self.world == 1:
+        if self.world == 1 or self.parallel == "tp":
             return None
         key = (valid_tokens, local_tokens)
         if key not in self._sp:
@@ -120,13 +137,21 @@ class BlockStack:
         barrier that follows the last step)."""
         for sp in self._sp.values():
             sp.close()
-        self._sp = {}
+        for tp in self._tp.values():
+            tp.close()
+        self._sp, self._tp = {}, {}
 
     def run(self, h: torch.Tensor, mods: list[torch.Tensor], segments: list[Segment], cos: torch.Tensor,
             sin: torch.Tensor, valid_tokens: int) -> torch.Tensor:
         """The block loop on this rank's tokens h [T, Hd]; returns one of the two
         workspace output buffers."""
         ws = self.workspace(h.shape[0])
+        if self.parallel == "tp":
+            from .tp import tp_block_forward
+            tp = self.tensor_parallel(h.shape[0])
+            for i, w in enumerate(self.weights):
+                h = tp_block_forward(h, mods[i], segments, w, cos, sin, self.cfg, ws, tp, out=ws.out[i % 2])
+            return h
         sp = self.sequence_parallel(valid_tokens, h.shape[0])
         for i, w in enumerate(self.weights):
             h = block_forward(h, mods[i], segments, w, cos, sin, self.cfg, ws, out=ws.out[i % 2], sp=sp)
@@ -138,15 +163,21 @@ class DiTStep:
     tokens [T, Hd] on the device; ``__call__`` is the end-to-end entry point
     (host tensor in, host tensor out)."""
 
-    def __init__(self, cfg: StepConfig, device, world: int = 1, rank: int = 0, group=None, seed: int = 0):
+    def __init__(self, cfg: StepConfig, device, world: int = 1, rank: int = 0, group=None, seed: int = 0,
+                 parallel: str = "sp"):
         self.cfg = cfg
         self.device = torch.device(device)
         bc = cfg.block
         self.world, self.rank = world, rank
-        self.local, start, padded = local_rows(cfg.tokens, world, rank)
+        self.parallel = parallel if world > 1 else "sp"
+        if self.parallel == "tp":
+            # tensor parallelism: every rank runs all tokens on its slice of the weights
+            self.local, start = cfg.tokens, 0
+        else:
+            self.local, start, padded = local_rows(cfg.tokens, world, rank)
         self.start = start
         self.group = group
-        self.stack = BlockStack(bc, cfg.blocks, self.device, world, rank, group, seed)
+        self.stack = BlockStack(bc, cfg.blocks, self.device, world, rank, group, seed, parallel=self.parallel)
         self.weights = self.stack.weights
         self.time = random_time_embedder(bc.hidden, self.device, seed=seed + 7)
         # per-token tables of the local rows; padded rows reuse row 0 (:1706-1710)
