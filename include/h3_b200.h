@@ -173,6 +173,17 @@ int h3_linear_swiglu(const h3_tensor *y, const h3_tensor *x, const h3_tensor *w_
 int h3_linear_gated_residual(const h3_tensor *out, const h3_tensor *x, const h3_tensor *w,
                              const h3_tensor *residual, const h3_tensor *gate, void *stream);
 
+/* QKV projection with the q/k RMSNorm + RoPE of h3_qk_norm_rope applied in the GEMM
+ * epilogue, each head row stored straight to its destination: x [T,K], w [3*H*128, K]
+ * (rows [q | k | v], head-major), q_dsts / k_dsts / v_dsts arrays of ndst descriptors
+ * [T, hpd, 128] (same strides; H = ndst * hpd, H even), head h to destination
+ * h / hpd, slot h % hpd.  Destinations may be peers' receive buffers (the Ulysses
+ * send).  cos/sin [T, 48].  Equal bit for bit to h3_linear followed by h3_qk_norm_rope. */
+int h3_linear_qkv_norm_rope(const h3_tensor *x, const h3_tensor *w, const h3_tensor *q_dsts,
+                            const h3_tensor *k_dsts, const h3_tensor *v_dsts, int32_t ndst,
+                            const h3_tensor *norm_q, const h3_tensor *norm_k, const h3_tensor *cos,
+                            const h3_tensor *sin, float eps, void *stream);
+
 /* Reorder the [up; gate] rows of a gate_up weight [2F,K] into 128-row blocks
  * [up_0 | gate_0 | up_1 | gate_1 ...] consumed by h3_linear_swiglu. */
 int h3_pack_gate_up(const h3_tensor *dst, const h3_tensor *src, void *stream);

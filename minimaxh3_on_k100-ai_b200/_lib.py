@@ -65,6 +65,7 @@ SIGNATURES = {
     "h3_linear_swiglu": [P, P, P, _V],
     "h3_linear_gated_residual": [P, P, P, P, P, _V],
     "h3_pack_gate_up": [P, P, _V],
+    "h3_linear_qkv_norm_rope": [P, P, P, P, P, _I, P, P, P, P, _F, _V],
     "h3_linear_f32": [P, P, P, P, _V],
     "h3_gather_rows": [P, P, P, _V],
     "h3_index_copy_rows": [P, P, P, _V],

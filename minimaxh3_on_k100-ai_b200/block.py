@@ -107,12 +107,19 @@ class Workspace:
         self.qkv = torch.empty(tokens, 3 * hd, **e)
         self.q = torch.empty(tokens, cfg.heads, cfg.head_dim, **e)
         self.k = torch.empty(tokens, cfg.heads, cfg.head_dim, **e)
+        self.v = torch.empty(tokens, cfg.heads, cfg.head_dim, **e)
         self.attn = torch.empty(tokens, cfg.heads, cfg.head_dim, **e)
         self.attn_out = torch.empty(tokens, hd, **e)
         self.residual = torch.empty(tokens, hd, **e)
         self.normalized2 = torch.empty(tokens, hd, **e)
         self.hidden = torch.empty(tokens, f, **e)
         self.out = [torch.empty(tokens, hd, **e), torch.empty(tokens, hd, **e)]
+
+
+def qkv_fused(heads: int, cos: torch.Tensor) -> bool:
+    """Whether the QKV projection can carry the q/k norm + RoPE in its epilogue
+    (two heads per 256-column tile, the reference's 48 rotated pairs)."""
+    return heads % 2 == 0 and cos.shape[-1] == 48
 
 
 def _col(modulation: torch.Tensor, index: int, hidden: int, seg: Segment) -> torch.Tensor:
@@ -136,12 +143,18 @@ def block_forward(x: torch.Tensor, modulation: torch.Tensor, segments: list[Segm
         ops.h3_rms_modulate_(ws.normalized[r], x[r], w.norm1, _col(modulation, 1, hd, s),
                              _col(modulation, 0, hd, s), cfg.eps)
     if sp is None or sp.world == 1:
-        ops.linear_(ws.qkv, ws.normalized, w.w_qkv)
-        qkv = ws.qkv.view(t, 3, h, d)
-        ops.h3_qk_norm_rope_(ws.q.unsqueeze(1), qkv[:, 0].unsqueeze(1), w.norm_q, cos, sin, cfg.qk_eps)
-        ops.h3_qk_norm_rope_(ws.k.unsqueeze(1), qkv[:, 1].unsqueeze(1), w.norm_k, cos, sin, cfg.qk_eps)
-        ops.mha_(ws.attn.unsqueeze(0), ws.q.unsqueeze(0), ws.k.unsqueeze(0), qkv[:, 2].unsqueeze(0),
-                 1.0 / math.sqrt(d))
+        if qkv_fused(h, cos):
+            # one GEMM whose epilogue normalises and rotates q/k and stores q, k, v per head
+            ops.linear_qkv_norm_rope_([ws.q], [ws.k], [ws.v], ws.normalized, w.w_qkv, w.norm_q, w.norm_k,
+                                      cos, sin, cfg.qk_eps)
+            v = ws.v
+        else:
+            ops.linear_(ws.qkv, ws.normalized, w.w_qkv)
+            qkv = ws.qkv.view(t, 3, h, d)
+            ops.h3_qk_norm_rope_(ws.q.unsqueeze(1), qkv[:, 0].unsqueeze(1), w.norm_q, cos, sin, cfg.qk_eps)
+            ops.h3_qk_norm_rope_(ws.k.unsqueeze(1), qkv[:, 1].unsqueeze(1), w.norm_k, cos, sin, cfg.qk_eps)
+            v = qkv[:, 2]
+        ops.mha_(ws.attn.unsqueeze(0), ws.q.unsqueeze(0), ws.k.unsqueeze(0), v.unsqueeze(0), 1.0 / math.sqrt(d))
         attn_flat = ws.attn.view(t, hd)
     else:
         attn_flat = sp.attention(ws.normalized, w.w_qkv, w.norm_q, w.norm_k, cos, sin, cfg.qk_eps)

@@ -7,6 +7,10 @@
 //                                                     patches/InfiniLM.patch:1172-1179)
 //   y = bf16(res + bf16(gate * bf16(x W^T)))         (down-proj + h3_gated_residual,
 //                                                     patches/InfiniLM.patch:1391-1394)
+//   q, k, v = x Wqkv^T with q/k RMSNorm + RoPE        (QKV projection + h3_qk_norm_rope_,
+//             stored per head into destination         patches/InfiniLM.patch:744-839, and the
+//             buffers (local, or a peer's receive      Ulysses send of gather_sequence :895-910)
+//             buffer over NVLink)
 // The epilogues round the accumulator to BF16 first, exactly where the unfused
 // reference materialises the linear's BF16 output, then apply the pointwise op
 // with its staged rounding, so fused == unfused bit for bit.
@@ -40,7 +44,9 @@ constexpr int OFF_BAR = STAGES * STAGE_BYTES;
 constexpr int NUM_BARS = 2 * STAGES + 4;
 constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 16 + 1024;
 
-enum Epi { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_GATED_RES = 2 };
+enum Epi { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_GATED_RES = 2, EPI_QKV = 3 };
+constexpr int QKV_HALF = 48;              // rotated pairs per head (3 axes x 16 frequencies)
+constexpr int QKV_HW = QKV_HALF / 2;      // ... as packed BF16x2 words
 
 struct Params {
     int M, N, K;            // N: accumulator columns (weight rows)
@@ -51,6 +57,15 @@ struct Params {
     int64_t ldr;
     const __nv_bfloat16 *gate;
     int64_t ldg;            // 0 broadcasts one gate row
+    // EPI_QKV: accumulator column c = part * hcols + head * 128 + d (part 0/1/2 = q/k/v);
+    // head h goes to destination h / hpd, head slot h % hpd
+    int hcols, hpd;
+    __nv_bfloat16 *dst[3][H3_EXCHANGE_MAX_RANKS];
+    int64_t drow, dhead;    // destination strides: token, head (elements)
+    const __nv_bfloat16 *norm_q, *norm_k;
+    const __nv_bfloat16 *cos, *sin;
+    int64_t cs0, ss0;
+    float eps;
 };
 
 __device__ __forceinline__ void tile_coords(const Params &p, int tile, int &m, int &n) {
@@ -172,7 +187,82 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint32_t tbase = tmem + acc * BN + lane_off;
             const int row = m * BM + wq * 32 + lane;
             const bool row_ok = row < p.M;
-            if (EPI == EPI_SWIGLU) {
+            if (EPI == EPI_QKV) {
+                // the tile's 256 columns are two heads of one part; this thread owns one token
+                uint32_t cw[QKV_HW], sw[QKV_HW];
+                if (row_ok) {
+#pragma unroll
+                    for (int q = 0; q < QKV_HW / 4; ++q) {
+                        const uint4 c4 = *reinterpret_cast<const uint4 *>(p.cos + (int64_t)row * p.cs0 + 8 * q);
+                        const uint4 s4 = *reinterpret_cast<const uint4 *>(p.sin + (int64_t)row * p.ss0 + 8 * q);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            cw[4 * q + e] = w32(c4, e);
+                            sw[4 * q + e] = w32(s4, e);
+                        }
+                    }
+                }
+#pragma unroll 1
+                for (int hh = 0; hh < 2; ++hh) {
+                    const int col = n * BN + hh * 128;
+                    const int part = col / p.hcols;
+                    const int head = (col - part * p.hcols) >> 7;
+                    const int dp = head / p.hpd, hloc = head - dp * p.hpd;
+                    uint32_t xw[64];
+#pragma unroll
+                    for (int cc = 0; cc < 4; ++cc) {
+                        uint32_t v[32];
+                        tmem_ld32(tbase + hh * 128 + cc * 32, v);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 16; ++i)   // the linear's BF16 output
+                            xw[16 * cc + i] = pack2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+                    }
+                    if (!row_ok) continue;
+                    if (part < 2) {
+                        // RMSNorm over the head with the exact summation tree of the q/k
+                        // kernel (16 partial sums of 8 columns, then a xor-8/4/2/1 tree)
+                        float s16[16];
+#pragma unroll
+                        for (int l = 0; l < 16; ++l) {
+                            float sacc = 0.f;
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                const uint32_t sq = bmul2(xw[4 * l + i], xw[4 * l + i]);
+                                sacc = add_rn(sacc, blo(sq));
+                                sacc = add_rn(sacc, bhi(sq));
+                            }
+                            s16[l] = sacc;
+                        }
+#pragma unroll
+                        for (int o = 8; o > 0; o >>= 1)
+#pragma unroll
+                            for (int l = 0; l < o; ++l) s16[l] = add_rn(s16[l], s16[l + o]);
+                        const float mean = bf(__fmul_rn(s16[0], 0.0078125f));
+                        const float var = bf(add_rn(mean, p.eps));
+                        const uint32_t r2 = bsplat(bf(rsqrt_torch(var)));
+                        const __nv_bfloat16 *nw = part == 0 ? p.norm_q : p.norm_k;
+#pragma unroll
+                        for (int q = 0; q < 16; ++q) {
+                            const uint4 w4 = *reinterpret_cast<const uint4 *>(nw + 8 * q);
+#pragma unroll
+                            for (int e = 0; e < 4; ++e)
+                                xw[4 * q + e] = bmul2(bmul2(xw[4 * q + e], r2), w32(w4, e));  // bf(bf(x*r)*w)
+                        }
+                        // RoPE: y0 = bf(bf(a*c) + bf(-b*s)), y1 = bf(bf(b*c) + bf(a*s))
+#pragma unroll
+                        for (int j = 0; j < QKV_HW; ++j) {
+                            const uint32_t a = xw[j], b = xw[j + QKV_HW];
+                            xw[j] = badd2(bmul2(a, cw[j]), bmul2(bneg2(b), sw[j]));
+                            xw[j + QKV_HW] = badd2(bmul2(b, cw[j]), bmul2(a, sw[j]));
+                        }
+                    }
+                    __nv_bfloat16 *dst = p.dst[part][dp] + (int64_t)row * p.drow + (int64_t)hloc * p.dhead;
+#pragma unroll
+                    for (int q = 0; q < 16; ++q)
+                        st_global_v4(dst + 8 * q, xw[4 * q], xw[4 * q + 1], xw[4 * q + 2], xw[4 * q + 3]);
+                }
+            } else if (EPI == EPI_SWIGLU) {
                 // accumulator columns [0,128) = up, [128,256) = gate of features n*128 + c
 #pragma unroll 1
                 for (int cc = 0; cc < 4; ++cc) {
@@ -293,7 +383,7 @@ int launch_gemm(const h3_tensor *x, const h3_tensor *w, gemm::Params &p, cudaStr
     p.num_n = (p.N + gemm::BN - 1) / gemm::BN;
     p.num_tiles = p.num_m * p.num_n;
     if (p.num_tiles == 0) return H3_OK;
-    static std::atomic<bool> attr_set[3][64];
+    static std::atomic<bool> attr_set[4][64];
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return H3_ERR_UNSUPPORTED;
@@ -370,6 +460,68 @@ extern "C" int h3_linear_gated_residual(const h3_tensor *out, const h3_tensor *x
     p.gate = static_cast<const __nv_bfloat16 *>(gate->data);
     p.ldg = gate->strides[0];
     return launch_gemm<gemm::EPI_GATED_RES>(x, w, p, (cudaStream_t)stream);
+}
+
+// QKV projection with q/k RMSNorm + RoPE in the epilogue, each head row stored to
+// its destination: q_dsts/k_dsts/v_dsts are arrays of ndst descriptors [T, hpd, 128]
+// (same strides), head h of the projection goes to destination h / hpd.
+extern "C" int h3_linear_qkv_norm_rope(const h3_tensor *x, const h3_tensor *w, const h3_tensor *q_dsts,
+                                       const h3_tensor *k_dsts, const h3_tensor *v_dsts, int32_t ndst,
+                                       const h3_tensor *norm_q, const h3_tensor *norm_k, const h3_tensor *cos,
+                                       const h3_tensor *sin, float eps, void *stream) {
+    if (!q_dsts || !k_dsts || !v_dsts) return H3_ERR_NULL;
+    H3_CHECK(check_matrix(x));
+    H3_CHECK(check_matrix(w));
+    if (x->shape[1] != w->shape[1]) return H3_ERR_BAD_SHAPE;
+    if (x->shape[1] % gemm::BK != 0 || x->shape[1] == 0) return H3_ERR_UNSUPPORTED;
+    if (x->shape[0] > 0x7fffffffLL || w->shape[0] > 0x7fffffffLL) return H3_ERR_UNSUPPORTED;
+    if (ndst < 1 || ndst > H3_EXCHANGE_MAX_RANKS) return H3_ERR_BAD_SHAPE;
+    const int64_t T = x->shape[0];
+    const h3_tensor *d0 = &q_dsts[0];
+    if (d0->ndim != 3 || d0->shape[2] != 128) return H3_ERR_BAD_SHAPE;
+    const int64_t hpd = d0->shape[1], H = hpd * ndst;
+    if (hpd < 1 || w->shape[0] != 3 * H * 128) return H3_ERR_BAD_SHAPE;
+    if ((H * 128) % gemm::BN != 0) return H3_ERR_UNSUPPORTED;   // two heads per tile: H even
+    gemm::Params p{};
+    const h3_tensor *sets[3] = {q_dsts, k_dsts, v_dsts};
+    for (int part = 0; part < 3; ++part) {
+        for (int i = 0; i < ndst; ++i) {
+            const h3_tensor *d = &sets[part][i];
+            H3_CHECK(check_bf16(d));
+            if (d->ndim != 3 || d->shape[0] != T || d->shape[1] != hpd || d->shape[2] != 128) return H3_ERR_BAD_SHAPE;
+            if (d->strides[0] != d0->strides[0] || d->strides[1] != d0->strides[1] || d->strides[2] != 1)
+                return H3_ERR_BAD_LAYOUT;
+            if (!aligned16(d->data)) return H3_ERR_BAD_LAYOUT;
+            p.dst[part][i] = static_cast<__nv_bfloat16 *>(d->data);
+        }
+    }
+    if (d0->strides[0] % 8 != 0 || d0->strides[1] % 8 != 0) return H3_ERR_BAD_LAYOUT;
+    for (const h3_tensor *nw : {norm_q, norm_k}) {
+        H3_CHECK(check_bf16(nw));
+        if (nw->ndim != 1 || nw->shape[0] != 128) return H3_ERR_BAD_SHAPE;
+        if (nw->strides[0] != 1 || !aligned16(nw->data)) return H3_ERR_BAD_LAYOUT;
+    }
+    for (const h3_tensor *cs : {cos, sin}) {
+        H3_CHECK(check_bf16(cs));
+        if (cs->ndim != 2 || cs->shape[0] != T) return H3_ERR_BAD_SHAPE;
+        if (cs->shape[1] != gemm::QKV_HALF) return H3_ERR_UNSUPPORTED;
+        if (cs->strides[1] != 1 || (T > 1 && cs->strides[0] % 8 != 0) || !aligned16(cs->data)) return H3_ERR_BAD_LAYOUT;
+    }
+    p.M = (int)T;
+    p.N = (int)w->shape[0];
+    p.K = (int)x->shape[1];
+    p.hcols = (int)(H * 128);
+    p.hpd = (int)hpd;
+    p.drow = d0->strides[0];
+    p.dhead = d0->strides[1];
+    p.norm_q = static_cast<const __nv_bfloat16 *>(norm_q->data);
+    p.norm_k = static_cast<const __nv_bfloat16 *>(norm_k->data);
+    p.cos = static_cast<const __nv_bfloat16 *>(cos->data);
+    p.sin = static_cast<const __nv_bfloat16 *>(sin->data);
+    p.cs0 = cos->strides[0];
+    p.ss0 = sin->strides[0];
+    p.eps = eps;
+    return launch_gemm<gemm::EPI_QKV>(x, w, p, (cudaStream_t)stream);
 }
 
 extern "C" int h3_pack_gate_up(const h3_tensor *dst, const h3_tensor *src, void *stream) {

@@ -28,6 +28,7 @@ __all__ = [
     "h3_rope_cache", "h3_rope_cache_sectioned", "rope_powers", "timestep_embedding", "mha", "mha_",
     "linear", "linear_", "linear_swiglu", "linear_gated_residual", "pack_gate_up",
     "linear_f32", "linear_f32_", "gather_rows", "gather_rows_", "index_copy_rows_", "silu", "silu_",
+    "linear_qkv_norm_rope_",
 ]
 
 
@@ -199,6 +200,20 @@ def linear_(out, x, weight):
 def linear(x, weight):
     out = torch.empty(*x.shape[:-1], weight.shape[0], dtype=x.dtype, device=x.device)
     return linear_(out, x, weight)
+
+
+def _desc_array(ts):
+    return (_lib.H3Tensor * len(ts))(*[desc(t) for t in ts])
+
+
+def linear_qkv_norm_rope_(q_outs, k_outs, v_outs, x, weight, norm_q, norm_k, cos, sin, eps):
+    """q, k, v = x W^T with q/k RMSNorm + RoPE in the GEMM epilogue; head h goes to
+    q_outs[h // hpd][:, h % hpd] (lists of [T, hpd, 128] tensors; bitwise
+    h3_linear followed by h3_qk_norm_rope)."""
+    require_cuda(x, weight, norm_q, norm_k, cos, sin, *q_outs, *k_outs, *v_outs)
+    call("h3_linear_qkv_norm_rope", desc(_flat(x)), desc(weight), _desc_array(q_outs), _desc_array(k_outs),
+         _desc_array(v_outs), len(q_outs), desc(norm_q), desc(norm_k), desc(cos), desc(sin), float(eps),
+         stream_of(x))
 
 
 def pack_gate_up(weight):

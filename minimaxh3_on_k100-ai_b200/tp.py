@@ -32,7 +32,7 @@ import math
 import torch
 
 from . import _lib, ops
-from .block import BlockConfig, BlockWeights, Segment, _col
+from .block import BlockConfig, BlockWeights, Segment, _col, qkv_fused
 from .ulysses import PeerExchange
 
 
@@ -100,6 +100,7 @@ class TPWorkspace:
         self.qkv = torch.empty(tokens, 3 * hl * cfg.head_dim, **e)
         self.q = torch.empty(tokens, hl, cfg.head_dim, **e)
         self.k = torch.empty(tokens, hl, cfg.head_dim, **e)
+        self.v = torch.empty(tokens, hl, cfg.head_dim, **e)
         self.attn = torch.empty(tokens, hl, cfg.head_dim, **e)
         self.residual = torch.empty(tokens, cfg.hidden, **e)
         self.normalized2 = torch.empty(tokens, cfg.hidden, **e)
@@ -118,11 +119,17 @@ def tp_block_forward(x: torch.Tensor, modulation: torch.Tensor, segments: list[S
         r = slice(s.start, s.start + s.length)
         ops.h3_rms_modulate_(ws.normalized[r], x[r], w.norm1, _col(modulation, 1, hd, s),
                              _col(modulation, 0, hd, s), cfg.eps)
-    ops.linear_(ws.qkv, ws.normalized, w.w_qkv)
-    qkv = ws.qkv.view(n, 3, hl, d)
-    ops.h3_qk_norm_rope_(ws.q.unsqueeze(1), qkv[:, 0].unsqueeze(1), w.norm_q, cos, sin, cfg.qk_eps)
-    ops.h3_qk_norm_rope_(ws.k.unsqueeze(1), qkv[:, 1].unsqueeze(1), w.norm_k, cos, sin, cfg.qk_eps)
-    ops.mha_(ws.attn.unsqueeze(0), ws.q.unsqueeze(0), ws.k.unsqueeze(0), qkv[:, 2].unsqueeze(0), 1.0 / math.sqrt(d))
+    if qkv_fused(hl, cos):
+        ops.linear_qkv_norm_rope_([ws.q], [ws.k], [ws.v], ws.normalized, w.w_qkv, w.norm_q, w.norm_k, cos, sin,
+                                  cfg.qk_eps)
+        v = ws.v
+    else:
+        ops.linear_(ws.qkv, ws.normalized, w.w_qkv)
+        qkv = ws.qkv.view(n, 3, hl, d)
+        ops.h3_qk_norm_rope_(ws.q.unsqueeze(1), qkv[:, 0].unsqueeze(1), w.norm_q, cos, sin, cfg.qk_eps)
+        ops.h3_qk_norm_rope_(ws.k.unsqueeze(1), qkv[:, 1].unsqueeze(1), w.norm_k, cos, sin, cfg.qk_eps)
+        v = qkv[:, 2]
+    ops.mha_(ws.attn.unsqueeze(0), ws.q.unsqueeze(0), ws.k.unsqueeze(0), v.unsqueeze(0), 1.0 / math.sqrt(d))
     ops.linear_(tp.part, ws.attn.view(n, hl * d), w.w_o)
     o = tp.allreduce()
     for s in segments:

@@ -223,6 +223,7 @@ class SequenceParallel:
                 *[self.peers.peer_desc(p, name, shape, slot) for p in range(w)])
             self.dst_q, self.dst_k = arr("q", (t, hs, d)), arr("k", (t, hs, d))
             self.dst_v, self.dst_back = arr("v", (t, hs * d)), arr("back", (t, hs * d))
+            self.dst_v3 = arr("v", (t, hs, d))
         else:
             self.send = [[torch.empty(w, t, hs, d, **e) for _ in range(3)] for hs in self.group_heads]
             self.recv = [[torch.empty(w, t, hs, d, **e) for _ in range(3)] for hs in self.group_heads]
@@ -274,17 +275,25 @@ class SequenceParallel:
         w, t, d, hl = self.world, self.tokens, self.head_dim, self.heads_local
         px = self.peers
         stream = torch.cuda.current_stream(self.device).cuda_stream
-        qkv = self.qkv[:t * 3 * w * hl * d].view(t, 3 * w * hl * d)
-        self.kernels.linear(qkv, normalized, w_qkv)
-        parts = qkv.view(t, 3, w, hl, d)
         cos_d, sin_d = _lib.desc(cos), _lib.desc(sin)
         # tokens -> heads: block p (heads p*Hl..) of my tokens goes to slot r of rank p,
-        # stored by the producing kernels themselves (one launch each for q, k, v)
-        _lib.call("h3_qk_norm_rope_multi", self.dst_q, w, _lib.desc(parts[:, 0]), _lib.desc(norm_q), cos_d, sin_d,
-                  float(qk_eps), stream)
-        _lib.call("h3_qk_norm_rope_multi", self.dst_k, w, _lib.desc(parts[:, 1]), _lib.desc(norm_k), cos_d, sin_d,
-                  float(qk_eps), stream)
-        _lib.call("h3_copy_blocks", self.dst_v, w, _lib.desc(parts[:, 2].permute(1, 0, 2, 3).flatten(2)), stream)
+        # stored by the producing kernels themselves
+        from .block import qkv_fused
+        if qkv_fused(self.heads, cos):
+            # the QKV GEMM's epilogue normalises/rotates q and k and stores every head row
+            # into its destination rank's receive buffer (one launch for the whole send)
+            _lib.call("h3_linear_qkv_norm_rope", _lib.desc(normalized), _lib.desc(w_qkv), self.dst_q, self.dst_k,
+                      self.dst_v3, w, _lib.desc(norm_q), _lib.desc(norm_k), cos_d, sin_d, float(qk_eps), stream)
+        else:
+            qkv = self.qkv[:t * 3 * w * hl * d].view(t, 3 * w * hl * d)
+            self.kernels.linear(qkv, normalized, w_qkv)
+            parts = qkv.view(t, 3, w, hl, d)
+            _lib.call("h3_qk_norm_rope_multi", self.dst_q, w, _lib.desc(parts[:, 0]), _lib.desc(norm_q), cos_d,
+                      sin_d, float(qk_eps), stream)
+            _lib.call("h3_qk_norm_rope_multi", self.dst_k, w, _lib.desc(parts[:, 1]), _lib.desc(norm_k), cos_d,
+                      sin_d, float(qk_eps), stream)
+            _lib.call("h3_copy_blocks", self.dst_v, w, _lib.desc(parts[:, 2].permute(1, 0, 2, 3).flatten(2)),
+                      stream)
         px.signal(self.SLOT_QKV, stream)
         px.wait(self.SLOT_QKV, stream)
         q = self.recv_p2p[0].view(1, w * t, hl, d)

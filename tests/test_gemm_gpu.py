@@ -118,3 +118,33 @@ def test_bad_k_rejected(h3):
         h3.linear(x, w)
     with pytest.raises(ValueError):                               # K mismatch
         h3.linear(x, torch.zeros(32, 64, dtype=torch.bfloat16, device=DEV))
+
+
+@pytest.mark.parametrize("T,H,K,ndst", [(300, 4, 512, 1), (1000, 40, 5120, 1), (257, 8, 256, 2), (130, 10, 640, 5)])
+def test_qkv_norm_rope_epilogue_equals_unfused(T, H, K, ndst):
+    """The QKV GEMM with q/k RMSNorm + RoPE in its epilogue, each head stored to its
+    destination, equals h3_linear followed by h3_qk_norm_rope bit for bit."""
+    import h3b200
+    from h3b200 import ops
+    from oracle import h3_oracle as O
+    torch.manual_seed(T + H)
+    x = torch.randn(T, K, device="cuda").bfloat16()
+    w = (torch.randn(3 * H * 128, K, device="cuda") * K ** -0.5).bfloat16()
+    nq = (torch.randn(128, device="cuda") * 0.1 + 1).bfloat16()
+    nk = (torch.randn(128, device="cuda") * 0.1 + 1).bfloat16()
+    table = O.rotary_cache(O.grid_positions(1, 1, T)).cuda()
+    cos, sin = table[:, :48], table[:, 48:]
+    hpd = H // ndst
+    outs = [[torch.empty(T, hpd, 128, dtype=torch.bfloat16, device="cuda") for _ in range(ndst)] for _ in range(3)]
+    ops.linear_qkv_norm_rope_(outs[0], outs[1], outs[2], x, w, nq, nk, cos, sin, 1e-6)
+    qkv = ops.linear(x, w).view(T, 3, H, 128)
+    ref_q = torch.empty(T, 1, H, 128, dtype=torch.bfloat16, device="cuda")
+    ref_k = torch.empty_like(ref_q)
+    h3b200.h3_qk_norm_rope_(ref_q, qkv[:, 0].unsqueeze(1), nq, cos, sin, 1e-6)
+    h3b200.h3_qk_norm_rope_(ref_k, qkv[:, 1].unsqueeze(1), nk, cos, sin, 1e-6)
+    for p in range(ndst):
+        hs = slice(p * hpd, (p + 1) * hpd)
+        assert torch.equal(outs[0][p], ref_q[:, 0, hs]), f"q block {p}"
+        assert torch.equal(outs[1][p], ref_k[:, 0, hs]), f"k block {p}"
+        assert torch.equal(outs[2][p], qkv[:, 2, hs]), f"v block {p}"
+    assert h3b200.load().h3_device_error() == 0
