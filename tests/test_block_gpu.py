@@ -96,3 +96,9 @@ def test_step_short_stack(h3):
         h = O.block_forward(h, mods[i], _oracle_weights(w), step.cos.cpu(), step.sin.cpu(), 4, segments=segs)
     assert O.max_abs_rel(out.cpu(), h) <= 2e-2
     assert h3.load().h3_device_error() == 0
+
+
+def test_graft_entry_smoke():
+    """The smoke entry point the driver runs (one small block vs the CPU oracle)."""
+    import __graft_entry__
+    __graft_entry__.smoke()
