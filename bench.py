@@ -324,14 +324,16 @@ def run_ours(args, rank, world, local_rank, group):
         part = step.stack.tensor_parallel(t).part
         hdq, fr = w0.w_qkv.shape[0], w0.w_down.shape[1]
         gemm = {
-            "qkv": (time_call(lambda: ops.linear_(ws.qkv, ws.normalized, w0.w_qkv)), 2.0 * t * hdq * bc.hidden),
+            "qkv_norm_rope": (time_call(lambda: ops.linear_qkv_norm_rope_(
+                [ws.q], [ws.k], [ws.v], ws.normalized, w0.w_qkv, w0.norm_q, w0.norm_k, step.cos, step.sin,
+                bc.qk_eps)), 2.0 * t * hdq * bc.hidden),
             "out": (time_call(lambda: ops.linear_(part, ws.attn.view(t, -1), w0.w_o)), 2.0 * t * bc.hidden * hdq / 3),
             "gate_up_swiglu": (time_call(lambda: ops.linear_swiglu(ws.normalized2, w0.w_gate_up_packed,
                                                                    out=ws.hidden)), 2.0 * t * 2 * fr * bc.hidden),
             "down": (time_call(lambda: ops.linear_(part, ws.hidden, w0.w_down)), 2.0 * t * fr * bc.hidden),
         }
     else:
-        gemm = _sp_gemms(ops, ws, w0, t, bc, time_call)
+        gemm = _sp_gemms(ops, ws, w0, t, bc, time_call, step.cos, step.sin)
 
     # max over ranks
     vals = torch.tensor([dev_s, e2e_s, attn_ms], dtype=torch.float64, device=device)
@@ -439,11 +441,16 @@ def _timed(fn, reps, stream):
     return a.elapsed_time(b) / reps
 
 
-def _sp_gemms(ops, ws, w0, t, bc, time_call):
+def _sp_gemms(ops, ws, w0, t, bc, time_call, cos, sin):
     """The block's four projections on this rank's tokens (one GPU or sequence
-    parallelism), each timed live: {name: (ms, flop)}."""
+    parallelism), each timed live as the step launches it: {name: (ms, flop)}.
+    The QKV projection carries the q/k RMSNorm + RoPE in its epilogue (here
+    stored to local buffers)."""
     return {
-        "qkv": (time_call(lambda: ops.linear_(ws.qkv, ws.normalized, w0.w_qkv)), 2.0 * t * 3 * bc.hidden * bc.hidden),
+        "qkv_norm_rope": (time_call(lambda: ops.linear_qkv_norm_rope_([ws.q], [ws.k], [ws.v], ws.normalized,
+                                                                        w0.w_qkv, w0.norm_q, w0.norm_k, cos, sin,
+                                                                        bc.qk_eps)),
+                          2.0 * t * 3 * bc.hidden * bc.hidden),
         "out": (time_call(lambda: ops.linear_(ws.attn_out, ws.attn.view(t, -1), w0.w_o)), 2.0 * t * bc.hidden * bc.hidden),
         "gate_up_swiglu": (time_call(lambda: ops.linear_swiglu(ws.normalized2, w0.w_gate_up_packed, out=ws.hidden)),
                            2.0 * t * 2 * bc.ffn * bc.hidden),
