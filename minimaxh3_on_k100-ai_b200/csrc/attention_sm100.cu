@@ -6,7 +6,11 @@
 //   O = sum P_bf16 V / sum P  (fp32 accumulation), keys masked by K's length.
 //
 // One CTA owns two 128-row Q tiles of one (batch, head) and streams K/V tiles of
-// 128 keys by TMA (no multicast).  Warp roles (384 threads):
+// 128 keys by TMA (no multicast).  A CTA fills an SM, so when the grid's last
+// wave would hold at most half as many pairs as there are SMs, those pairs run as
+// two one-tile CTAs each (a one-tile CTA takes about half a pair's time); the
+// per-tile arithmetic does not change, so results are bitwise the same.  Warp
+// roles (384 threads):
 //   warp 0        TMA producer for Q and K (one lane)
 //   warp 1        tcgen05.mma issuer for S = Q K^T (one lane) and TMEM owner
 //   warp 2        tcgen05.mma issuer for O += P V (one lane)
@@ -64,6 +68,9 @@ constexpr int NQ = 2;                         // Q tiles per CTA
 #endif
 constexpr int KSLOTS = H3_ATTN_KSLOTS;        // K ring slots
 constexpr int VSLOTS = H3_ATTN_VSLOTS;        // V ring slots
+#ifndef H3_ATTN_SPLIT_TAIL
+#define H3_ATTN_SPLIT_TAIL 1   // run a short last wave of Q-tile pairs as one-tile CTAs
+#endif
 #ifndef H3_ATTN_L2_AHEAD
 #define H3_ATTN_L2_AHEAD 4
 #endif
@@ -85,7 +92,8 @@ constexpr int OFF_P = OFF_Q + NQ * TILE;
 constexpr int OFF_K = OFF_P + NQ * TILE;
 constexpr int OFF_V = OFF_K + KSLOTS * TILE;
 constexpr int OFF_BAR = OFF_V + VSLOTS * TILE;
-constexpr int NUM_BARS = 1 + 2 * KSLOTS + 2 * VSLOTS + 4 * NQ;
+constexpr int VSLOTS_1 = VSLOTS > 2 ? VSLOTS : 2;  // V barriers: a one-tile CTA's slot 1 is Q tile 1's space
+constexpr int NUM_BARS = 1 + 2 * KSLOTS + 2 * VSLOTS_1 + 4 * NQ;
 constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 16 + 1024;  // + tmem slot, abort flag, alignment slack
 static_assert(SMEM_BYTES <= 232448, "shared memory over the sm_100 per-block limit");
 
@@ -93,6 +101,9 @@ struct Params {
     int Sq, Sk, H, B;
     int nkv;
     float scale_log2;
+    int tiles;       // 128-row Q tiles per (batch, head)
+    int pairs;       // Q tile pairs per (batch, head): ceil(tiles / 2)
+    int split_from;  // CTAs [0, split_from) own a pair; pair split_from + i runs as CTAs split_from + 2i (+1)
 };
 
 
@@ -177,8 +188,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint64_t *k_full = bars + 1;
     uint64_t *k_empty = k_full + KSLOTS;
     uint64_t *v_full = k_empty + KSLOTS;
-    uint64_t *v_empty = v_full + VSLOTS;
-    uint64_t *s_full = v_empty + VSLOTS;    // [t]: S_t(j) in TMEM
+    uint64_t *v_empty = v_full + VSLOTS_1;
+    uint64_t *s_full = v_empty + VSLOTS_1;  // [t]: S_t(j) in TMEM
     uint64_t *s_free = s_full + NQ;         // [t]: softmax t has read S_t(j)
     uint64_t *p_ready = s_free + NQ;        // [t]: P_t(j) in shared memory, O_t rescaled
     uint64_t *o_done = p_ready + NQ;        // [t]: P_t(j) V_j has landed in O_t
@@ -187,9 +198,29 @@ __global__ void __launch_bounds__(THREADS, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int h = blockIdx.y, b = blockIdx.z;
-    const int q0 = blockIdx.x * (NQ * BM);
+    // CTA -> (batch, head, first Q row, Q tiles): the grid's last pairs run as two
+    // one-tile CTAs when that shortens the final wave; a tile's arithmetic is the
+    // same either way
+    const int cta = (int)blockIdx.x;
+    int pair = cta, tile0 = 0, nq;
+    if (cta >= p.split_from) {
+        pair = p.split_from + ((cta - p.split_from) >> 1);
+        tile0 = (cta - p.split_from) & 1;
+    }
+    const int hb = pair / p.pairs;
+    const int h = hb % p.H, b = hb / p.H;
+    tile0 += (pair - hb * p.pairs) * NQ;
+    nq = cta >= p.split_from ? 1 : NQ;
+    if (nq > p.tiles - tile0) nq = p.tiles - tile0;
+    if (nq <= 0) return;   // second half of a split pair past Sq (uniform over the CTA)
+    const int q0 = tile0 * BM;
     const int nkv = p.nkv;
+    // A pair's softmax hides a V tile's load behind the other tile's work; a lone
+    // tile's does not, so a one-tile CTA double-buffers V, its second slot in the
+    // unused Q tile 1.  V_j goes to slot vslot(j), its use count there is vuse(j).
+    const bool v2 = nq == 1 && VSLOTS == 1;
+    auto vslot = [&](int j) { return v2 ? (j & 1) : j % VSLOTS; };
+    auto vuse = [&](int j) { return v2 ? (j >> 1) : j / VSLOTS; };
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
@@ -197,7 +228,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(&k_full[i], 1);
             mbar_init(&k_empty[i], 1);
         }
-        for (int i = 0; i < VSLOTS; ++i) {
+        for (int i = 0; i < VSLOTS_1; ++i) {
             mbar_init(&v_full[i], 1);
             mbar_init(&v_empty[i], 1);
         }
@@ -226,8 +257,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (kq) {
                 tma_prefetch_desc(&tq);
                 tma_prefetch_desc(&tk);
-                mbar_expect_tx(q_full, NQ * TILE);
-                for (int t = 0; t < NQ; ++t)
+                mbar_expect_tx(q_full, nq * TILE);
+                for (int t = 0; t < nq; ++t)
                     for (int hf = 0; hf < 2; ++hf)
                         tma_load_4d(sQ + t * TILE + hf * HALF, &tq, q_full, hf * 64, q0 + t * BM, h, b);
             } else {
@@ -254,8 +285,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const int ks = j % KSLOTS;
                     ok = load_tile(&tk, sK + ks * TILE, &k_full[ks], &k_empty[ks], j / KSLOTS, j * BN);
                 } else {
-                    const int vs = j % VSLOTS;
-                    ok = load_tile(&tv, sV + vs * TILE, &v_full[vs], &v_empty[vs], j / VSLOTS, j * BN);
+                    const int vs = vslot(j);
+                    uint8_t *dst = v2 ? (vs ? sQ + TILE : sV) : sV + vs * TILE;
+                    ok = load_tile(&tv, dst, &v_full[vs], &v_empty[vs], vuse(j), j * BN);
                 }
             }
         } else if ((warp == 1 || warp == 2) && lane == 0) {
@@ -282,7 +314,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 for (int j = 0; j < nkv && ok; ++j) {
                     const int ks = j % KSLOTS;
                     ok = mbar_wait(&k_full[ks], (j / KSLOTS) & 1, abort_flag);
-                    for (int t = 0; t < NQ && ok; ++t) {
+                    for (int t = 0; t < nq && ok; ++t) {
                         if (j > 0) ok = mbar_wait(&s_free[t], (j - 1) & 1, abort_flag);
                         if (!ok) break;
                         tc_fence_after();
@@ -295,13 +327,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             } else {
                 // O_t += P_t(j) V_j once softmax t has written P_t(j)
                 for (int j = 0; j < nkv && ok; ++j) {
-                    const int vs = j % VSLOTS;
-                    ok = mbar_wait(&v_full[vs], (j / VSLOTS) & 1, abort_flag);
-                    for (int t = 0; t < NQ && ok; ++t) {
+                    const int vs = vslot(j);
+                    const uint32_t vb = v2 ? (vs ? q_base + TILE : v_base) : v_base + vs * TILE;
+                    ok = mbar_wait(&v_full[vs], vuse(j) & 1, abort_flag);
+                    for (int t = 0; t < nq && ok; ++t) {
                         ok = mbar_wait(&p_ready[t], j & 1, abort_flag);
                         if (!ok) break;
                         tc_fence_after();
-                        issue(tmem + O_COL + t * HD, p_base + t * TILE, v_base + vs * TILE, true, j > 0);
+                        issue(tmem + O_COL + t * HD, p_base + t * TILE, vb, true, j > 0);
                         umma_commit(&o_done[t]);
                     }
                     if (!ok) break;
@@ -310,7 +343,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             if (!ok) drain_in_flight();
         }
-    } else {
+    } else if (((warp - 4) >> 2) < nq) {
         // ------------------------------------------------------------ softmax / epilogue
         const int t = (warp - 4) >> 2;
         const int row = (warp & 3) * 32 + lane;
@@ -512,16 +545,31 @@ extern "C" int h3_mha(const h3_tensor *out, const h3_tensor *q, const h3_tensor 
     p.nkv = (Sk + attn::BN - 1) / attn::BN;
     p.scale_log2 = scale * 1.4426950408889634f;
     static bool attr_set[64] = {};
+    static int sm_count[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    if (dev < 0 || dev >= 64) return H3_ERR_UNSUPPORTED;
+    if (!attr_set[dev]) {
         if (cudaFuncSetAttribute(attn::fa_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  attn::SMEM_BYTES) != cudaSuccess)
             return H3_ERR_LAUNCH;
+        if (cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+            sm_count[dev] <= 0)
+            return H3_ERR_DRIVER;
         attr_set[dev] = true;
     }
-    const dim3 grid((unsigned)((Sq + attn::NQ * attn::BM - 1) / (attn::NQ * attn::BM)), (unsigned)H, (unsigned)B);
-    attn::fa_fwd_kernel<<<grid, attn::THREADS, attn::SMEM_BYTES, (cudaStream_t)stream>>>(tq, tk, tv, to, p);
+    p.tiles = (Sq + attn::BM - 1) / attn::BM;
+    p.pairs = (p.tiles + attn::NQ - 1) / attn::NQ;
+    const int64_t npairs = (int64_t)p.pairs * H * B;
+    // one CTA per SM: a last wave of r <= SMs/2 pairs finishes sooner as 2r one-tile CTAs
+    // (about half a pair's time each, one per SM)
+    const int64_t r = npairs % sm_count[dev];
+    const int64_t split = (H3_ATTN_SPLIT_TAIL && r > 0 && 2 * r <= sm_count[dev]) ? r : 0;
+    const int64_t ctas = npairs + split;
+    if (ctas > (int64_t)0x7fffffff) return H3_ERR_UNSUPPORTED;
+    p.split_from = (int)(npairs - split);
+    attn::fa_fwd_kernel<<<(unsigned)ctas, attn::THREADS, attn::SMEM_BYTES, (cudaStream_t)stream>>>(tq, tk, tv, to,
+                                                                                                   p);
     return launch_status();
 }
 

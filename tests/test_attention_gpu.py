@@ -125,3 +125,26 @@ def test_bad_shapes(h3):
     q = torch.zeros(1, 16, 2, 64, dtype=torch.bfloat16, device=DEV)
     with pytest.raises(ValueError):
         h3.mha(q, q, q)
+
+
+def test_one_tile_ctas_equal_pairs(h3):
+    """When the grid's last wave would hold at most half as many Q-tile pairs as
+    there are SMs, those pairs run as one-tile CTAs.  158 heads of two tiles put
+    the last 10 pairs (on a 148-SM B200) in one-tile CTAs, and every single-head
+    call of two tiles runs one-tile CTAs; each tile's arithmetic is the same
+    either way, so every head agrees bitwise with its single-head call."""
+    torch.manual_seed(31)
+    Sq, Sk, H = 256, 1000, 158
+    q = torch.randn(1, Sq, H, 128, dtype=torch.bfloat16, device=DEV)
+    k = torch.randn(1, Sk, H, 128, dtype=torch.bfloat16, device=DEV)
+    v = torch.randn(1, Sk, H, 128, dtype=torch.bfloat16, device=DEV)
+    out = h3.mha(q, k, v)
+    _check(out, q, k, v, mean_err=5e-4)
+    for h in range(H):
+        one = h3.mha(q[:, :, h:h + 1], k[:, :, h:h + 1], v[:, :, h:h + 1])
+        assert torch.equal(one, out[:, :, h:h + 1]), f"head {h}"
+    # an odd tile count: the last pair of each head has one tile
+    q3 = q[:, :129]
+    out3 = h3.mha(q3, k, v)
+    assert torch.equal(out3, out[:, :129])
+    assert h3.load().h3_device_error() == 0
