@@ -174,9 +174,11 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk) {
     return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
-__global__ void __launch_bounds__(THREADS, 1)
-    fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                  const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap to, Params p) {
+// The work of one CTA on NQT (1 or 2) Q tiles starting at row q0 of (batch b, head h).
+template <int NQT>
+__device__ __forceinline__ void fa_cta(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv,
+                                       const CUtensorMap &to, const Params &p, const int h, const int b,
+                                       const int q0) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sQ = smem + OFF_Q;
@@ -198,27 +200,12 @@ __global__ void __launch_bounds__(THREADS, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    // CTA -> (batch, head, first Q row, Q tiles): the grid's last pairs run as two
-    // one-tile CTAs when that shortens the final wave; a tile's arithmetic is the
-    // same either way
-    const int cta = (int)blockIdx.x;
-    int pair = cta, tile0 = 0, nq;
-    if (cta >= p.split_from) {
-        pair = p.split_from + ((cta - p.split_from) >> 1);
-        tile0 = (cta - p.split_from) & 1;
-    }
-    const int hb = pair / p.pairs;
-    const int h = hb % p.H, b = hb / p.H;
-    tile0 += (pair - hb * p.pairs) * NQ;
-    nq = cta >= p.split_from ? 1 : NQ;
-    if (nq > p.tiles - tile0) nq = p.tiles - tile0;
-    if (nq <= 0) return;   // second half of a split pair past Sq (uniform over the CTA)
-    const int q0 = tile0 * BM;
+    constexpr int nq = NQT;
     const int nkv = p.nkv;
     // A pair's softmax hides a V tile's load behind the other tile's work; a lone
     // tile's does not, so a one-tile CTA double-buffers V, its second slot in the
     // unused Q tile 1.  V_j goes to slot vslot(j), its use count there is vuse(j).
-    const bool v2 = nq == 1 && VSLOTS == 1;
+    constexpr bool v2 = NQT == 1 && VSLOTS == 1;
     auto vslot = [&](int j) { return v2 ? (j & 1) : j % VSLOTS; };
     auto vuse = [&](int j) { return v2 ? (j >> 1) : j / VSLOTS; };
 
@@ -487,6 +474,29 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc_fence_after();
         tmem_dealloc(tmem, TMEM_COLS);
     }
+}
+
+// CTA -> (batch, head, first Q row, Q tiles): CTAs [0, split_from) own a pair of Q
+// tiles, the grid's last pairs run as two one-tile CTAs each.  Each kind runs its
+// own compile-time specialisation of the same tile code (the pair path carries no
+// run-time tile count), and a tile's arithmetic is the same in both.
+__global__ void __launch_bounds__(THREADS, 1)
+    fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                  const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap to, Params p) {
+    const int cta = (int)blockIdx.x;
+    const bool single = cta >= p.split_from;
+    int pair = cta, tile0 = 0;
+    if (single) {
+        pair = p.split_from + ((cta - p.split_from) >> 1);
+        tile0 = (cta - p.split_from) & 1;
+    }
+    const int hb = pair / p.pairs;
+    const int h = hb % p.H, b = hb / p.H;
+    tile0 += (pair - hb * p.pairs) * NQ;
+    const int left = p.tiles - tile0;   // Q tiles of this head from tile0 on
+    if (left <= 0) return;              // second half of a split pair past Sq (uniform over the CTA)
+    if (!single && left >= NQ) fa_cta<NQ>(tq, tk, tv, to, p, h, b, tile0 * BM);
+    else fa_cta<1>(tq, tk, tv, to, p, h, b, tile0 * BM);
 }
 
 }  // namespace attn

@@ -12,8 +12,12 @@
 //  * Per-head ops (q/k norm + RoPE): a half-warp per 128-wide head row (16 lanes x
 //    8 elements), two rows in flight per half-warp, RoPE partners exchanged by
 //    shuffle, output written straight into the (permuted) all-to-all send layout.
-//  * Element-wise ops (gated residual, SwiGLU): 2-D grid (column vectors x rows),
-//    two 16-byte vectors per thread, no 64-bit division per element.
+//  * Element-wise ops (gated residual, SwiGLU): flat grid over (row, column
+//    vector), one 16-byte vector of each operand per thread, no 64-bit division.
+// Launch shapes (rows per task, vectors per thread, occupancy) were chosen by
+// timing CUDA-graph-replayed launches on B200 at the reference's benchmark shapes
+// ([8192, 1792], [8192, 4864], q/k [8192, 14, 128]) and at the DiT step's: many
+// resident warps with little work each beat fewer warps with deeper pipelines.
 // Each kernel has a vectorised path (inner stride 1, 16-byte aligned rows) and a
 // strided path with the same arithmetic and summation order (identical bits).
 #include <math.h>
@@ -61,7 +65,7 @@ struct EwArgs {
 
 enum { EW_GATED_RESIDUAL = 0, EW_SWIGLU = 1 };
 #ifndef H3_EW_VPT
-#define H3_EW_VPT 4
+#define H3_EW_VPT 1
 #endif
 constexpr int EW_THREADS = 256, EW_VPT = H3_EW_VPT;   // vectors of 8 per thread
 
@@ -130,11 +134,17 @@ struct RowArgs {
     float eps;
 };
 
-constexpr int ROW_WARPS = 4;            // rows per CTA (one warp each)
-#ifndef H3_ROW_PAIR_MAXV
-#define H3_ROW_PAIR_MAXV 2              // rows of at most this many 16-byte vectors per lane go two per warp
-                                        // (rows <= 512 elements; measured: wider rows run faster one per
-                                        // warp, e.g. K8 at [8192, 1792] 3031 -> 3360 GB/s)
+#ifndef H3_ROW_WARPS
+#define H3_ROW_WARPS 4
+#endif
+constexpr int ROW_WARPS = H3_ROW_WARPS;  // rows per CTA (one warp each)
+#ifndef H3_ROW_PIPE_MAXV
+#define H3_ROW_PIPE_MAXV 8              // rows of at most this many 16-byte vectors per lane are pipelined
+#endif
+#ifndef H3_ROW_PIPE_RPW
+#define H3_ROW_PIPE_RPW 1               // ... H3_ROW_PIPE_RPW rows per warp (1: one row per warp; deeper
+                                        // pipelines measured slower, e.g. AdaLN at [8192, 1792] 3560 GB/s
+                                        // with 4 rows per warp against 4300 with 1)
 #endif
 
 // Phase 1 of a row: its input vectors into registers (for the fused residual
@@ -267,20 +277,21 @@ __device__ __forceinline__ void row_finish(const RowArgs &args, int64_t row, int
     }
 }
 
-// One warp per row, RPW rows per warp with every row's loads issued before the
-// first row's arithmetic (more bytes in flight for narrow rows).
+// One warp per row; with RPW > 1, RPW consecutive rows per warp, software-
+// pipelined (row u+1's loads issued before row u is normalised and stored).
 template <int MODE, bool VEC, int VPT, int RPW>
 __global__ void __launch_bounds__(ROW_WARPS * 32) row_kernel(RowArgs args) {
     const int lane = threadIdx.x & 31;
     const int64_t row0 = ((int64_t)blockIdx.x * ROW_WARPS + (threadIdx.x >> 5)) * RPW;
     if (row0 >= args.rows) return;  // whole warp leaves together
-    uint4 v[RPW][VPT];
+    uint4 v[2][VPT];   // the second buffer is dead (and not allocated) when RPW == 1
+    row_load<MODE, VEC, VPT>(args, row0, lane, v[0]);
 #pragma unroll
-    for (int u = 0; u < RPW; ++u)
-        if (row0 + u < args.rows) row_load<MODE, VEC, VPT>(args, row0 + u, lane, v[u]);
-#pragma unroll
-    for (int u = 0; u < RPW; ++u)
-        if (row0 + u < args.rows) row_finish<MODE, VEC, VPT>(args, row0 + u, lane, v[u]);
+    for (int u = 0; u < RPW; ++u) {
+        if (u + 1 < RPW && row0 + u + 1 < args.rows)
+            row_load<MODE, VEC, VPT>(args, row0 + u + 1, lane, v[(u + 1) & 1]);
+        if (row0 + u < args.rows) row_finish<MODE, VEC, VPT>(args, row0 + u, lane, v[u & 1]);
+    }
 }
 
 // ===========================================================================
@@ -305,10 +316,10 @@ struct HeadArgs {
 };
 
 #ifndef H3_HEAD_ROWS
-#define H3_HEAD_ROWS 8
+#define H3_HEAD_ROWS 2
 #endif
 #ifndef H3_HEAD_MINB
-#define H3_HEAD_MINB 1
+#define H3_HEAD_MINB 12   // resident CTAs per SM the register allocation must allow (40 registers)
 #endif
 constexpr int HEAD_THREADS = 128;                                      // 8 half-warps
 constexpr int HEAD_ROWS_PER_HW = H3_HEAD_ROWS;                         // rows in flight per half-warp
@@ -512,11 +523,11 @@ static int launch_row(RowArgs &args, bool vec, cudaStream_t stream) {
     if (args.rows == 0 || args.C == 0) return H3_OK;
     const int64_t nvec = (args.C + 7) / 8;
     const int vpt = (int)((nvec + 31) / 32);
-    // rows per warp follow the instantiated width bucket: 2 for buckets <= 8 vectors
-    // per lane, else 1; the grid is sized from the same constant
+    // rows per warp follow the instantiated width bucket: H3_ROW_PIPE_RPW for buckets
+    // <= H3_ROW_PIPE_MAXV vectors per lane, else 1; the grid is sized from the same constant
 #define H3_ROW_LAUNCH(VEC_, V)                                                              \
     {                                                                                       \
-        constexpr int R = (V) <= H3_ROW_PAIR_MAXV ? 2 : 1;                                  \
+        constexpr int R = (V) <= H3_ROW_PIPE_MAXV ? H3_ROW_PIPE_RPW : 1;                    \
         const int64_t blocks = (args.rows + ROW_WARPS * R - 1) / (ROW_WARPS * R);           \
         if (blocks > 0x7fffffffLL) return H3_ERR_UNSUPPORTED;                               \
         row_kernel<MODE, VEC_, V, R><<<(unsigned)blocks, ROW_WARPS * 32, 0, stream>>>(args); \
