@@ -20,6 +20,7 @@ import argparse
 import json
 import math
 import os
+import platform
 import statistics
 import subprocess
 import sys
@@ -51,6 +52,18 @@ def parse():
                    help="step: BASELINE config 5 (default, the headline); attention: config 2; "
                         "pointwise: config 1 op set; gemm: the block's four projections at config 3")
     return p.parse_args()
+
+
+def cpu_model() -> str:
+    """The host CPU's model name (from /proc/cpuinfo), recorded beside CPU timings."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return platform.processor() or "unknown"
 
 
 def peaks():
@@ -397,7 +410,7 @@ def run_ours(args, rank, world, local_rank, group):
         cpu_sample_step_seconds(sample_tokens=256)            # first call: weights, thread pools
         est, spent = cpu_sample_step_seconds(sample_tokens=256)
         line["cpu_baseline"] = {
-            "value": round(est, 2), "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "value": round(est, 2), "unit": UNIT, "cores": torch.get_num_threads(), "cpu_model": cpu_model(), "kind": "port",
             "sample": f"CPU oracle (reference torch compositions): one block's token-local ops on 256 of 18944 "
                       f"tokens + attention of those 256 queries over all 18944 keys (40 heads), full widths, "
                       f"measured {spent:.1f} s; extrapolated linearly x74 per block and x40 blocks "
@@ -428,7 +441,8 @@ def run_reference(args, rank):
             "warmup": args.warmup, "ms_per_step": round(v * 1e3, 1), "higher_is_better": False, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "impl": "reference",
             "config": workload_config(args, args.gpus),
-            "cpu_baseline": {"value": round(v, 2), "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+            "cpu_baseline": {"value": round(v, 2), "unit": UNIT, "cores": cores, "cpu_model": cpu_model(), "kind": "port",
+                             "sample": sample},
             "e2e": {"value": round(v, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
@@ -544,7 +558,7 @@ def run_gemm(args):
         O.linear(xc, wc)
         spent = time.perf_counter() - t0
         line["cpu_baseline"] = {"value": round(2.0 * 256 * 3 * hd * hd / spent / 1e12, 4), "unit": "TFLOP/s",
-                                "cores": torch.get_num_threads(), "kind": "port",
+                                "cores": torch.get_num_threads(), "cpu_model": cpu_model(), "kind": "port",
                                 "sample": f"oracle QKV linear (fp32 accumulate) on 256 of 18432 tokens ({spent:.2f} s)"}
     return line
 
@@ -604,7 +618,7 @@ def run_attention(args):
         O.attention_fp32(qc, kc, vc, D ** -0.5, chunk=256)
         spent = time.perf_counter() - t0
         line["cpu_baseline"] = {"value": round(flop / (spent * S / 256) / 1e12, 4), "unit": "TFLOP/s",
-                                "cores": torch.get_num_threads(), "kind": "port",
+                                "cores": torch.get_num_threads(), "cpu_model": cpu_model(), "kind": "port",
                                 "sample": f"oracle fp32 attention of 256 of 18432 queries over all keys, 40 heads "
                                           f"({spent:.1f} s), extrapolated x72"}
     return line
