@@ -8,8 +8,8 @@
 // One CTA owns two 128-row Q tiles of one (batch, head) and streams K/V tiles of
 // 128 keys by TMA (no multicast).  A CTA fills an SM, so when the grid's last
 // wave would hold at most half as many pairs as there are SMs, those pairs run as
-// two one-tile CTAs each (a one-tile CTA takes about half a pair's time); the
-// per-tile arithmetic does not change, so results are bitwise the same.  Warp
+// two one-tile CTAs each (measured alone, a one-tile CTA takes about 0.7 of a pair's
+// time); the per-tile arithmetic does not change, so results are bitwise the same.  Warp
 // roles (384 threads):
 //   warp 0        TMA producer for Q and K (one lane)
 //   warp 1        tcgen05.mma issuer for S = Q K^T (one lane) and TMEM owner
@@ -554,27 +554,24 @@ extern "C" int h3_mha(const h3_tensor *out, const h3_tensor *q, const h3_tensor 
     p.B = B;
     p.nkv = (Sk + attn::BN - 1) / attn::BN;
     p.scale_log2 = scale * 1.4426950408889634f;
-    static bool attr_set[64] = {};
-    static int sm_count[64] = {};
+    static std::atomic<bool> attr_set[64];
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return H3_ERR_UNSUPPORTED;
-    if (!attr_set[dev]) {
+    if (!attr_set[dev].load()) {
         if (cudaFuncSetAttribute(attn::fa_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  attn::SMEM_BYTES) != cudaSuccess)
             return H3_ERR_LAUNCH;
-        if (cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-            sm_count[dev] <= 0)
-            return H3_ERR_DRIVER;
-        attr_set[dev] = true;
+        attr_set[dev].store(true);
     }
+    const int sms = num_sms();
     p.tiles = (Sq + attn::BM - 1) / attn::BM;
     p.pairs = (p.tiles + attn::NQ - 1) / attn::NQ;
     const int64_t npairs = (int64_t)p.pairs * H * B;
     // one CTA per SM: a last wave of r <= SMs/2 pairs finishes sooner as 2r one-tile CTAs
-    // (about half a pair's time each, one per SM)
-    const int64_t r = npairs % sm_count[dev];
-    const int64_t split = (H3_ATTN_SPLIT_TAIL && r > 0 && 2 * r <= sm_count[dev]) ? r : 0;
+    // (one per SM; measured alone, a one-tile CTA takes about 0.7 of a pair's time)
+    const int64_t r = npairs % sms;
+    const int64_t split = (H3_ATTN_SPLIT_TAIL && r > 0 && 2 * r <= sms) ? r : 0;
     const int64_t ctas = npairs + split;
     if (ctas > (int64_t)0x7fffffff) return H3_ERR_UNSUPPORTED;
     p.split_from = (int)(npairs - split);
