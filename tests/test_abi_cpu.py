@@ -1,6 +1,5 @@
 """CPU checks of the C-ABI boundary: the library loads and exports every entry
 point declared in include/h3_b200.h (no compute calls: there is no GPU here)."""
-import ctypes
 import os
 import re
 

@@ -5,7 +5,6 @@ max-abs-rel = max|out - ref| / max|ref|.  The GEMM accumulation order is the
 only unpinned arithmetic (the reference's BLAS is not bitwise specified), so
 the block is compared by tolerance; repeated runs must be bitwise identical.
 """
-import dataclasses
 
 import pytest
 import torch

@@ -349,5 +349,4 @@ def test_empty_inputs(h3):
 
 
 def test_no_device_wait_expired(h3):
-    import ctypes
     assert h3.load().h3_device_error() == 0
