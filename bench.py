@@ -1,5 +1,5 @@
 #!/usr/bin/env python3
-"""Benchmark of the B200 H3 DiT hot path (the 40-block
+"""Benchmark of the B200 H3 DiT hot path (benchmark config 5: the 40-block
 denoising step on 18432 latent + 512 conditioning tokens).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
@@ -480,7 +480,7 @@ def _sp_gemms(ops, ws, w0, t, bc, time_call, cos, sin):
 
 
 def run_gemm(args):
-    """The block's four projections at BASELINE config 3 (18432 tokens, hidden 5120,
+    """The block's four projections at benchmark config 3 (18432 tokens, hidden 5120,
     FFN 13824) with their fused epilogues: QKV, out-proj, gate_up + SwiGLU,
     down + gated residual.  About 1.7 GB on the device; every operand set is read
     once per launch and the weights alone exceed L2."""
@@ -564,7 +564,7 @@ def run_gemm(args):
 
 
 def run_attention(args):
-    """non-causal attention, Q,K,V [1, 40, 18432, 128] (passed in
+    """Benchmark config 2: non-causal attention, Q,K,V [1, 40, 18432, 128] (passed in
     the mha [B, S, H, D] layout), scale 1/sqrt(128).  Inputs (3 x 189 MB) exceed L2."""
     import h3b200
     from h3b200 import _lib, ops
@@ -631,7 +631,7 @@ POINTWISE_BYTES = {  # algorithmic bytes at config 1 (bf16)
 
 
 def run_pointwise(args):
-    """BASELINE config 1 op set at its shapes; GB/s of algorithmic bytes per op."""
+    """Benchmark config 1 op set at its shapes; GB/s of algorithmic bytes per op."""
     import h3b200
     from h3b200 import _lib, ops
     from oracle import h3_oracle as O

@@ -73,7 +73,7 @@ class BlockConfig:
 
 def random_block_weights(cfg: BlockConfig, device, seed: int = 0, std: float = 0.02,
                          adaln: bool = True, temb_dim: int | None = None) -> BlockWeights:
-    """Random-init weights ~N(0, std), norm weights ones,
+    """Random-init weights ~N(0, std) (benchmark configs 3-5), norm weights ones,
     qk-norm weights ones.  Generated on the device (no checkpoint is used).  The
     AdaLN projection reads a time embedding of ``temb_dim`` (default: hidden)."""
     g = torch.Generator(device=device)

@@ -28,7 +28,7 @@ unit gate: bf16(x + bf16(1 * y)) = bf16(x + y).
 surface: same forward signature, packed-input record and output record.
 
 Weights are random-init (no checkpoint in this environment); sizes follow the
-BASELINE block config (hidden 5120, 40 heads, FFN 13824) with the reference's
+benchmark block config (hidden 5120, 40 heads, FFN 13824) with the reference's
 patch (24 latent channels x (1,2,2) = 96), audio (32) and text (5120) widths.
 """
 from __future__ import annotations

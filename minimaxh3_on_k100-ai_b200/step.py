@@ -1,4 +1,4 @@
-"""The 40-block DiT denoising step on 1..W GPUs.
+"""The 40-block DiT denoising step (benchmark config 5) on 1..W GPUs.
 
 Mirrors ``MiniMaxH3Transformer::forward`` (patches/InfiniLM.patch:1626-1826)
 for the parts on the hot path: RoPE table for the joint sequence, time
@@ -9,7 +9,7 @@ rank r runs the loop on its T = ceil(S/W) tokens and the blocks exchange heads
 through ``ulysses``.
 
 Inputs are the joint sequence's hidden states (video latent tokens followed by
-conditioning tokens) already at model width, as BASELINE config 5 specifies;
+conditioning tokens) already at model width, as benchmark config 5 specifies;
 weights are random-init (no checkpoint).
 """
 from __future__ import annotations

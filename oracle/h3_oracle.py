@@ -70,7 +70,7 @@ def rms_modulate(x, weight, scale, shift, eps):
 
 def ln_modulate(x, scale, shift, eps):
     """LayerNorm variant of AdaLN (mean-subtracted, no affine), the form the
-    BASELINE configs describe.  Not in the reference; defined here as torch's
+    benchmark configs describe.  Not in the reference; defined here as torch's
     fp32 layer_norm rounded once to BF16, then the reference's staged modulate."""
     normalized = _r(torch.nn.functional.layer_norm(x.float(), (x.shape[-1],), eps=eps))
     return modulate(normalized, scale, shift)

@@ -109,7 +109,7 @@ def test_sequence_parallel_shapes(h3):
 
 
 def test_bench_shape_sampled_rows(h3):
-    """[1, 40, 18432, 128] (given here in the [B,S,H,D] mha layout)."""
+    """Benchmark config 2: [1, 40, 18432, 128] (given here in the [B,S,H,D] mha layout)."""
     torch.manual_seed(0)
     S, H = 18432, 40
     q = torch.randn(1, S, H, 128, dtype=torch.bfloat16, device=DEV)

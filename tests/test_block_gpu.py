@@ -1,6 +1,6 @@
 """One DiT block and a short block stack on one GPU against the CPU oracle.
 
-Tolerance: max-abs-rel <= 2e-2 per block output, where
+Tolerance (the target for the block): max-abs-rel <= 2e-2 per block output, where
 max-abs-rel = max|out - ref| / max|ref|.  The GEMM accumulation order is the
 only unpinned arithmetic (the reference's BLAS is not bitwise specified), so
 the block is compared by tolerance; repeated runs must be bitwise identical.

@@ -157,7 +157,7 @@ def test_timestep_embedding_golden(h3):
 
 
 # ---------------------------------------------------------------------------
-# config-1 shapes, seed 0, vs the CPU oracle
+# benchmark config-1 shapes, seed 0, vs the CPU oracle
 # ---------------------------------------------------------------------------
 @pytest.fixture(scope="module")
 def cfg1():

@@ -1,4 +1,4 @@
-"""Ulysses sequence parallelism on real GPUs: a short DiT
+"""Ulysses sequence parallelism on real GPUs (benchmark config 4): a short DiT
 step on W = 2 ranks (one process per GPU, NCCL) must reproduce the 1-GPU run of
 the same kernels bit for bit, and match the CPU oracle within the block
 tolerance.  Skipped when fewer than two GPUs are visible."""
