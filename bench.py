@@ -607,7 +607,7 @@ def run_attention(args):
             "gpu_launches": launches,
             "roofline": {"kernel": "fa_fwd_kernel", "bound": "tensor", "achieved": round(achieved, 1),
                          "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": round(achieved / pk["bf16_tflops"], 4),
-                         "peak_source": f"{kind} bf16_tflops (burst)", "traffic": _ncu_traffic("fa_fwd_kernel")},
+                         "peak_source": f"{kind} bf16_tflops (burst)", "traffic": _ncu_traffic("fa_fwd_kernel", "bytes_per_launch_config2")},
             "clocks": clocks}
     if not args.no_cpu_baseline:
         from oracle import h3_oracle as O
@@ -742,10 +742,11 @@ def run_pointwise(args):
                          "traffic": _ncu_traffic(top)}}
 
 
-def _ncu_traffic(kernel):
+def _ncu_traffic(kernel, key="bytes_per_launch_at_bench_shape"):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary (None if absent)."""
     tpath = os.path.join(ROOT, "profiles", "ncu_traffic.json")
     try:
-        return json.load(open(tpath)).get(kernel, {}).get("bytes_per_launch_at_bench_shape")
+        return json.load(open(tpath)).get(kernel, {}).get(key)
     except (OSError, ValueError):
         return None
 
