@@ -173,10 +173,17 @@ def attention_fp32(q, k, v, scale, chunk: int = 1024) -> torch.Tensor:
 # Timestep embedding (patches/InfiniCore.patch:2115-2137, test :2834-2845)
 # --------------------------------------------------------------------------
 def timestep_embedding(t: torch.Tensor, dim: int, max_period: float = 10000.0) -> torch.Tensor:
+    """Sinusoidal embedding [N, dim] = cat(cos(t f_k), sin(t f_k)), f_k =
+    exp(-ln(max_period) k / half), with the reference's fp32 exponent and angle.
+    exp, cos and sin are evaluated in float64 and rounded once: the correctly
+    rounded fp32 values, so the result does not depend on which vectorised fp32
+    exp the host CPU's torch build picks (a 1-ulp frequency difference moves
+    t = 999's angle by ~6e-5 rad, more than the reference's 2e-5 tolerance)."""
     half = dim // 2
     exponent = -math.log(max_period) * torch.arange(half, dtype=torch.float32) / half
-    angles = t.float().unsqueeze(1) * exponent.exp().unsqueeze(0)
-    return torch.cat((angles.cos(), angles.sin()), dim=1)
+    freqs = exponent.double().exp().float()
+    angles = t.float().unsqueeze(1) * freqs.unsqueeze(0)
+    return torch.cat((angles.double().cos(), angles.double().sin()), dim=1).float()
 
 
 # --------------------------------------------------------------------------
@@ -224,8 +231,11 @@ def ulysses_scatter_back(returned: Sequence[torch.Tensor], group_heads: Sequence
 # --------------------------------------------------------------------------
 def linear(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     """y = x W^T, BF16 in/out, fp32 accumulation (no bias on the block linears,
-    patches/InfiniLM.patch:734-741, 1163-1169)."""
-    return _r(x.float() @ weight.float().t())
+    patches/InfiniLM.patch:734-741, 1163-1169).  The dot products are summed in
+    float64 and rounded to fp32 once, so a row's result does not depend on how
+    many rows the host BLAS is given (its fp32 kernels change the summation order
+    with the matrix shape), and equals a fp32 accumulation up to its rounding."""
+    return _r((x.double() @ weight.double().t()).float())
 
 
 def token_modulation(modulation: torch.Tensor, segments, n: int) -> torch.Tensor:
