@@ -146,6 +146,15 @@ def call(name: str, *args) -> None:
     check(getattr(lib, name)(*conv), name)
 
 
+def check_device(where: str) -> None:
+    """Synchronise the current device and raise if a bounded device-side wait gave
+    up (a peer that never signalled, an mbarrier that never completed), a row index
+    was out of range, or the device reported an error since the last check.  The
+    kernels that hit such a condition return normally and leave their outputs
+    incomplete, so every public entry point that hands results back checks here."""
+    check(load().h3_device_error(), f"{where} (device status)")
+
+
 def require_cuda(*tensors: torch.Tensor) -> None:
     dev = None
     for t in tensors:

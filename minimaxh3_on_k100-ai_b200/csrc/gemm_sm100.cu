@@ -376,13 +376,14 @@ int mat_tmap(CUtensorMap *map, const h3_tensor *t, uint32_t box_rows) {
 
 template <int EPI>
 int launch_gemm(const h3_tensor *x, const h3_tensor *w, gemm::Params &p, cudaStream_t stream) {
+    // an empty product launches nothing (a tensor map cannot describe a zero extent)
+    if (p.M == 0 || p.N == 0) return H3_OK;
     CUtensorMap ta, tb;
     H3_CHECK(mat_tmap(&ta, x, gemm::BM));
     H3_CHECK(mat_tmap(&tb, w, gemm::BN));
     p.num_m = (p.M + gemm::BM - 1) / gemm::BM;
     p.num_n = (p.N + gemm::BN - 1) / gemm::BN;
     p.num_tiles = p.num_m * p.num_n;
-    if (p.num_tiles == 0) return H3_OK;
     static std::atomic<bool> attr_set[4][64];
     int dev = 0;
     cudaGetDevice(&dev);

@@ -38,7 +38,7 @@ from dataclasses import dataclass, field
 
 import torch
 
-from . import ops
+from . import _lib, ops
 from .block import (BlockConfig, add_bias, random_time_embedder, segments_from_indices, time_embedding,
                     unit_gate)
 from .step import AUDIO_TAG, TEXT_TAG, VIDEO_TAG, BlockStack
@@ -223,6 +223,10 @@ class H3Transformer:
             audio_all = self._gather_rows_of_ranks(audio_all)[:seq]
         video_out = ops.gather_rows(video_all, video_indices)
         audio_out = ops.gather_rows(audio_all, audio_indices)
+        # a bounded wait that gave up, or an index outside its table, leaves rows
+        # incomplete without a launch error: report it before handing results back
+        with torch.cuda.device(self.device):
+            _lib.check_device("H3Transformer.forward")
         return video_out.unsqueeze(0), audio_out.unsqueeze(0)
 
     __call__ = forward
@@ -292,43 +296,56 @@ class MiniMaxH3TransformerInputs:
     text_indices: torch.Tensor
 
     def validate(self) -> None:
-        sequence_length = self.position_ids.shape[0]
-        if self.position_ids.ndim != 2 or self.position_ids.shape[1] != 3:
-            raise ValueError("position_ids must have shape [sequence_length, 3]")
+        """Reject malformed packed inputs before any device work.  Rules (the
+        interface's contract): the positions table is [S, 3] and fixes S; the
+        per-token tables (timestep index, modality tag) hold S integers; the three
+        row-index vectors are flat integer vectors; timestep is a flat vector;
+        every hidden-state input is one [1, tokens, channels] batch.  Shape
+        problems raise ValueError, element-type problems TypeError."""
+        def shape_of(t):
+            return tuple(t.shape)
+
+        def is_index(t):
+            return t.dtype in _INDEX_DTYPES
+
+        pos = self.position_ids
+        if pos.ndim != 2 or pos.shape[1] != 3:
+            raise ValueError(f"position_ids: expected a [S, 3] table, got {shape_of(pos)}")
+        if not (pos.is_floating_point() or is_index(pos)):
+            raise TypeError(f"position_ids: expected floating-point or integer elements, got {pos.dtype}")
+        s = pos.shape[0]
         if self.timestep.ndim != 1:
-            raise ValueError("timestep must have shape [num_timesteps]")
-        for name in ("timestep_indices", "token_tags"):
-            tensor = getattr(self, name)
-            if tensor.shape != (sequence_length,):
-                raise ValueError(f"{name} must have shape [{sequence_length}], got {tuple(tensor.shape)}")
-            if tensor.dtype not in _INDEX_DTYPES:
-                raise TypeError(f"{name} must use int32 or int64 indices")
-        for name in ("video_indices", "audio_indices", "text_indices"):
-            tensor = getattr(self, name)
-            if tensor.ndim != 1:
-                raise ValueError(f"{name} must be one-dimensional")
-            if tensor.dtype not in _INDEX_DTYPES:
-                raise TypeError(f"{name} must use int32 or int64 indices")
-        if not (self.position_ids.is_floating_point() or self.position_ids.dtype in _INDEX_DTYPES):
-            raise TypeError("position_ids must use a floating-point or integer dtype")
-        for name in ("video_hidden_states", "audio_hidden_states", "encoder_hidden_states"):
-            tensor = getattr(self, name)
-            if tensor.ndim != 3 or tensor.shape[0] != 1:
-                raise ValueError(f"{name} must have shape [1, tokens, channels]")
+            raise ValueError(f"timestep: expected a flat vector, got {shape_of(self.timestep)}")
+        per_token = {"timestep_indices": self.timestep_indices, "token_tags": self.token_tags}
+        row_sets = {"video_indices": self.video_indices, "audio_indices": self.audio_indices,
+                    "text_indices": self.text_indices}
+        for label, t in per_token.items():
+            if shape_of(t) != (s,):
+                raise ValueError(f"{label}: expected one entry per token ({s}), got {shape_of(t)}")
+        for label, t in row_sets.items():
+            if t.ndim != 1:
+                raise ValueError(f"{label}: expected a flat vector, got {shape_of(t)}")
+        for label, t in {**per_token, **row_sets}.items():
+            if not is_index(t):
+                raise TypeError(f"{label}: expected int32 or int64 elements, got {t.dtype}")
+        streams = {"video_hidden_states": self.video_hidden_states,
+                   "audio_hidden_states": self.audio_hidden_states,
+                   "encoder_hidden_states": self.encoder_hidden_states}
+        for label, t in streams.items():
+            if t.ndim != 3 or t.shape[0] != 1:
+                raise ValueError(f"{label}: expected one batch [1, tokens, channels], got {shape_of(t)}")
 
 
 @dataclass(frozen=True)
 class MiniMaxH3TransformerOutput:
+    """The forward's result: ``sample`` holds the video rows, ``audio_sample`` the
+    audio rows (field names of the interface's output record, :6589-6603);
+    ``video`` / ``audio`` name the same tensors by modality."""
     sample: torch.Tensor
     audio_sample: torch.Tensor
 
-    @property
-    def video(self) -> torch.Tensor:
-        return self.sample
-
-    @property
-    def audio(self) -> torch.Tensor:
-        return self.audio_sample
+    video = property(lambda self: self.sample)
+    audio = property(lambda self: self.audio_sample)
 
 
 def run_packed(model: H3Transformer, inputs: MiniMaxH3TransformerInputs) -> MiniMaxH3TransformerOutput:

@@ -18,7 +18,7 @@ from dataclasses import dataclass, field
 
 import torch
 
-from . import ops
+from . import _lib, ops
 from .block import (BlockConfig, Segment, Workspace, adaln_modulation, add_bias, block_forward,
                     random_block_weights, random_time_embedder, segments_from_indices, time_embedding)
 from .ulysses import SequenceParallel, local_rows
@@ -101,9 +101,26 @@ class BlockStack:
                 self._ws[tokens] = Workspace(tokens, self.cfg, self.device)
         return self._ws[tokens]
 
+    def _evict(self, cache: dict, key) -> None:
+        """Keep only the exchange of the shape about to run: a previous shape's
+        peer buffers (CUDA-IPC allocations mapped by every peer) are released
+        collectively first.  Every rank changes shape at the same call, so the
+        barrier pairs up; after it no peer still writes into the old buffers (each
+        rank's last wait on them completed before it got here)."""
+        stale = [k for k in cache if k != key]
+        if not stale:
+            return
+        import torch.distributed as dist
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for k in stale:
+            cache.pop(k).close()
+
     def tensor_parallel(self, tokens: int):
         if tokens not in self._tp:
             from .tp import TensorParallel
+            self._evict(self._tp, tokens)
             self._tp[tokens] = TensorParallel(self.world, self.rank, self.group, tokens, self.cfg.hidden, self.device)
         return self._tp[tokens]
 
@@ -112,6 +129,7 @@ class BlockStack:
             return None
         key = (valid_tokens, local_tokens)
         if key not in self._sp:
+            self._evict(self._sp, key)
             self._sp[key] = SequenceParallel(self.world, self.rank, self.group, valid_tokens, local_tokens,
                                              self.cfg.heads, self.cfg.head_dim, self.device)
         return self._sp[key]
@@ -245,4 +263,13 @@ class DiTStep:
             out_host = torch.empty(y.shape, dtype=y.dtype, pin_memory=True)
         out_host.copy_(y, non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()
+        self.check()
         return out_host
+
+    def check(self) -> None:
+        """Raise if a bounded device-side wait of the step gave up (a peer that
+        never signalled its exchange flag, an mbarrier that never completed) or the
+        device reported an error: such kernels return normally and leave their
+        outputs incomplete.  Synchronises the device."""
+        with torch.cuda.device(self.device):
+            _lib.check_device("DiTStep")

@@ -42,6 +42,19 @@ def test_linear_shapes(h3, M, N, K):
     _assert_gemm_close(y, _ref(x, w))
 
 
+def test_linear_empty_rows(h3):
+    """M = 0: every projection entry point returns success and launches nothing,
+    as the attention entry point does for an empty query sequence."""
+    w = (torch.randn(512, 256, device=DEV) * 0.02).bfloat16()
+    x = torch.empty(0, 256, dtype=torch.bfloat16, device=DEV)
+    assert h3.linear(x, w).shape == (0, 512)
+    res = torch.empty(0, 512, dtype=torch.bfloat16, device=DEV)
+    assert h3.linear_gated_residual(x, w, res, torch.ones(512, dtype=torch.bfloat16, device=DEV)).shape == (0, 512)
+    packed = h3.pack_gate_up((torch.randn(512, 256, device=DEV) * 0.02).bfloat16())
+    assert h3.linear_swiglu(x, packed).shape == (0, 256)
+    torch.cuda.synchronize()
+
+
 def test_linear_strided_rows(h3):
     torch.manual_seed(9)
     big = torch.randn(500, 1024 + 64, dtype=torch.bfloat16, device=DEV)

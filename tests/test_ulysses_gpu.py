@@ -1,7 +1,23 @@
-"""Ulysses sequence parallelism on real GPUs (benchmark config 4): a short DiT
-step on W = 2 ranks (one process per GPU, NCCL) must reproduce the 1-GPU run of
-the same kernels bit for bit, and match the CPU oracle within the block
-tolerance.  Skipped when fewer than two GPUs are visible."""
+"""Multi-GPU runs on real GPUs (benchmark configs 4 and 5 at W = 2, 4 and 8; one
+process per GPU, NCCL for set-up, the peer-memory exchange on the data path).
+
+For each world size W that fits on the box, W worker processes are spawned once
+and run every case; the tests then compare their outputs with the 1-GPU run of
+the same kernels:
+
+* a short DiT step with 40 heads (5 per rank at W = 8, an odd count) on 361
+  tokens, so the last rank carries padding rows: bitwise equal to 1 GPU;
+* the full config-5 step shape (18432 latent + 512 conditioning tokens, hidden
+  5120, FFN 13824) over 2 blocks: the gathered W-GPU output bitwise equal to
+  1 GPU;
+* the whole transformer forward (refiner replicated, blocks sequence-parallel,
+  output rows all-gathered): every rank's output bitwise equal to 1 GPU;
+* tensor parallelism (W = 2, 4): ranks agree, runs repeat bitwise, and the
+  result matches 1 GPU within the block tolerance;
+
+and every worker's device status (bounded waits, launch errors) is clean.
+Skipped for a world size that needs more GPUs than are visible.
+"""
 import os
 import socket
 
@@ -11,7 +27,7 @@ import torch.multiprocessing as mp
 
 pytestmark = pytest.mark.gpu
 
-WORLD = 2
+WORLDS = (2, 4, 8)
 
 
 def _free_port():
@@ -22,133 +38,172 @@ def _free_port():
     return p
 
 
-def _cfg():
+def _small_cfg():
     from h3b200.block import BlockConfig
     from h3b200.step import StepConfig
-    # 2 x 10 x 16 latent grid + 41 conditioning tokens = 361 tokens: T = 181 per rank,
-    # so the last rank carries one padding row; 4 heads -> 2 per rank
+    # 2 x 10 x 16 latent grid + 41 conditioning tokens = 361 tokens (padding on the
+    # last rank at every W); 40 heads x 128 = hidden 5120 as in the benchmark block
+    return StepConfig(blocks=2, video_grid=(2, 10, 16), cond_tokens=41,
+                      block=BlockConfig(hidden=5120, heads=40, ffn=1024))
+
+
+def _full_cfg():
+    from h3b200.step import StepConfig
+    return StepConfig(blocks=2)          # 18432 + 512 tokens, hidden 5120, FFN 13824
+
+
+def _tp_cfg():
+    from h3b200.block import BlockConfig
+    from h3b200.step import StepConfig
     return StepConfig(blocks=3, video_grid=(2, 10, 16), cond_tokens=41,
-                      block=BlockConfig(hidden=512, heads=4, ffn=1536))
-
-
-def _x(cfg):
-    g = torch.Generator().manual_seed(123)
-    return torch.randn(cfg.tokens, cfg.block.hidden, generator=g).bfloat16()
-
-
-def _worker(rank, port, path):
-    import datetime
-    import torch.distributed as dist
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=120),
-                            device_id=torch.device("cuda", rank))
-    from h3b200.step import DiTStep
-    cfg = _cfg()
-    step = DiTStep(cfg, f"cuda:{rank}", world=WORLD, rank=rank, group=dist.group.WORLD, seed=9)
-    x = _x(cfg)
-    local = torch.zeros(step.local, cfg.block.hidden, dtype=torch.bfloat16)
-    rows = x[step.start:min(step.start + step.local, cfg.tokens)]
-    local[:rows.shape[0]] = rows
-    out = step.forward(local.to(f"cuda:{rank}")).cpu()
-    torch.save(out, f"{path}.{rank}")
-    assert step.sp.exchange == "p2p"
-    dist.barrier()
-    step.close()
-    dist.destroy_process_group()
-
-
-@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
-def test_ulysses_two_gpus_bitwise_equal_to_one(tmp_path):
-    path = str(tmp_path / "sp")
-    mp.start_processes(_worker, args=(_free_port(), path), nprocs=WORLD, start_method="spawn")
-    from h3b200.step import DiTStep
-    cfg = _cfg()
-    one = DiTStep(cfg, "cuda:0", seed=9)
-    ref = one.forward(_x(cfg).to("cuda:0")).cpu()
-    sp = torch.cat([torch.load(f"{path}.{r}") for r in range(WORLD)])[:cfg.tokens]
-    assert torch.equal(sp, ref), "W-GPU output differs from the 1-GPU run"
-
-
-def _model_worker(rank, port, path):
-    import datetime
-    import torch.distributed as dist
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=120),
-                            device_id=torch.device("cuda", rank))
-    from h3b200.model import H3Transformer, packed_inputs
-    cfg = _model_cfg()
-    model = H3Transformer(cfg, f"cuda:{rank}", world=WORLD, rank=rank, group=dist.group.WORLD, seed=11)
-    inputs = packed_inputs(cfg, video_grid=(2, 6, 10), audio_tokens=13, text_tokens=30, seed=2)
-    video, audio = model(**{k: v.to(f"cuda:{rank}") for k, v in inputs.items()})
-    torch.save((video.cpu(), audio.cpu()), f"{path}.{rank}")
-    torch.cuda.synchronize()
-    dist.barrier()
-    model.close()
-    dist.destroy_process_group()
+                      block=BlockConfig(hidden=1024, heads=8, ffn=1536))
 
 
 def _model_cfg():
     from h3b200.block import BlockConfig
     from h3b200.model import H3ModelConfig
-    return H3ModelConfig(block=BlockConfig(hidden=512, heads=4, ffn=1536), blocks=2, refiner_blocks=2, text_dim=512)
+    return H3ModelConfig(block=BlockConfig(hidden=1024, heads=8, ffn=1536), blocks=2, refiner_blocks=2,
+                         text_dim=1024)
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
-def test_model_forward_two_gpus_bitwise_equal_to_one(tmp_path):
-    """The whole transformer forward (refiner replicated, blocks sequence-parallel,
-    output rows all-gathered): 163 tokens, so one rank carries a padding row."""
-    path = str(tmp_path / "model")
-    mp.start_processes(_model_worker, args=(_free_port(), path), nprocs=WORLD, start_method="spawn")
-    from h3b200.model import H3Transformer, packed_inputs
-    cfg = _model_cfg()
-    model = H3Transformer(cfg, "cuda:0", seed=11)
-    inputs = packed_inputs(cfg, video_grid=(2, 6, 10), audio_tokens=13, text_tokens=30, seed=2)
-    video, audio = model(**{k: v.to("cuda:0") for k, v in inputs.items()})
-    for r in range(WORLD):
-        v, a = torch.load(f"{path}.{r}")
-        assert torch.equal(v, video.cpu()) and torch.equal(a, audio.cpu()), f"rank {r} differs from the 1-GPU run"
+def _x(cfg, seed=123):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(cfg.tokens, cfg.block.hidden, generator=g).bfloat16()
 
 
-def _tp_worker(rank, port, path):
+def _local_rows(step, cfg, x):
+    local = torch.zeros(step.local, cfg.block.hidden, dtype=torch.bfloat16)
+    rows = x[step.start:min(step.start + step.local, cfg.tokens)]
+    local[:rows.shape[0]] = rows
+    return local
+
+
+def _worker(rank, world, port, path):
     import datetime
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=120),
+    dev = f"cuda:{rank}"
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=180),
                             device_id=torch.device("cuda", rank))
+    import h3b200
+    from h3b200.model import H3Transformer, packed_inputs
     from h3b200.step import DiTStep
-    cfg = _cfg()
-    step = DiTStep(cfg, f"cuda:{rank}", world=WORLD, rank=rank, group=dist.group.WORLD, seed=9, parallel="tp")
-    assert step.local == cfg.tokens and step.sp is None
-    x = _x(cfg).to(f"cuda:{rank}")
-    out1 = step.forward(x).clone()
-    out2 = step.forward(x).clone()
-    torch.save((out1.cpu(), torch.equal(out1, out2)), f"{path}.{rank}")
+    res = {}
+    for name, cfg in (("small", _small_cfg()), ("full", _full_cfg())):
+        step = DiTStep(cfg, dev, world=world, rank=rank, group=dist.group.WORLD, seed=9)
+        assert step.sp.exchange == "p2p"
+        res[name] = step.forward(_local_rows(step, cfg, _x(cfg)).to(dev)).cpu()
+        torch.cuda.synchronize()
+        dist.barrier()
+        step.close()
+        del step
+        torch.cuda.empty_cache()
+    mcfg = _model_cfg()
+    model = H3Transformer(mcfg, dev, world=world, rank=rank, group=dist.group.WORLD, seed=11)
+    inputs = packed_inputs(mcfg, video_grid=(2, 6, 10), audio_tokens=13, text_tokens=30, seed=2)
+    video, audio = model(**{k: v.to(dev) for k, v in inputs.items()})
+    res["model"] = (video.cpu(), audio.cpu())
     torch.cuda.synchronize()
     dist.barrier()
-    step.close()
+    model.close()
+    if world <= 4:
+        cfg = _tp_cfg()
+        step = DiTStep(cfg, dev, world=world, rank=rank, group=dist.group.WORLD, seed=9, parallel="tp")
+        assert step.local == cfg.tokens and step.sp is None
+        x = _x(cfg).to(dev)
+        out1 = step.forward(x).clone()
+        out2 = step.forward(x).clone()
+        res["tp"] = (out1.cpu(), torch.equal(out1, out2))
+        torch.cuda.synchronize()
+        dist.barrier()
+        step.close()
+    res["status"] = h3b200.load().h3_device_error()
+    torch.save(res, f"{path}.{rank}")
+    dist.barrier()
     dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
-def test_tensor_parallel_two_gpus_matches_one(tmp_path):
+_RUNS: dict = {}
+_ONE_GPU: dict = {}
+
+
+def _run(world, tmp_path_factory):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    if world not in _RUNS:
+        path = str(tmp_path_factory.mktemp(f"w{world}") / "res")
+        mp.start_processes(_worker, args=(world, _free_port(), path), nprocs=world, start_method="spawn")
+        _RUNS[world] = [torch.load(f"{path}.{r}") for r in range(world)]
+    return _RUNS[world]
+
+
+def _one_gpu(name):
+    """The same case on one GPU (cuda:0), computed once per test session."""
+    if name not in _ONE_GPU:
+        from h3b200.model import H3Transformer, packed_inputs
+        from h3b200.step import DiTStep
+        if name == "model":
+            mcfg = _model_cfg()
+            model = H3Transformer(mcfg, "cuda:0", seed=11)
+            inputs = packed_inputs(mcfg, video_grid=(2, 6, 10), audio_tokens=13, text_tokens=30, seed=2)
+            video, audio = model(**{k: v.to("cuda:0") for k, v in inputs.items()})
+            _ONE_GPU[name] = (video.cpu(), audio.cpu())
+        else:
+            cfg = {"small": _small_cfg, "full": _full_cfg, "tp": _tp_cfg}[name]()
+            step = DiTStep(cfg, "cuda:0", seed=9)
+            _ONE_GPU[name] = step.forward(_x(cfg).to("cuda:0")).cpu()
+            step.close()
+            del step
+            torch.cuda.empty_cache()
+    return _ONE_GPU[name]
+
+
+@pytest.mark.parametrize("world", WORLDS)
+def test_device_status_clean(world, tmp_path_factory):
+    runs = _run(world, tmp_path_factory)
+    assert [r["status"] for r in runs] == [0] * world, "a bounded wait gave up or the device reported an error"
+
+
+@pytest.mark.parametrize("world", WORLDS)
+def test_sequence_parallel_step_bitwise_equal_to_one(world, tmp_path_factory):
+    runs = _run(world, tmp_path_factory)
+    cfg = _small_cfg()
+    sp = torch.cat([r["small"] for r in runs])[:cfg.tokens]
+    assert torch.equal(sp, _one_gpu("small")), f"{world}-GPU output differs from the 1-GPU run"
+
+
+@pytest.mark.parametrize("world", WORLDS)
+def test_full_step_shape_bitwise_equal_to_one(world, tmp_path_factory):
+    """Benchmark config 5's shape (18944 tokens, full widths), 2 blocks."""
+    runs = _run(world, tmp_path_factory)
+    cfg = _full_cfg()
+    sp = torch.cat([r["full"] for r in runs])[:cfg.tokens]
+    ref = _one_gpu("full")
+    assert torch.equal(sp, ref), (f"{world}-GPU output differs from the 1-GPU run in "
+                                  f"{(sp != ref).any(-1).sum().item()} of {cfg.tokens} rows")
+
+
+@pytest.mark.parametrize("world", WORLDS)
+def test_model_forward_bitwise_equal_to_one(world, tmp_path_factory):
+    runs = _run(world, tmp_path_factory)
+    video, audio = _one_gpu("model")
+    for r, res in enumerate(runs):
+        v, a = res["model"]
+        assert torch.equal(v, video) and torch.equal(a, audio), f"rank {r} differs from the 1-GPU run"
+
+
+@pytest.mark.parametrize("world", (2, 4))
+def test_tensor_parallel_matches_one(world, tmp_path_factory):
     """Tensor parallelism (heads and FFN columns split, peer all-reduce): every rank
     holds the same full output, runs are deterministic, and the result matches the
     1-GPU step within the block tolerance (the all-reduce sums per-rank BF16
     partials, so it is not bitwise the 1-GPU accumulation)."""
     from oracle import h3_oracle as O
-    path = str(tmp_path / "tp")
-    mp.start_processes(_tp_worker, args=(_free_port(), path), nprocs=WORLD, start_method="spawn")
-    from h3b200.step import DiTStep
-    cfg = _cfg()
-    ref = DiTStep(cfg, "cuda:0", seed=9).forward(_x(cfg).to("cuda:0")).cpu()
-    outs = [torch.load(f"{path}.{r}") for r in range(WORLD)]
-    for r in range(WORLD):
+    runs = _run(world, tmp_path_factory)
+    outs = [r["tp"] for r in runs]
+    for r in range(world):
         assert outs[r][1], f"rank {r}: two runs differ"
         assert torch.equal(outs[r][0], outs[0][0]), f"rank {r} differs from rank 0"
-    assert O.max_abs_rel(outs[0][0], ref) <= 2e-2
+    assert O.max_abs_rel(outs[0][0], _one_gpu("tp")) <= 2e-2
