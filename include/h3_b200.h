@@ -158,6 +158,16 @@ int h3_timestep_embedding(const h3_tensor *out, const h3_tensor *t, float max_pe
 int h3_mha(const h3_tensor *out, const h3_tensor *q, const h3_tensor *k, const h3_tensor *v,
            float scale, void *stream);
 
+/* h3_mha for one sequence (q [1,Sq,Hl,128]) whose output rows are stored straight
+ * to their owners: row g of head h goes to dsts[g / R] row g % R, head slot h, where
+ * dsts is an array of ndst descriptors [R, Hl, 128] (same strides, 16-byte aligned
+ * rows; typically this rank's head slice of every rank's return buffer, mapped from
+ * the peers) and ndst * R >= Sq.  The Ulysses heads -> tokens all-to-all of
+ * attend_exchanged_groups / scatter_sequence (InfiniLM.patch:1006-1014, 1127-1137)
+ * done by the attention kernel's own epilogue.  Arithmetic identical to h3_mha. */
+int h3_mha_scatter(const h3_tensor *dsts, int32_t ndst, const h3_tensor *q, const h3_tensor *k,
+                   const h3_tensor *v, float scale, void *stream);
+
 /* ---------------- projections (BF16 in/out, fp32 accumulate) ---------------- */
 
 /* y [M,N] = x [M,K] * w[N,K]^T.  Rows of x, w, y contiguous (inner stride 1),
@@ -172,6 +182,36 @@ int h3_linear_swiglu(const h3_tensor *y, const h3_tensor *x, const h3_tensor *w_
 /* out [M,N] = bf16(residual + bf16(gate * bf16(x * w^T))); gate [M,N] (stride 0 ok). */
 int h3_linear_gated_residual(const h3_tensor *out, const h3_tensor *x, const h3_tensor *w,
                              const h3_tensor *residual, const h3_tensor *gate, void *stream);
+
+/* h3_linear_gated_residual, plus the row sums of squares of out in per-tile pieces:
+ * sq [M, ceil(N/256)] F32, sq[i][n] = fp32 sum over columns [256n, 256n+256) of
+ * bf16(out[i][c]^2), added in column order.  The out-projection + residual half of
+ * the block's post-attention step (to_out.0 then h3_gated_residual_rms_modulate,
+ * InfiniLM.patch:866, 1377-1390; op checks InfiniCore.patch:992-1004). */
+int h3_linear_gated_residual_sq(const h3_tensor *out, const h3_tensor *sq, const h3_tensor *x,
+                                const h3_tensor *w, const h3_tensor *residual, const h3_tensor *gate,
+                                void *stream);
+
+/* h3_rms_modulate with the row's sum of squares read from sq [rows, ceil(C/256)] F32
+ * (as h3_linear_gated_residual_sq writes it) instead of recomputed: total = lane l of
+ * a warp sums sq[l], sq[l+32], ... in order, then an xor-16/8/4/2/1 tree; then the
+ * staged mean / eps / rsqrt / normalise / weight / modulate roundings of
+ * h3_rms_modulate.  Element-wise (no row in registers).  Rows 16-byte aligned with
+ * inner stride 1 (H3_ERR_BAD_LAYOUT otherwise).  The norm half of
+ * h3_gated_residual_rms_modulate (InfiniCore.patch:179-181, 992-1004). */
+int h3_rms_modulate_sq(const h3_tensor *y, const h3_tensor *x, const h3_tensor *sq, const h3_tensor *weight,
+                       const h3_tensor *scale, const h3_tensor *shift, float eps, void *stream);
+
+/* The out-projection fused with h3_gated_residual_rms_modulate (InfiniLM.patch:866 then
+ * :1377-1390): residual_out = bf16(residual + bf16(gate * bf16(x w^T))) and
+ * out = RMSNorm + AdaLN of residual_out, with the sums of squares passed through
+ * `workspace` [M, ceil(N/256)] F32 (caller-owned scratch: the two launches of
+ * h3_linear_gated_residual_sq and h3_rms_modulate_sq). */
+int h3_linear_gated_residual_rms_modulate(const h3_tensor *residual_out, const h3_tensor *out,
+                                          const h3_tensor *x, const h3_tensor *w, const h3_tensor *residual,
+                                          const h3_tensor *gate, const h3_tensor *weight,
+                                          const h3_tensor *scale, const h3_tensor *shift, float eps,
+                                          const h3_tensor *workspace, void *stream);
 
 /* QKV projection with the q/k RMSNorm + RoPE of h3_qk_norm_rope applied in the GEMM
  * epilogue, each head row stored straight to its destination: x [T,K], w [3*H*128, K]

@@ -61,9 +61,13 @@ SIGNATURES = {
     "h3_rope_cache_sectioned": [P, P, P, _I, _I, _I, _V],
     "h3_timestep_embedding": [P, P, _F, _V],
     "h3_mha": [P, P, P, P, _F, _V],
+    "h3_mha_scatter": [P, _I, P, P, P, _F, _V],
     "h3_linear": [P, P, P, _V],
     "h3_linear_swiglu": [P, P, P, _V],
     "h3_linear_gated_residual": [P, P, P, P, P, _V],
+    "h3_linear_gated_residual_sq": [P, P, P, P, P, P, _V],
+    "h3_rms_modulate_sq": [P, P, P, P, P, P, _F, _V],
+    "h3_linear_gated_residual_rms_modulate": [P, P, P, P, P, P, P, P, P, _F, P, _V],
     "h3_pack_gate_up": [P, P, _V],
     "h3_linear_qkv_norm_rope": [P, P, P, P, P, _I, P, P, P, P, _F, _V],
     "h3_linear_f32": [P, P, P, P, _V],

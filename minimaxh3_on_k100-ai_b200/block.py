@@ -114,6 +114,11 @@ class Workspace:
         self.normalized2 = torch.empty(tokens, hd, **e)
         self.hidden = torch.empty(tokens, f, **e)
         self.out = [torch.empty(tokens, hd, **e), torch.empty(tokens, hd, **e)]
+        # per-256-column sums of squares written by the projections' epilogues for
+        # the RMSNorm passes that follow: of the residual, and of each output buffer
+        sq = ops.sq_partials_shape(tokens, hd)
+        self.sq = torch.empty(sq, dtype=torch.float32, device=device)
+        self.out_sq = [torch.empty(sq, dtype=torch.float32, device=device) for _ in range(2)]
 
 
 def qkv_fused(heads: int, cos: torch.Tensor) -> bool:
@@ -130,18 +135,32 @@ def _col(modulation: torch.Tensor, index: int, hidden: int, seg: Segment) -> tor
 
 def block_forward(x: torch.Tensor, modulation: torch.Tensor, segments: list[Segment], w: BlockWeights,
                   cos: torch.Tensor, sin: torch.Tensor, cfg: BlockConfig, ws: Workspace,
-                  out: torch.Tensor | None = None, sp=None) -> torch.Tensor:
+                  out: torch.Tensor | None = None, sp=None, x_sq: torch.Tensor | None = None,
+                  out_sq: torch.Tensor | None = None, fused_norms: bool = True) -> torch.Tensor:
     """One block on this rank's tokens x [T, Hd] -> out [T, Hd].
 
     modulation [rows, 6*Hd]; cos/sin [T, half] for this rank's tokens.  ``sp``
-    is a ``ulysses.SequenceParallel`` (None on one GPU)."""
+    is a ``ulysses.SequenceParallel`` (None on one GPU).
+
+    With ``fused_norms`` (the default) the out-projection's epilogue computes the
+    gated residual and its per-tile sums of squares, and the post-attention
+    RMSNorm + AdaLN reads those sums instead of reducing the row again
+    (``h3_rms_modulate_sq``); the down-projection does the same for the block's
+    output into ``out_sq`` when given, and the pre-attention RMSNorm uses
+    ``x_sq`` (x's sums from the previous block) when given.  The residuals are
+    bitwise those of the unfused ops; the normalised rows differ from them only by
+    the order of the fp32 sum of squares."""
     t, hd = x.shape
     h, d = cfg.heads, cfg.head_dim
     out = ws.out[0] if out is None else out
     for s in segments:
         r = slice(s.start, s.start + s.length)
-        ops.h3_rms_modulate_(ws.normalized[r], x[r], w.norm1, _col(modulation, 1, hd, s),
-                             _col(modulation, 0, hd, s), cfg.eps)
+        if fused_norms and x_sq is not None:
+            ops.h3_rms_modulate_sq_(ws.normalized[r], x[r], x_sq[r], w.norm1, _col(modulation, 1, hd, s),
+                                    _col(modulation, 0, hd, s), cfg.eps)
+        else:
+            ops.h3_rms_modulate_(ws.normalized[r], x[r], w.norm1, _col(modulation, 1, hd, s),
+                                 _col(modulation, 0, hd, s), cfg.eps)
     if sp is None or sp.world == 1:
         if qkv_fused(h, cos):
             # one GEMM whose epilogue normalises and rotates q/k and stores q, k, v per head
@@ -158,17 +177,29 @@ def block_forward(x: torch.Tensor, modulation: torch.Tensor, segments: list[Segm
         attn_flat = ws.attn.view(t, hd)
     else:
         attn_flat = sp.attention(ws.normalized, w.w_qkv, w.norm_q, w.norm_k, cos, sin, cfg.qk_eps)
-    ops.linear_(ws.attn_out, attn_flat, w.w_o)
-    for s in segments:
-        r = slice(s.start, s.start + s.length)
-        ops.h3_gated_residual_rms_modulate_(ws.residual[r], ws.normalized2[r], x[r], _col(modulation, 2, hd, s),
-                                            ws.attn_out[r], w.norm2, _col(modulation, 4, hd, s),
-                                            _col(modulation, 3, hd, s), cfg.eps)
+    if fused_norms:
+        for s in segments:
+            r = slice(s.start, s.start + s.length)
+            ops.linear_gated_residual_sq(attn_flat[r], w.w_o, x[r], modulation[s.row, 2 * hd:3 * hd],
+                                         out=ws.residual[r], sq=ws.sq[r])
+            ops.h3_rms_modulate_sq_(ws.normalized2[r], ws.residual[r], ws.sq[r], w.norm2,
+                                    _col(modulation, 4, hd, s), _col(modulation, 3, hd, s), cfg.eps)
+    else:
+        ops.linear_(ws.attn_out, attn_flat, w.w_o)
+        for s in segments:
+            r = slice(s.start, s.start + s.length)
+            ops.h3_gated_residual_rms_modulate_(ws.residual[r], ws.normalized2[r], x[r],
+                                                _col(modulation, 2, hd, s), ws.attn_out[r], w.norm2,
+                                                _col(modulation, 4, hd, s), _col(modulation, 3, hd, s), cfg.eps)
     ops.linear_swiglu(ws.normalized2, w.w_gate_up_packed, out=ws.hidden)
     for s in segments:
         r = slice(s.start, s.start + s.length)
-        ops.linear_gated_residual(ws.hidden[r], w.w_down, ws.residual[r], modulation[s.row, 5 * hd:6 * hd],
-                                  out=out[r])
+        gate_mlp = modulation[s.row, 5 * hd:6 * hd]
+        if fused_norms and out_sq is not None:
+            ops.linear_gated_residual_sq(ws.hidden[r], w.w_down, ws.residual[r], gate_mlp, out=out[r],
+                                         sq=out_sq[r])
+        else:
+            ops.linear_gated_residual(ws.hidden[r], w.w_down, ws.residual[r], gate_mlp, out=out[r])
     return out
 
 

@@ -47,9 +47,12 @@
 // BF16 tolerance (the tests' fp32 bounds), not bit for bit.
 //
 // H3_ATTN_POLY_PAIRS of every 8 key pairs of a full tile can be exponentiated on
-// the FMA pipe instead of the MUFU.  The epilogue divides by
-// the row sum, rounds to BF16 and writes through a swizzled shared tile with a
-// TMA store (rows past Sq are clipped).
+// the FMA pipe instead of the MUFU.  The epilogue divides by the row sum, rounds
+// to BF16 and writes through a swizzled shared tile with a TMA store (rows past
+// Sq are clipped), or -- for the Ulysses return leg (h3_mha_scatter) -- with
+// 16-byte row stores straight into the return buffer of the rank that owns each
+// row's token (a peer's memory over NVLink), so no separate copy or permute
+// follows the attention.
 #include <math.h>
 #include <stdint.h>
 
@@ -109,7 +112,24 @@ struct Params {
     int tiles;       // 128-row Q tiles per (batch, head)
     int pairs;       // Q tile pairs per (batch, head): ceil(tiles / 2)
     int split_from;  // CTAs [0, split_from) own a pair; pair split_from + i runs as CTAs split_from + 2i (+1)
+    // Scatter epilogue (ndst > 0, batch 1): output row g of head h goes to
+    // dst[g / rows_per_dst] + (g % rows_per_dst) * d_row + h * d_head -- the Ulysses
+    // return leg, each destination a rank's return buffer (local or a peer's).
+    int ndst;
+    int rows_per_dst;
+    int64_t d_row, d_head;
+    __nv_bfloat16 *dst[H3_EXCHANGE_MAX_RANKS];
 };
+
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ void st_global_v4(void *ptr, const uint4 &v) {
+    asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(ptr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
 
 
 __device__ __forceinline__ float ex2(float x) {
@@ -459,13 +479,31 @@ __device__ __forceinline__ void fa_cta(const CUtensorMap &tq, const CUtensorMap 
                                  pack_bf16x2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
                 }
             }
-            fence_proxy_async_smem();
-            named_bar_sync(1 + t, 128);
-            if (row == 0 && q0 + t * BM < p.Sq) {
-                tma_store_4d(&to, sQ + t * TILE, 0, q0 + t * BM, h, b);
-                tma_store_4d(&to, sQ + t * TILE + HALF, 64, q0 + t * BM, h, b);
-                tma_store_commit();
-                tma_store_wait_all();
+            if (p.ndst > 0) {
+                // row stores to each row's owner: 16 threads per 256-byte row, 8 rows
+                // per pass of the warpgroup (two whole rows per warp instruction)
+                named_bar_sync(1 + t, 128);
+                const int c = row & 15;
+                const uint32_t tile = out_tile + (uint32_t)(c >> 3) * HALF;
+#pragma unroll 4
+                for (int k = 0; k < BM / 8; ++k) {
+                    const int rr = (row >> 4) + 8 * k;
+                    const int g = q0 + t * BM + rr;
+                    if (g >= p.Sq) break;   // rows grow with k
+                    const int dq = g / p.rows_per_dst;
+                    const int tl = g - dq * p.rows_per_dst;
+                    const uint4 v = ld_shared_v4(tile + swz(rr, c & 7));
+                    st_global_v4(p.dst[dq] + (int64_t)tl * p.d_row + (int64_t)h * p.d_head + 8 * c, v);
+                }
+            } else {
+                fence_proxy_async_smem();
+                named_bar_sync(1 + t, 128);
+                if (row == 0 && q0 + t * BM < p.Sq) {
+                    tma_store_4d(&to, sQ + t * TILE, 0, q0 + t * BM, h, b);
+                    tma_store_4d(&to, sQ + t * TILE + HALF, 64, q0 + t * BM, h, b);
+                    tma_store_commit();
+                    tma_store_wait_all();
+                }
             }
         } else {
             drain_in_flight();
@@ -535,13 +573,18 @@ int check_attn_operand(const h3_tensor *t) {
 
 }  // namespace
 
-extern "C" int h3_mha(const h3_tensor *out, const h3_tensor *q, const h3_tensor *k, const h3_tensor *v, float scale,
-                      void *stream) {
-    H3_CHECK(check_attn_operand(out));
+namespace {
+
+// Shared launcher: `out` is the output view, or null with p.ndst > 0 (scatter).
+int launch_mha(const h3_tensor *out, const h3_tensor *q, const h3_tensor *k, const h3_tensor *v, float scale,
+               attn::Params &p, cudaStream_t stream) {
     H3_CHECK(check_attn_operand(q));
     H3_CHECK(check_attn_operand(k));
     H3_CHECK(check_attn_operand(v));
-    H3_CHECK(check_same_shape(out, q));
+    if (out) {
+        H3_CHECK(check_attn_operand(out));
+        H3_CHECK(check_same_shape(out, q));
+    }
     H3_CHECK(check_same_shape(k, v));
     if (q->shape[0] != k->shape[0] || q->shape[2] != k->shape[2]) return H3_ERR_BAD_SHAPE;
     const int B = (int)q->shape[0], Sq = (int)q->shape[1], H = (int)q->shape[2], Sk = (int)k->shape[1];
@@ -551,8 +594,8 @@ extern "C" int h3_mha(const h3_tensor *out, const h3_tensor *q, const h3_tensor 
     H3_CHECK(attn_tmap(&tq, q, attn::BM));
     H3_CHECK(attn_tmap(&tk, k, attn::BN));
     H3_CHECK(attn_tmap(&tv, v, attn::BN));
-    H3_CHECK(attn_tmap(&to, out, attn::BM));
-    attn::Params p;
+    if (out) H3_CHECK(attn_tmap(&to, out, attn::BM));
+    else to = tq;   // unused by the scatter epilogue
     p.Sq = Sq;
     p.Sk = Sk;
     p.H = H;
@@ -580,9 +623,44 @@ extern "C" int h3_mha(const h3_tensor *out, const h3_tensor *q, const h3_tensor 
     const int64_t ctas = npairs + split;
     if (ctas > (int64_t)0x7fffffff) return H3_ERR_UNSUPPORTED;
     p.split_from = (int)(npairs - split);
-    attn::fa_fwd_kernel<<<(unsigned)ctas, attn::THREADS, attn::SMEM_BYTES, (cudaStream_t)stream>>>(tq, tk, tv, to,
-                                                                                                   p);
+    attn::fa_fwd_kernel<<<(unsigned)ctas, attn::THREADS, attn::SMEM_BYTES, stream>>>(tq, tk, tv, to, p);
     return launch_status();
+}
+
+}  // namespace
+
+extern "C" int h3_mha(const h3_tensor *out, const h3_tensor *q, const h3_tensor *k, const h3_tensor *v, float scale,
+                      void *stream) {
+    if (!out) return H3_ERR_NULL;
+    attn::Params p{};
+    return launch_mha(out, q, k, v, scale, p, (cudaStream_t)stream);
+}
+
+extern "C" int h3_mha_scatter(const h3_tensor *dsts, int32_t ndst, const h3_tensor *q, const h3_tensor *k,
+                              const h3_tensor *v, float scale, void *stream) {
+    if (!dsts) return H3_ERR_NULL;
+    if (ndst < 1 || ndst > H3_EXCHANGE_MAX_RANKS) return H3_ERR_BAD_SHAPE;
+    H3_CHECK(check_attn_operand(q));
+    if (q->shape[0] != 1) return H3_ERR_UNSUPPORTED;   // one sequence (the Ulysses layout)
+    const h3_tensor *d0 = &dsts[0];
+    attn::Params p{};
+    for (int i = 0; i < ndst; ++i) {
+        const h3_tensor *d = &dsts[i];
+        H3_CHECK(check_bf16(d));
+        if (d->ndim != 3 || d->shape[0] != d0->shape[0] || d->shape[1] != q->shape[2] || d->shape[2] != 128)
+            return H3_ERR_BAD_SHAPE;
+        if (d->strides[0] != d0->strides[0] || d->strides[1] != d0->strides[1] || d->strides[2] != 1 ||
+            !aligned16(d->data) || d->strides[0] % 8 != 0 || d->strides[1] % 8 != 0)
+            return H3_ERR_BAD_LAYOUT;
+        p.dst[i] = static_cast<__nv_bfloat16 *>(d->data);
+    }
+    if (d0->shape[0] * ndst < q->shape[1] || d0->shape[0] > 0x7fffffffLL) return H3_ERR_BAD_SHAPE;
+    if (d0->shape[0] == 0) return q->shape[1] == 0 ? H3_OK : H3_ERR_BAD_SHAPE;
+    p.ndst = ndst;
+    p.rows_per_dst = (int)d0->shape[0];
+    p.d_row = d0->strides[0];
+    p.d_head = d0->strides[1];
+    return launch_mha(nullptr, q, k, v, scale, p, (cudaStream_t)stream);
 }
 
 // device error word of this translation unit (bounded waits in the attention kernel)

@@ -1,7 +1,8 @@
 // Peer-memory exchange for the Ulysses all-to-alls (patches/InfiniLM.patch:895-1137,
-// all_to_all_* InfiniCore.patch:526-577): the sending kernels (q/k RMSNorm + RoPE,
-// row copies of v and of the attention output) store straight into the peers'
-// receive buffers over NVLink, then one thread per rank raises an epoch flag in
+// all_to_all_* InfiniCore.patch:526-577): the producing kernels (the QKV
+// projection's epilogue, or the q/k RMSNorm + RoPE and row-copy kernels, and the
+// attention's scatter epilogue) store straight into the peers' receive buffers
+// over NVLink, then one thread per rank raises an epoch flag in
 // every peer's flag array and the receiver waits for its peers' flags before the
 // next kernel reads the data.  Receive buffers are plain cudaMalloc allocations
 // shared through CUDA IPC handles (no multicast objects, no NVLS).

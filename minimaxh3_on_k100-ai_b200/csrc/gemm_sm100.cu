@@ -44,7 +44,11 @@ constexpr int OFF_BAR = STAGES * STAGE_BYTES;
 constexpr int NUM_BARS = 2 * STAGES + 4;
 constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 16 + 1024;
 
-enum Epi { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_GATED_RES = 2, EPI_QKV = 3 };
+// EPI_GATED_RES_SQ: EPI_GATED_RES, plus the tile's share of the output row's sum
+// of squares for the RMSNorm that follows (sq[row][n] = fp32 sum over the tile's
+// columns, in column order, of bf16(out^2)), so the norm pass needs no reduction.
+enum Epi { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_GATED_RES = 2, EPI_QKV = 3, EPI_GATED_RES_SQ = 4 };
+constexpr int NUM_EPI = 5;
 constexpr int QKV_HALF = 48;              // rotated pairs per head (3 axes x 16 frequencies)
 constexpr int QKV_HW = QKV_HALF / 2;      // ... as packed BF16x2 words
 
@@ -57,6 +61,8 @@ struct Params {
     int64_t ldr;
     const __nv_bfloat16 *gate;
     int64_t ldg;            // 0 broadcasts one gate row
+    float *sq;              // EPI_GATED_RES_SQ: [M, ceil(N / BN)] fp32 partial sums of squares
+    int64_t ldsq;
     // EPI_QKV: accumulator column c = part * hcols + head * 128 + d (part 0/1/2 = q/k/v);
     // head h goes to destination h / hpd, head slot h % hpd
     int hcols, hpd;
@@ -289,6 +295,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                 }
             } else {
+                float ssq = 0.f;   // EPI_GATED_RES_SQ: this row's sum of bf16(out^2) over the tile
 #pragma unroll 1
                 for (int cc = 0; cc < BN / 32; ++cc) {
                     uint32_t v[32];
@@ -301,7 +308,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                             for (int i = 0; i < 16; ++i)
                                 w[i] = pack2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
-                        } else {  // EPI_GATED_RES
+                        } else {  // EPI_GATED_RES, EPI_GATED_RES_SQ
                             const __nv_bfloat16 *rp = p.res + (int64_t)row * p.ldr + col;
                             const __nv_bfloat16 *gp = p.gate + (int64_t)row * p.ldg + col;
 #pragma unroll
@@ -315,12 +322,21 @@ __global__ void __launch_bounds__(THREADS, 1)
                                     w[4 * q + e] = badd2(w32(r4, e), bmul2(w32(g4, e), y2));
                                 }
                             }
+                            if (EPI == EPI_GATED_RES_SQ) {
+#pragma unroll
+                                for (int i = 0; i < 16; ++i) {   // columns in order: lo, hi of each word
+                                    const uint32_t sq = bmul2(w[i], w[i]);
+                                    ssq = add_rn(ssq, blo(sq));
+                                    ssq = add_rn(ssq, bhi(sq));
+                                }
+                            }
                         }
                         __nv_bfloat16 *dst = p.out + (int64_t)row * p.ldo + col;
 #pragma unroll
                         for (int q = 0; q < 4; ++q) st_global_v4(dst + 8 * q, w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
                     }
                 }
+                if (EPI == EPI_GATED_RES_SQ && row_ok) p.sq[(int64_t)row * p.ldsq + n] = ssq;
             }
             tc_fence_before();
             mbar_arrive(&acc_empty[acc]);
@@ -384,7 +400,7 @@ int launch_gemm(const h3_tensor *x, const h3_tensor *w, gemm::Params &p, cudaStr
     p.num_m = (p.M + gemm::BM - 1) / gemm::BM;
     p.num_n = (p.N + gemm::BN - 1) / gemm::BN;
     p.num_tiles = p.num_m * p.num_n;
-    static std::atomic<bool> attr_set[4][64];
+    static std::atomic<bool> attr_set[gemm::NUM_EPI][64];
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return H3_ERR_UNSUPPORTED;
@@ -438,8 +454,12 @@ extern "C" int h3_linear_swiglu(const h3_tensor *y, const h3_tensor *x, const h3
     return launch_gemm<gemm::EPI_SWIGLU>(x, w_packed, p, (cudaStream_t)stream);
 }
 
-extern "C" int h3_linear_gated_residual(const h3_tensor *out, const h3_tensor *x, const h3_tensor *w,
-                                        const h3_tensor *residual, const h3_tensor *gate, void *stream) {
+namespace {
+
+// out = bf16(residual + bf16(gate * bf16(x w^T))); with sq, also the per-tile
+// partial sums of squares of out (EPI_GATED_RES_SQ)
+int gated_residual_gemm(const h3_tensor *out, const h3_tensor *x, const h3_tensor *w, const h3_tensor *residual,
+                        const h3_tensor *gate, const h3_tensor *sq, cudaStream_t stream) {
     H3_CHECK(check_gemm_operands(out, x, w));
     H3_CHECK(check_bf16(residual));
     H3_CHECK(check_bf16(gate));
@@ -460,7 +480,41 @@ extern "C" int h3_linear_gated_residual(const h3_tensor *out, const h3_tensor *x
     p.ldr = residual->strides[0];
     p.gate = static_cast<const __nv_bfloat16 *>(gate->data);
     p.ldg = gate->strides[0];
-    return launch_gemm<gemm::EPI_GATED_RES>(x, w, p, (cudaStream_t)stream);
+    if (!sq) return launch_gemm<gemm::EPI_GATED_RES>(x, w, p, stream);
+    H3_CHECK(check_desc(sq, H3_F32));
+    const int64_t nt = (out->shape[1] + gemm::BN - 1) / gemm::BN;
+    if (sq->ndim != 2 || sq->shape[0] != out->shape[0] || sq->shape[1] != nt) return H3_ERR_BAD_SHAPE;
+    if ((nt > 1 && sq->strides[1] != 1) || (sq->shape[0] > 1 && sq->strides[0] < nt)) return H3_ERR_BAD_LAYOUT;
+    p.sq = static_cast<float *>(sq->data);
+    p.ldsq = sq->strides[0];
+    return launch_gemm<gemm::EPI_GATED_RES_SQ>(x, w, p, stream);
+}
+
+}  // namespace
+
+extern "C" int h3_linear_gated_residual(const h3_tensor *out, const h3_tensor *x, const h3_tensor *w,
+                                        const h3_tensor *residual, const h3_tensor *gate, void *stream) {
+    return gated_residual_gemm(out, x, w, residual, gate, nullptr, (cudaStream_t)stream);
+}
+
+extern "C" int h3_linear_gated_residual_sq(const h3_tensor *out, const h3_tensor *sq, const h3_tensor *x,
+                                           const h3_tensor *w, const h3_tensor *residual, const h3_tensor *gate,
+                                           void *stream) {
+    if (!sq) return H3_ERR_NULL;
+    return gated_residual_gemm(out, x, w, residual, gate, sq, (cudaStream_t)stream);
+}
+
+extern "C" int h3_linear_gated_residual_rms_modulate(const h3_tensor *residual_out, const h3_tensor *out,
+                                                     const h3_tensor *x, const h3_tensor *w,
+                                                     const h3_tensor *residual, const h3_tensor *gate,
+                                                     const h3_tensor *weight, const h3_tensor *scale,
+                                                     const h3_tensor *shift, float eps, const h3_tensor *workspace,
+                                                     void *stream) {
+    if (!workspace || !residual_out) return H3_ERR_NULL;
+    H3_CHECK(check_bf16(out));
+    H3_CHECK(check_same_shape(out, residual_out));
+    H3_CHECK(h3_linear_gated_residual_sq(residual_out, workspace, x, w, residual, gate, stream));
+    return h3_rms_modulate_sq(out, residual_out, workspace, weight, scale, shift, eps, stream);
 }
 
 // QKV projection with q/k RMSNorm + RoPE in the epilogue, each head row stored to

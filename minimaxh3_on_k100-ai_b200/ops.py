@@ -28,7 +28,8 @@ __all__ = [
     "h3_rope_cache", "h3_rope_cache_sectioned", "rope_powers", "timestep_embedding", "mha", "mha_",
     "linear", "linear_", "linear_swiglu", "linear_gated_residual", "pack_gate_up",
     "linear_f32", "linear_f32_", "gather_rows", "gather_rows_", "index_copy_rows_", "silu", "silu_",
-    "linear_qkv_norm_rope_",
+    "linear_qkv_norm_rope_", "linear_gated_residual_sq", "h3_rms_modulate_sq_",
+    "linear_gated_residual_rms_modulate", "sq_partials_shape",
 ]
 
 
@@ -243,6 +244,58 @@ def linear_gated_residual(x, weight, residual, gate, out=None):
     call("h3_linear_gated_residual", desc(_flat(out)), desc(_flat(x)), desc(weight), desc(r2), desc(g2),
          stream_of(x))
     return out
+
+
+SQ_TILE = 256   # columns per partial sum of squares (the projection's output tile width)
+
+
+def sq_partials_shape(rows: int, width: int) -> tuple[int, int]:
+    """Shape of the per-tile sums of squares of a [rows, width] output."""
+    return rows, (width + SQ_TILE - 1) // SQ_TILE
+
+
+def linear_gated_residual_sq(x, weight, residual, gate, out=None, sq=None):
+    """(out, sq): out = bf16(residual + bf16(gate * (x W^T))) and its per-tile
+    row sums of squares sq [M, ceil(N/256)] F32 for ``h3_rms_modulate_sq_``."""
+    if out is None:
+        out = torch.empty_like(residual)
+    o2 = _flat(out)
+    if sq is None:
+        sq = torch.empty(sq_partials_shape(*o2.shape), dtype=torch.float32, device=out.device)
+    r2 = _flat(residual)
+    g2 = _rowlike(gate, r2) if gate.dim() == 1 else _flat(gate)
+    require_cuda(out, sq, x, weight, residual, g2)
+    call("h3_linear_gated_residual_sq", desc(o2), desc(sq), desc(_flat(x)), desc(weight), desc(r2), desc(g2),
+         stream_of(x))
+    return out, sq
+
+
+def h3_rms_modulate_sq_(out, x, sq, weight, scale, shift, eps):
+    """h3_rms_modulate_ with the row sums of squares taken from ``sq`` (written by
+    ``linear_gated_residual_sq``)."""
+    scale, shift = _rowlike(scale, x), _rowlike(shift, x)
+    require_cuda(out, x, sq, weight, scale, shift)
+    call("h3_rms_modulate_sq", desc(out), desc(x), desc(sq), desc(weight), desc(scale), desc(shift), float(eps),
+         stream_of(x))
+    return out
+
+
+def linear_gated_residual_rms_modulate(x, weight, residual, gate, norm_weight, scale, shift, eps,
+                                       residual_out=None, out=None, workspace=None):
+    """(residual_out, out) of the out-projection fused with
+    h3_gated_residual_rms_modulate; ``workspace`` [M, ceil(N/256)] F32 is scratch."""
+    residual_out = torch.empty_like(residual) if residual_out is None else residual_out
+    out = torch.empty_like(residual) if out is None else out
+    r2 = _flat(residual)
+    if workspace is None:
+        workspace = torch.empty(sq_partials_shape(*r2.shape), dtype=torch.float32, device=r2.device)
+    g2 = _rowlike(gate, r2) if gate.dim() == 1 else _flat(gate)
+    sc, sh = _rowlike(scale, r2), _rowlike(shift, r2)
+    require_cuda(residual_out, out, x, weight, residual, g2, norm_weight, sc, sh, workspace)
+    call("h3_linear_gated_residual_rms_modulate", desc(_flat(residual_out)), desc(_flat(out)), desc(_flat(x)),
+         desc(weight), desc(r2), desc(g2), desc(norm_weight), desc(sc), desc(sh), float(eps), desc(workspace),
+         stream_of(x))
+    return residual_out, out
 
 
 # ---------------------------------------------------------------------------

@@ -172,7 +172,11 @@ class BlockStack:
             return h
         sp = self.sequence_parallel(valid_tokens, h.shape[0])
         for i, w in enumerate(self.weights):
-            h = block_forward(h, mods[i], segments, w, cos, sin, self.cfg, ws, out=ws.out[i % 2], sp=sp)
+            # block i > 0 reads block i-1's output together with its per-tile sums of
+            # squares (written by the down-projection's epilogue)
+            x_sq = ws.out_sq[(i - 1) % 2] if i > 0 else None
+            h = block_forward(h, mods[i], segments, w, cos, sin, self.cfg, ws, out=ws.out[i % 2], sp=sp,
+                              x_sq=x_sq, out_sq=ws.out_sq[i % 2])
         return h
 
 

@@ -26,11 +26,13 @@ the permuted view of the send buffer ([T, W, Hs, D] view of [W, T, Hs, D]), so
 no separate pack pass is needed for q/k.
 
 On GPUs the exchange is peer-to-peer (``PeerExchange``): the receive buffers of
-every rank live in CUDA-IPC-shared allocations, the q/k RMSNorm + RoPE kernel
-stores each destination's block straight into that rank's receive buffer over
-NVLink (no send buffer, no separate collective), row-copy kernels do the same for
-v and for the attention output, and an epoch flag per rank (bounded device wait)
-replaces the collective's synchronisation.  ``exchange="collective"`` keeps the
+every rank live in CUDA-IPC-shared allocations, the QKV projection's epilogue
+(q/k RMSNorm + RoPE included) stores each head row straight into its
+destination rank's receive buffer over NVLink (no send buffer, no separate
+collective), the attention epilogue stores each output row straight into the
+token-major return rows of the rank that owns the token (``h3_mha_scatter``), so
+the out-projection reads them in place, and an epoch flag per rank (bounded
+device wait) replaces the collective's synchronisation.  ``exchange="collective"`` keeps the
 torch.distributed all_to_all_single path (NCCL, or gloo in the CPU tests).
 
 The exchange logic is written against a small ``kernels`` interface so the same
@@ -142,14 +144,15 @@ class PeerExchange:
         t = torch.as_tensor(_CudaBytes(self.own + self.offsets[name], 2 * n), device=self.device)
         return t.view(torch.bfloat16).view(*shape)
 
-    def peer_desc(self, p: int, name: str, shape, elem_offset: int = 0) -> _lib.H3Tensor:
-        """Descriptor of a contiguous BF16 block inside rank p's region (as mapped here)."""
+    def peer_desc(self, p: int, name: str, shape, elem_offset: int = 0, strides=None) -> _lib.H3Tensor:
+        """Descriptor of a BF16 block inside rank p's region (as mapped here):
+        contiguous, or with the given element strides."""
         d = _lib.H3Tensor()
         d.data = self.bases[p] + self.offsets[name] + 2 * elem_offset
         stride = 1
         for i in reversed(range(len(shape))):
             d.shape[i] = shape[i]
-            d.strides[i] = stride
+            d.strides[i] = stride if strides is None else strides[i]
             stride *= shape[i]
         d.ndim, d.dtype = len(shape), 0
         return d
@@ -216,14 +219,21 @@ class SequenceParallel:
             self.peers = PeerExchange(world, rank, group, self.device,
                                       {"q": block, "k": block, "v": block, "back": block})
             self.recv_p2p = [self.peers.local(n, (w, t, hs, d)) for n in ("q", "k", "v")]
-            self.back_p2p = self.peers.local("back", (w, t, hs, d))
+            # the returning attention rows land token-major, [T, W, Hl, D] = [T, H*D]
+            # with head p*Hl + j at slot (p, j): the out-projection's input as is
+            self.back_p2p = self.peers.local("back", (t, w, hs, d))
             # destination descriptors: slot `rank` of every rank's regions, as mapped here
             slot = rank * t * hs * d
             arr = lambda name, shape: (_lib.H3Tensor * w)(  # noqa: E731
                 *[self.peers.peer_desc(p, name, shape, slot) for p in range(w)])
             self.dst_q, self.dst_k = arr("q", (t, hs, d)), arr("k", (t, hs, d))
-            self.dst_v, self.dst_back = arr("v", (t, hs * d)), arr("back", (t, hs * d))
+            self.dst_v = arr("v", (t, hs * d))
             self.dst_v3 = arr("v", (t, hs, d))
+            # this rank's head slice (slot `rank` of the W head slices) of every rank's
+            # return rows: [T, Hl, D] with row stride W*Hl*D
+            self.dst_back = (_lib.H3Tensor * w)(*[
+                self.peers.peer_desc(p, "back", (t, hs, d), rank * hs * d, strides=(w * hs * d, d, 1))
+                for p in range(w)])
         else:
             self.send = [[torch.empty(w, t, hs, d, **e) for _ in range(3)] for hs in self.group_heads]
             self.recv = [[torch.empty(w, t, hs, d, **e) for _ in range(3)] for hs in self.group_heads]
@@ -299,14 +309,13 @@ class SequenceParallel:
         q = self.recv_p2p[0].view(1, w * t, hl, d)
         kk = self.recv_p2p[1].view(1, w * t, hl, d)[:, :self.valid]
         v = self.recv_p2p[2].view(1, w * t, hl, d)[:, :self.valid]
-        attn = self.attn[0]
-        self.kernels.mha(attn.unsqueeze(0), q, kk, v, 1.0 / math.sqrt(d))
-        # heads -> tokens: rows of rank q's tokens go back to slot r of rank q
-        _lib.call("h3_copy_blocks", self.dst_back, w, _lib.desc(attn.view(w, t, hl * d)), stream)
+        # heads -> tokens: the attention epilogue stores each output row straight into
+        # the return rows of the rank that owns its token (this rank's head slot)
+        _lib.call("h3_mha_scatter", self.dst_back, w, _lib.desc(q), _lib.desc(kk), _lib.desc(v),
+                  1.0 / math.sqrt(d), stream)
         px.signal(self.SLOT_OUT, stream)
         px.wait(self.SLOT_OUT, stream)
-        self.kernels.copy(self.out, self.back_p2p.permute(1, 0, 2, 3))
-        return self.out.view(t, w * hl * d)
+        return self.back_p2p.view(t, w * hl * d)
 
     # -- the exchange -----------------------------------------------------------
     def attention(self, normalized: torch.Tensor, w_qkv: torch.Tensor, norm_q, norm_k, cos, sin,

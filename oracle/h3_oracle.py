@@ -58,6 +58,109 @@ def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
     return _r(_r(xf * reciprocal.float()).float() * weight.float())
 
 
+# --------------------------------------------------------------------------
+# The CUDA kernels' fixed summation orders for the RMSNorm sum of squares.
+# The reference sums in its device's order (the torch oracle above in the host
+# CPU's vector order); the sum is fp32 and the mean is rounded to BF16, so a
+# different order can move the mean by one BF16 ulp on rare rows.  These
+# restatements sum in exactly the order each CUDA kernel uses, so a kernel can be
+# checked bit for bit: with the same order every other step is a correctly
+# rounded fp32 or BF16 operation on both sides.
+# --------------------------------------------------------------------------
+def _serial_sum(cols: torch.Tensor) -> torch.Tensor:
+    """fp32 sum over the last axis, one rounding per addition, left to right."""
+    acc = torch.zeros(cols.shape[:-1], dtype=torch.float32)
+    for j in range(cols.shape[-1]):
+        acc = acc + cols[..., j]
+    return acc
+
+
+def _xor_tree(lanes: torch.Tensor) -> torch.Tensor:
+    """An xor-shuffle butterfly over the last axis (a power of two, largest stride
+    first): lane l adds lane l ^ o; every lane ends with the same value."""
+    n = lanes.shape[-1]
+    idx = torch.arange(n)
+    o = n // 2
+    while o >= 1:
+        lanes = lanes + lanes[..., idx ^ o]
+        o //= 2
+    return lanes[..., 0]
+
+
+def sum_squares_in_kernel_order(squared: torch.Tensor, order: str) -> torch.Tensor:
+    """Row sums [R] of the fp32 values bf16(x^2) [R, C] in a kernel's order.
+
+    ``"row"``  -- the row kernels (one warp per row): lane l adds, in column order,
+                  the 8 columns of each of its vectors l, l+32, l+64, ...; then
+                  the 32-lane xor tree.
+    ``"head"`` -- the q/k head kernel and the QKV epilogue (C = 128): 16 lanes,
+                  lane l adds columns 8l..8l+7 in order; then the 16-lane tree.
+    ``"tiles"``-- a projection epilogue's per-256-column partials (each summed in
+                  column order) combined by ``h3_rms_modulate_sq``: lane l adds
+                  partials l, l+32, ... in order; then the 32-lane tree."""
+    r, c = squared.shape
+    sq = squared.float()
+    if order == "head":
+        lanes = _serial_sum(sq.view(r, 16, 8))
+        return _xor_tree(lanes)
+    if order == "row":
+        nvec = (c + 7) // 8
+        vpt = (nvec + 31) // 32
+        padded = torch.zeros(r, vpt * 32 * 8)
+        padded[:, :c] = sq
+        # element (k, lane, e) = column (lane + 32 k) * 8 + e; lane order: k major, then e
+        per_lane = padded.view(r, vpt, 32, 8).permute(0, 2, 1, 3).reshape(r, 32, vpt * 8)
+        return _xor_tree(_serial_sum(per_lane))
+    if order == "tiles":
+        nt = (c + 255) // 256
+        padded = torch.zeros(r, nt * 256)
+        padded[:, :c] = sq
+        partials = _serial_sum(padded.view(r, nt, 256))
+        k = (nt + 31) // 32
+        lanes = torch.zeros(r, k * 32)
+        lanes[:, :nt] = partials
+        return _xor_tree(_serial_sum(lanes.view(r, k, 32).transpose(1, 2)))
+    raise ValueError(f"unknown order {order!r}")
+
+
+def tile_square_partials(x: torch.Tensor) -> torch.Tensor:
+    """[R, ceil(C/256)] fp32: per 256-column tile, the column-order sum of
+    bf16(x^2) (what h3_linear_gated_residual_sq writes beside its output)."""
+    r, c = x.shape
+    nt = (c + 255) // 256
+    padded = torch.zeros(r, nt * 256)
+    padded[:, :c] = _r(x.float() * x.float()).float()
+    return _serial_sum(padded.view(r, nt, 256))
+
+
+def rms_norm_in_kernel_order(x: torch.Tensor, weight: torch.Tensor, eps: float, order: str) -> torch.Tensor:
+    """``rms_norm`` with the sum of squares taken in a CUDA kernel's order (see
+    ``sum_squares_in_kernel_order``); every other step as the reference stages it."""
+    lead = x.shape[:-1]
+    xf = x.float().reshape(-1, x.shape[-1])
+    squared = _r(xf * xf)
+    total = sum_squares_in_kernel_order(squared, order).unsqueeze(-1)
+    mean = _r(total / x.shape[-1])
+    variance = _r(mean.float() + torch.tensor(eps, dtype=torch.float32))
+    reciprocal = _r(1.0 / torch.sqrt(variance.float()))
+    out = _r(_r(xf * reciprocal.float()).float() * weight.float())
+    return out.view(*lead, x.shape[-1])
+
+
+def rms_modulate_in_kernel_order(x, weight, scale, shift, eps, order: str):
+    return modulate(rms_norm_in_kernel_order(x, weight, eps, order), scale, shift)
+
+
+def qk_norm_rope_in_kernel_order(x, weight, cos, sin, eps):
+    """``qk_norm_rope`` with the head kernel's sum order."""
+    normalized = rms_norm_in_kernel_order(x, weight, eps, "head")
+    extra = normalized.dim() - 2
+    c, s = cos, sin
+    for _ in range(extra - 1):
+        c, s = c.unsqueeze(1), s.unsqueeze(1)
+    return rope(normalized, c, s)
+
+
 def modulate(normalized: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor) -> torch.Tensor:
     """bf16(bf16(n * bf16(1 + scale)) + shift)."""
     factor = _r(scale.float() + 1.0)
@@ -145,6 +248,20 @@ def rotary_cache(positions: torch.Tensor, sections: Sequence[int] = (16, 16, 16)
         cols.append(positions[:, axis].float().unsqueeze(-1) * inverse.view(1, -1))
     angles = torch.cat(cols, dim=-1)
     return torch.cat((angles.cos(), angles.sin()), dim=-1).to(BF16)
+
+
+def rotary_cache_correctly_rounded(positions: torch.Tensor, sections: Sequence[int] = (16, 16, 16),
+                                   theta: float = 10000.0) -> torch.Tensor:
+    """``rotary_cache`` with cos/sin evaluated in float64 and rounded to fp32 once
+    (then to BF16), the way the CUDA table kernel evaluates them; the fp32 angles
+    are the reference's.  Host fp32 cos/sin are within an ulp of these values, so
+    the two tables differ in rare BF16 roundings only."""
+    cols = []
+    for axis, power in enumerate(rope_powers(sections, theta)):
+        inverse = 1.0 / power
+        cols.append(positions[:, axis].float().unsqueeze(-1) * inverse.view(1, -1))
+    angles = torch.cat(cols, dim=-1).double()
+    return torch.cat((angles.cos().float(), angles.sin().float()), dim=-1).to(BF16)
 
 
 def grid_positions(t: int, h: int, w: int) -> torch.Tensor:
@@ -285,6 +402,36 @@ def block_forward(x: torch.Tensor, modulation: torch.Tensor, weights: dict, cos:
     hidden = swiglu(gate_up[:, :f], gate_up[:, f:])
     mlp = linear(hidden, weights["w_down"])
     return gated_residual(residual, gate_mlp, mlp)
+
+
+def block_forward_rows(x: torch.Tensor, modulation: torch.Tensor, weights: dict, cos: torch.Tensor,
+                       sin: torch.Tensor, heads: int, rows: torch.Tensor, eps: float = 1e-6,
+                       qk_eps: float = 1e-6, segments=None) -> torch.Tensor:
+    """``block_forward`` evaluated for the token rows ``rows`` only, at any
+    sequence length: every op of the block is row-local except attention, whose
+    keys and values need all tokens -- so k and v are projected for every token
+    (one fp32-accumulated GEMM over all rows, the only all-token work), the
+    queries and everything after attention only for the requested rows.
+    Returns [len(rows), Hd]; equals ``block_forward(...)[rows]`` up to the GEMM
+    accumulation order of the all-token k/v product."""
+    n, hd = x.shape
+    d = hd // heads
+    mod = token_modulation(modulation, segments, n).reshape(n, 6, hd)
+    shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = (mod[:, i] for i in range(6))
+    normalized = rms_modulate(x, weights["norm1"], scale_msa, shift_msa, eps)
+    w_qkv = weights["w_qkv"]
+    kv = _r(normalized.float() @ w_qkv[hd:].float().t()).view(n, 2, heads, d)
+    k = qk_norm_rope(kv[:, 0], weights["norm_k"], cos, sin, qk_eps)
+    v = kv[:, 1]
+    q = qk_norm_rope(linear(normalized[rows], w_qkv[:hd]).view(-1, heads, d), weights["norm_q"], cos[rows],
+                     sin[rows], qk_eps)
+    attn = _r(attention_fp32(q[None], k[None], v[None], d ** -0.5)[0]).reshape(-1, hd)
+    residual = gated_residual(x[rows], gate_msa[rows], linear(attn, weights["w_o"]))
+    normalized2 = rms_modulate(residual, weights["norm2"], scale_mlp[rows], shift_mlp[rows], eps)
+    gate_up = linear(normalized2, weights["w_gate_up"])
+    f = gate_up.shape[1] // 2
+    hidden = swiglu(gate_up[:, :f], gate_up[:, f:])
+    return gated_residual(residual, gate_mlp[rows], linear(hidden, weights["w_down"]))
 
 
 # --------------------------------------------------------------------------

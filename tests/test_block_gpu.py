@@ -101,3 +101,49 @@ def test_graft_entry_smoke():
     """The smoke entry point the driver runs (one small block vs the CPU oracle)."""
     import __graft_entry__
     __graft_entry__.smoke()
+
+
+def _sample_rows(n, segments, count=256, seed=0):
+    """First/last rows, both sides of every segment boundary, the rest random."""
+    picks = {0, n - 1}
+    for start, length, _ in segments:
+        picks.update({start, max(start - 1, 0), start + length - 1, min(start + length, n - 1)})
+    g = torch.Generator().manual_seed(seed)
+    rest = torch.randperm(n, generator=g)[:count].tolist()
+    for r in rest:
+        if len(picks) >= count:
+            break
+        picks.add(r)
+    return torch.tensor(sorted(picks))
+
+
+@pytest.mark.parametrize("video_grid,cond", [((32, 24, 24), 0), ((32, 24, 24), 512)])
+def test_block_full_size_sampled_rows(h3, video_grid, cond):
+    """Benchmark config 3 (18432 tokens on the 32x24x24 grid, hidden 5120, 40 heads,
+    FFN 13824) and the config-5 joint sequence (+512 conditioning tokens, two
+    modulation segments): the whole block runs on the GPU; 256 sampled rows are
+    compared with the oracle, which evaluates the block for those rows only (their
+    queries attend over all keys).  Tolerance: max-abs-rel <= 2e-2 (the block's)."""
+    from h3b200.block import BlockConfig, Segment, Workspace, block_forward, random_block_weights
+    from h3b200.step import StepConfig, joint_positions
+    cfg = BlockConfig()
+    scfg = StepConfig(video_grid=video_grid, cond_tokens=cond)
+    n = scfg.tokens
+    segments = [(0, scfg.video_tokens, 0)] + ([(scfg.video_tokens, cond, 1)] if cond else [])
+    w = random_block_weights(cfg, DEV, seed=7, adaln=False)
+    for name in ("norm1", "norm2"):
+        getattr(w, name).copy_((torch.randn(cfg.hidden) * 0.1 + 1).bfloat16())
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn(n, cfg.hidden, generator=g).bfloat16()
+    mod = (torch.randn(2, 6 * cfg.hidden, generator=g) * 0.3).bfloat16()
+    table = O.rotary_cache(joint_positions(scfg))
+    cos, sin = table[:, :48], table[:, 48:]
+    ws = Workspace(n, cfg, DEV)
+    out = block_forward(x.to(DEV), mod.to(DEV), [Segment(*s) for s in segments], w, cos.to(DEV), sin.to(DEV),
+                        cfg, ws).cpu()
+    rows = _sample_rows(n, segments)
+    ref = O.block_forward_rows(x, mod, _oracle_weights(w), cos, sin, cfg.heads, rows, segments=segments)
+    err = O.max_abs_rel(out[rows], ref)
+    print(f"PARITY op=block tokens={n} sampled_rows={len(rows)} max_abs_rel={err:.3e}")
+    assert err <= 2e-2
+    assert h3.load().h3_device_error() == 0

@@ -69,3 +69,41 @@ def test_exchange_kernels_check_arguments(h3):
     outs = _descs([torch.zeros(10, 3, 128, dtype=torch.bfloat16, device=DEV) for _ in range(3)])
     args = [ctypes.byref(_lib.desc(t)) for t in (x, w, cs, cs)]
     assert lib.h3_qk_norm_rope_multi(outs, 3, *args, 1e-6, s) == 2                  # n != x.shape[1]
+
+
+@pytest.mark.parametrize("W,T,Hl,valid", [(4, 300, 5, 1190), (8, 2368, 5, 18944), (2, 181, 2, 361), (1, 257, 3, 257)])
+def test_mha_scatter_equals_mha_then_permute(h3, W, T, Hl, valid):
+    """The scatter epilogue stores row g of head h at row g % T of destination g // T,
+    head slot h: the same bits as h3_mha followed by the heads -> tokens permute
+    (destinations are slices of token-major return buffers [T, W, Hl, 128], this
+    rank's slot 1 of W)."""
+    from h3b200 import _lib
+    torch.manual_seed(W * 1000 + T)
+    q = torch.randn(1, W * T, Hl, 128, device=DEV).bfloat16()
+    k = torch.randn(1, valid, Hl, 128, device=DEV).bfloat16()
+    v = torch.randn(1, valid, Hl, 128, device=DEV).bfloat16()
+    ref = h3.mha(q, k, v)
+    slot = min(1, W - 1)
+    backs = [torch.full((T, W, Hl, 128), 7.0, dtype=torch.bfloat16, device=DEV) for _ in range(W)]
+    dsts = (_lib.H3Tensor * W)(*[_lib.desc(b[:, slot]) for b in backs])
+    _lib.call("h3_mha_scatter", dsts, W, _lib.desc(q), _lib.desc(k), _lib.desc(v), 128 ** -0.5, _lib.stream_of(q))
+    for p in range(W):
+        assert torch.equal(backs[p][:, slot], ref[0, p * T:(p + 1) * T]), f"destination {p}"
+        others = [s for s in range(W) if s != slot]
+        assert all(bool((backs[p][:, s] == 7.0).all()) for s in others), "stores outside the head slot"
+    assert h3.load().h3_device_error() == 0
+
+
+def test_mha_scatter_checks_arguments(h3):
+    from h3b200 import _lib
+    lib = h3.load()
+    q = torch.zeros(1, 100, 2, 128, dtype=torch.bfloat16, device=DEV)
+    s = _lib.stream_of(q)
+    few = (_lib.H3Tensor * 2)(*[_lib.desc(torch.zeros(40, 2, 128, dtype=torch.bfloat16, device=DEV))
+                                for _ in range(2)])
+    args = [ctypes.byref(_lib.desc(t)) for t in (q, q, q)]
+    assert lib.h3_mha_scatter(few, 2, *args, 0.1, s) == 2          # 2 x 40 rows < 100 queries
+    heads = (_lib.H3Tensor * 3)(*[_lib.desc(torch.zeros(40, 3, 128, dtype=torch.bfloat16, device=DEV))
+                                  for _ in range(3)])
+    assert lib.h3_mha_scatter(heads, 3, *args, 0.1, s) == 2        # head count differs from q's
+    assert lib.h3_mha_scatter(heads, 9, *args, 0.1, s) == 2        # more than 8 destinations

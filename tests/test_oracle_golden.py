@@ -111,3 +111,56 @@ def test_ulysses_permutation_roundtrip():
     for r in range(world):
         out = O.ulysses_scatter_back(returned[r], groups)  # [T, W, Hl, D]
         assert torch.equal(out.reshape(tokens, heads, d), locals_[r])
+
+
+def test_kernel_order_sums_match_hand_computation():
+    """The kernel-order restatements on a case small enough to add by hand."""
+    torch.manual_seed(0)
+    sq = O._r(torch.randn(3, 16) ** 2).float()
+    # row kernel: two vectors (lanes 0 and 1), each summed left to right, then the tree
+    lane0 = torch.zeros(3)
+    lane1 = torch.zeros(3)
+    for j in range(8):
+        lane0 = lane0 + sq[:, j]
+        lane1 = lane1 + sq[:, 8 + j]
+    assert torch.equal(O.sum_squares_in_kernel_order(sq, "row"), lane0 + lane1)
+    # tiles: one partial per 256 columns, here one tile
+    assert torch.equal(O.sum_squares_in_kernel_order(sq, "tiles"), O._serial_sum(sq))
+    assert O.tile_square_partials(torch.randn(2, 600).bfloat16()).shape == (2, 3)   # ragged last tile
+
+
+def test_kernel_order_sums_close_to_exact():
+    torch.manual_seed(1)
+    for width, order in ((1792, "row"), (5120, "row"), (5120, "tiles"), (128, "head")):
+        sq = O._r(torch.randn(64, width) ** 2).float()
+        exact = sq.double().sum(-1)
+        got = O.sum_squares_in_kernel_order(sq, order).double()
+        assert float(((got - exact) / exact).abs().max()) < 1e-5
+
+
+def test_tile_partials_feed_the_tile_order():
+    torch.manual_seed(2)
+    x = torch.randn(5, 5120).bfloat16()
+    partials = O.tile_square_partials(x)
+    assert partials.shape == (5, 20)
+    sq = O._r(x.float() * x.float()).float()
+    lanes = torch.zeros(5, 32)
+    lanes[:, :20] = partials
+    assert torch.equal(O._xor_tree(lanes), O.sum_squares_in_kernel_order(sq, "tiles"))
+
+
+def test_kernel_order_norm_equals_reference_on_most_rows():
+    """Only the fp32 sum order differs from the reference restatement: the BF16
+    outputs agree on nearly every element."""
+    torch.manual_seed(3)
+    x = torch.randn(512, 5120).bfloat16()
+    w = (torch.randn(5120) * 0.1 + 1).bfloat16()
+    for order in ("row", "tiles"):
+        d = O.bf16_ulp_distance(O.rms_norm_in_kernel_order(x, w, 1e-6, order), O.rms_norm(x, w, 1e-6))
+        assert int(d.max()) <= 1 and float((d == 0).float().mean()) > 0.99
+
+
+def test_correctly_rounded_rope_table_close_to_reference():
+    pos = O.grid_positions(8, 32, 32)
+    d = O.bf16_ulp_distance(O.rotary_cache_correctly_rounded(pos), O.rotary_cache(pos))
+    assert int(d.max()) <= 1
