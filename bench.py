@@ -179,17 +179,17 @@ def cpu_sample_step_seconds(sample_tokens=128, total_tokens=18944, blocks=40, se
     kv = w["kv"]
     t0 = time.perf_counter()
     nrm = O.rms_modulate(x, ones, mod[1], mod[0], 1e-6)
-    qkv = O.linear(nrm, w["w_qkv"]).view(n, 3, heads, d)
+    qkv = O.linear(nrm, w["w_qkv"], row_exact=False).view(n, 3, heads, d)
     q = O.qk_norm_rope(qkv[:, 0], torch.ones(d).bfloat16(), cos, sin, 1e-6)
     O.qk_norm_rope(qkv[:, 1], torch.ones(d).bfloat16(), cos, sin, 1e-6)
     t1 = time.perf_counter()
     attn = O.attention_fp32(q[None], kv, kv, d ** -0.5, chunk=n).bfloat16()[0].reshape(n, hd)
     t2 = time.perf_counter()
-    o = O.linear(attn, w["w_o"])
+    o = O.linear(attn, w["w_o"], row_exact=False)
     res, n2 = O.gated_residual_rms_modulate(x, mod[2], o, ones, mod[4], mod[3], 1e-6)
-    gu = O.linear(n2, w["w_gate_up"])
+    gu = O.linear(n2, w["w_gate_up"], row_exact=False)
     hidden = O.swiglu(gu[:, :f], gu[:, f:])
-    O.gated_residual(res, mod[5], O.linear(hidden, w["w_down"]))
+    O.gated_residual(res, mod[5], O.linear(hidden, w["w_down"], row_exact=False))
     t3 = time.perf_counter()
     per_block = (t3 - t0) * (total_tokens / n)
     return per_block * blocks, (t3 - t0)
@@ -348,8 +348,22 @@ def run_ours(args, rank, world, local_rank, group):
                                                                    out=ws.hidden)), 2.0 * t * 2 * fr * bc.hidden),
             "down": (time_call(lambda: ops.linear_(part, ws.hidden, w0.w_down)), 2.0 * t * fr * bc.hidden),
         }
+        norms = {}
     else:
         gemm = _sp_gemms(ops, ws, w0, t, bc, time_call, step.cos, step.sin)
+        norms = _sp_norms(ops, ws, w0, t, bc, time_call)
+
+    # device time of one eager step split by phase (every rank runs it; the
+    # exchange waits show how long a rank stands waiting for its slowest peer)
+    from h3b200 import phases as _phases
+    sync_all()
+    phase_ms = _phases.record(lambda: step.forward(x_dev))
+    sync_all()
+    names = sorted(phase_ms)
+    mine = torch.tensor([phase_ms[n] for n in names], dtype=torch.float64, device=device)
+    most = mine.clone()
+    if world > 1:
+        torch.distributed.all_reduce(most, op=torch.distributed.ReduceOp.MAX, group=group)
 
     # max over ranks
     vals = torch.tensor([dev_s, e2e_s, attn_ms], dtype=torch.float64, device=device)
@@ -384,6 +398,15 @@ def run_ours(args, rank, world, local_rank, group):
     for k, (ms, fl) in gemm.items():
         breakdown[k] = {"ms": round(ms, 3), "tflops": round(fl / (ms * 1e-3) / 1e12, 1),
                         "launches_per_step": args.blocks}
+    hbm = pk.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+    for k, (ms, nbytes) in norms.items():
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        breakdown[k] = {"ms": round(ms, 3), "gbs": round(gbs, 1), "frac_of_hbm": round(gbs / hbm, 3),
+                        "bytes_per_launch": int(nbytes),
+                        "launches_per_step": len(step.segments) * (2 * args.blocks - 1 if k == "rms_modulate_sq" else 1)}
+    per_block = args.blocks
+    phase_line = {n: {"rank0_ms_per_block": round(m / per_block, 3), "max_ms_per_block": round(x / per_block, 3)}
+                  for n, m, x in zip(names, mine.tolist(), most.tolist())}
     # model FLOPs of the step: all heads' attention over the joint sequence plus the
     # block GEMMs on all tokens (AdaLN GEMVs excluded)
     attn_total = 4.0 * cfg.tokens * cfg.tokens * bc.head_dim * bc.heads
@@ -405,6 +428,9 @@ def run_ours(args, rank, world, local_rank, group):
                      "traffic": traffic, "flop_per_launch": attn_flop, "ms_per_launch": round(attn_ms, 3)},
         "step_tflops": round(step_flop / dev_s / 1e12, 1),
         "kernels": breakdown,
+        "phases_eager": {"note": "one eager (not graph-replayed) step, device time between phase marks, "
+                                 "per block; wait_* = a rank waiting for its peers' exchange flags",
+                         **phase_line},
         "cuda_graph": graph_note,
         "clocks": clocks,
     }
@@ -468,17 +494,37 @@ def _sp_gemms(ops, ws, w0, t, bc, time_call, cos, sin):
     """The block's four projections on this rank's tokens (one GPU or sequence
     parallelism), each timed live as the step launches it: {name: (ms, flop)}.
     The QKV projection carries the q/k RMSNorm + RoPE in its epilogue (here
-    stored to local buffers)."""
+    stored to local buffers); the out- and down-projections carry the gated
+    residual and the per-tile sums of squares of their output."""
+    gate = ws.residual[0]
     return {
         "qkv_norm_rope": (time_call(lambda: ops.linear_qkv_norm_rope_([ws.q], [ws.k], [ws.v], ws.normalized,
                                                                         w0.w_qkv, w0.norm_q, w0.norm_k, cos, sin,
                                                                         bc.qk_eps)),
                           2.0 * t * 3 * bc.hidden * bc.hidden),
-        "out": (time_call(lambda: ops.linear_(ws.attn_out, ws.attn.view(t, -1), w0.w_o)), 2.0 * t * bc.hidden * bc.hidden),
+        "out_gated_residual_sq": (time_call(lambda: ops.linear_gated_residual_sq(
+            ws.attn.view(t, -1), w0.w_o, ws.out[0], gate, out=ws.residual, sq=ws.sq)), 2.0 * t * bc.hidden * bc.hidden),
         "gate_up_swiglu": (time_call(lambda: ops.linear_swiglu(ws.normalized2, w0.w_gate_up_packed, out=ws.hidden)),
                            2.0 * t * 2 * bc.ffn * bc.hidden),
-        "down_gated_residual": (time_call(lambda: ops.linear_gated_residual(
-            ws.hidden, w0.w_down, ws.residual, ws.residual[0], out=ws.out[1])), 2.0 * t * bc.ffn * bc.hidden),
+        "down_gated_residual_sq": (time_call(lambda: ops.linear_gated_residual_sq(
+            ws.hidden, w0.w_down, ws.residual, gate, out=ws.out[1], sq=ws.out_sq[1])), 2.0 * t * bc.ffn * bc.hidden),
+    }
+
+
+def _sp_norms(ops, ws, w0, t, bc, time_call):
+    """The step's RMSNorm + AdaLN passes on this rank's tokens, timed live:
+    {name: (ms, algorithmic bytes)}.  ``rms_modulate_sq`` is the element-wise pass
+    after each projection that wrote per-tile sums of squares (two per block);
+    ``rms_modulate`` the row kernel of the first block's input (once per step)."""
+    hd = bc.hidden
+    row = ws.residual[0]
+    nt = ws.sq.shape[1]
+    return {
+        "rms_modulate_sq": (time_call(lambda: ops.h3_rms_modulate_sq_(ws.normalized2, ws.residual, ws.sq, w0.norm2,
+                                                                      row, row, bc.eps)),
+                            t * hd * 2 * 2 + t * nt * 4),
+        "rms_modulate": (time_call(lambda: ops.h3_rms_modulate_(ws.normalized, ws.out[0], w0.norm1, row, row,
+                                                                bc.eps)), t * hd * 2 * 2),
     }
 
 
@@ -556,9 +602,9 @@ def run_gemm(args):
         from oracle import h3_oracle as O
         torch.set_num_threads(os.cpu_count() or 1)
         xc, wc = hx[:256], w_qkv.cpu()
-        O.linear(xc[:16], wc)
+        O.linear(xc[:16], wc, row_exact=False)
         t0 = time.perf_counter()
-        O.linear(xc, wc)
+        O.linear(xc, wc, row_exact=False)
         spent = time.perf_counter() - t0
         line["cpu_baseline"] = {"value": round(2.0 * 256 * 3 * hd * hd / spent / 1e12, 4), "unit": "TFLOP/s",
                                 "cores": torch.get_num_threads(), "cpu_model": cpu_model(), "kind": "port",

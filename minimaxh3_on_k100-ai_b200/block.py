@@ -5,13 +5,13 @@ Follows ``MiniMaxH3TransformerBlock::forward_segmented`` (patches/InfiniLM.patch
 1353-1397) and ``MiniMaxH3Transformer::forward`` (:1626-1826):
 
     per segment  n1  = h3_rms_modulate(x, norm1.w, scale_msa, shift_msa)      (K6)
-                 qkv = n1 W_qkv^T                                              (K10, tcgen05)
-                 q,k = h3_qk_norm_rope(qkv[q|k], norm_q/k.w, cos, sin)         (K2)
+                 q,k,v = n1 W_qkv^T, q/k RMSNorm + RoPE in the epilogue        (K10+K2, tcgen05)
                  a   = mha(q, k, v)                                            (K1, tcgen05)
-                 o   = a W_o^T                                                 (K10)
-    per segment  res, n2 = h3_gated_residual_rms_modulate(x, gate_msa, o, ...) (K8)
+    per segment  res = bf16(x + bf16(gate_msa * bf16(a W_o^T)))  + sums of squares   (K10+K8a)
+                 n2  = RMSNorm + AdaLN of res from those sums                  (K8b, element-wise)
                  h   = swiglu(n2 W_up^T, n2 W_gate^T)   (fused epilogue)       (K10+K9)
-    per segment  out = bf16(res + bf16(gate_mlp * bf16(h W_down^T)))          (K10+K7 fused)
+    per segment  out = bf16(res + bf16(gate_mlp * bf16(h W_down^T)))  + sums of squares (K10+K7)
+    (the next block's K6 then reads out's sums instead of reducing its rows again)
 
 Modulation columns are ordered shift_msa, scale_msa, gate_msa, shift_mlp,
 scale_mlp, gate_mlp (:1313-1318); a segment's row is broadcast over its tokens
@@ -27,6 +27,7 @@ from dataclasses import dataclass, field
 import torch
 
 from . import ops
+from .phases import mark
 
 
 @dataclass
@@ -153,6 +154,7 @@ def block_forward(x: torch.Tensor, modulation: torch.Tensor, segments: list[Segm
     t, hd = x.shape
     h, d = cfg.heads, cfg.head_dim
     out = ws.out[0] if out is None else out
+    mark("norm1")
     for s in segments:
         r = slice(s.start, s.start + s.length)
         if fused_norms and x_sq is not None:
@@ -162,6 +164,7 @@ def block_forward(x: torch.Tensor, modulation: torch.Tensor, segments: list[Segm
             ops.h3_rms_modulate_(ws.normalized[r], x[r], w.norm1, _col(modulation, 1, hd, s),
                                  _col(modulation, 0, hd, s), cfg.eps)
     if sp is None or sp.world == 1:
+        mark("qkv_norm_rope")
         if qkv_fused(h, cos):
             # one GEMM whose epilogue normalises and rotates q/k and stores q, k, v per head
             ops.linear_qkv_norm_rope_([ws.q], [ws.k], [ws.v], ws.normalized, w.w_qkv, w.norm_q, w.norm_k,
@@ -173,10 +176,12 @@ def block_forward(x: torch.Tensor, modulation: torch.Tensor, segments: list[Segm
             ops.h3_qk_norm_rope_(ws.q.unsqueeze(1), qkv[:, 0].unsqueeze(1), w.norm_q, cos, sin, cfg.qk_eps)
             ops.h3_qk_norm_rope_(ws.k.unsqueeze(1), qkv[:, 1].unsqueeze(1), w.norm_k, cos, sin, cfg.qk_eps)
             v = qkv[:, 2]
+        mark("attention")
         ops.mha_(ws.attn.unsqueeze(0), ws.q.unsqueeze(0), ws.k.unsqueeze(0), v.unsqueeze(0), 1.0 / math.sqrt(d))
         attn_flat = ws.attn.view(t, hd)
     else:
         attn_flat = sp.attention(ws.normalized, w.w_qkv, w.norm_q, w.norm_k, cos, sin, cfg.qk_eps)
+    mark("out_proj_norm")
     if fused_norms:
         for s in segments:
             r = slice(s.start, s.start + s.length)
@@ -191,7 +196,9 @@ def block_forward(x: torch.Tensor, modulation: torch.Tensor, segments: list[Segm
             ops.h3_gated_residual_rms_modulate_(ws.residual[r], ws.normalized2[r], x[r],
                                                 _col(modulation, 2, hd, s), ws.attn_out[r], w.norm2,
                                                 _col(modulation, 4, hd, s), _col(modulation, 3, hd, s), cfg.eps)
+    mark("gate_up_swiglu")
     ops.linear_swiglu(ws.normalized2, w.w_gate_up_packed, out=ws.hidden)
+    mark("down_gated_residual")
     for s in segments:
         r = slice(s.start, s.start + s.length)
         gate_mlp = modulation[s.row, 5 * hd:6 * hd]

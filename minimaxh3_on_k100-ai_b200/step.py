@@ -21,6 +21,7 @@ import torch
 from . import _lib, ops
 from .block import (BlockConfig, Segment, Workspace, adaln_modulation, add_bias, block_forward,
                     random_block_weights, random_time_embedder, segments_from_indices, time_embedding)
+from .health import bounded_collective, bounded_sync
 from .ulysses import SequenceParallel, local_rows
 
 # token tags video 0, text 1, audio 2 (patches/InfiniLM.patch:137); adaln row = 3 * timestep_index + tag (:1695-1697)
@@ -91,6 +92,10 @@ class BlockStack:
         self._ws: dict = {}
         self._sp: dict[tuple[int, int], SequenceParallel] = {}
         self._tp: dict = {}
+        # tensor parallelism: all-reduces chunked behind their GEMMs (same bits either way)
+        self.tp_overlap = True
+        # host-side bound on the step's collectives (a late or missing rank -> CollectiveTimeout)
+        self.collective_timeout_s = 120.0
 
     def workspace(self, tokens: int):
         if tokens not in self._ws:
@@ -144,7 +149,12 @@ class BlockStack:
         activated = ops.silu(temb, dtype=torch.bfloat16)
         local = torch.stack([add_bias(ops.linear(activated, w.w_adaln), w.b_adaln) for w in self.weights])
         gathered = torch.empty((self.world,) + tuple(local.shape), dtype=local.dtype, device=local.device)
-        dist.all_gather_into_tensor(gathered, local, group=self.group)
+        if local.is_cuda and torch.cuda.is_current_stream_capturing():
+            dist.all_gather_into_tensor(gathered, local, group=self.group)   # recorded into the graph
+        else:
+            # a peer that is late or gone becomes an error here, not a hang
+            bounded_collective(lambda: dist.all_gather_into_tensor(gathered, local, group=self.group, async_op=True),
+                               "AdaLN modulation all-gather", self.collective_timeout_s)
         blocks, t, n = local.shape
         full = gathered.permute(1, 2, 0, 3).reshape(blocks, t * self.world * n)   # rank-major columns
         rows = t * bc.modalities
@@ -168,7 +178,8 @@ class BlockStack:
             from .tp import tp_block_forward
             tp = self.tensor_parallel(h.shape[0])
             for i, w in enumerate(self.weights):
-                h = tp_block_forward(h, mods[i], segments, w, cos, sin, self.cfg, ws, tp, out=ws.out[i % 2])
+                h = tp_block_forward(h, mods[i], segments, w, cos, sin, self.cfg, ws, tp, out=ws.out[i % 2],
+                                     overlap=self.tp_overlap)
             return h
         sp = self.sequence_parallel(valid_tokens, h.shape[0])
         for i, w in enumerate(self.weights):
@@ -266,7 +277,9 @@ class DiTStep:
         if out_host is None:
             out_host = torch.empty(y.shape, dtype=y.dtype, pin_memory=True)
         out_host.copy_(y, non_blocking=True)
-        torch.cuda.current_stream(self.device).synchronize()
+        # bounded: a replayed graph whose exchange or collective waits on a missing
+        # peer raises DeviceTimeout here instead of blocking the host for good
+        bounded_sync(torch.cuda.current_stream(self.device), self.stack.collective_timeout_s, "DiTStep")
         self.check()
         return out_host
 

@@ -37,23 +37,46 @@ from .ulysses import PeerExchange
 
 
 class TensorParallel:
-    """All-reduce of a [tokens, hidden] BF16 partial over peer memory."""
+    """All-reduce of a [tokens, hidden] BF16 partial over peer memory.
+
+    ``allreduce_overlapped`` is the reference's chunked overlap
+    (``forward_overlapped``, patches/InfiniLM.patch:1399-1476, ``H3_TP_OVERLAP``):
+    the rows are cut into ``chunks`` row blocks; the producer (the row-parallel
+    GEMM) writes block c on the compute stream while block c-1 is being summed on
+    a side stream, so the exchange hides behind the next block's GEMM tiles.  Each
+    block's rows are split among the ranks; every row is summed exactly as in the
+    unchunked all-reduce (fp32, rank order, one rounding), so both give the same
+    bits."""
 
     SLOT_PARTIAL, SLOT_SUM = 0, 1
 
-    def __init__(self, world: int, rank: int, group, tokens: int, hidden: int, device):
+    def __init__(self, world: int, rank: int, group, tokens: int, hidden: int, device, chunks: int = 4):
         self.world, self.rank = world, rank
         nbytes = tokens * hidden * 2
         self.px = PeerExchange(world, rank, group, device, {"part": nbytes, "sum": nbytes})
         self.part = self.px.local("part", (tokens, hidden))
         self.sum = self.px.local("sum", (tokens, hidden))
-        chunk = (tokens + world - 1) // world
-        r0, r1 = min(tokens, rank * chunk), min(tokens, (rank + 1) * chunk)
-        self.rows = r1 - r0
-        shape = (self.rows, hidden)
-        self.srcs = (_lib.H3Tensor * world)(*[self.px.peer_desc(p, "part", shape, r0 * hidden) for p in range(world)])
-        self.dsts = (_lib.H3Tensor * world)(*[self.px.peer_desc(p, "sum", shape, r0 * hidden) for p in range(world)])
+        self.srcs, self.dsts, self.rows = self._owned(0, tokens, hidden)
         self.device = torch.device(device)
+        # row blocks of the overlapped form: multiples of the GEMM's 128-row tiles
+        per_block = -(-tokens // max(1, chunks))
+        step = max(128, -(-per_block // 128) * 128)
+        self.blocks = [(c0, min(tokens, c0 + step)) for c0 in range(0, tokens, step)]
+        self.block_descs = [self._owned(c0, c1, hidden) for c0, c1 in self.blocks]
+        self.side = torch.cuda.Stream(self.device) if self.device.type == "cuda" else None
+
+    def _owned(self, r0: int, r1: int, hidden: int):
+        """(srcs, dsts, rows): this rank's share of rows [r0, r1) in every rank's
+        partial (srcs) and sum (dsts) buffers, as mapped here."""
+        share = -(-(r1 - r0) // self.world)
+        a = min(r1, r0 + self.rank * share)
+        b = min(r1, a + share)
+        shape = (b - a, hidden)
+        srcs = (_lib.H3Tensor * self.world)(*[self.px.peer_desc(p, "part", shape, a * hidden)
+                                              for p in range(self.world)])
+        dsts = (_lib.H3Tensor * self.world)(*[self.px.peer_desc(p, "sum", shape, a * hidden)
+                                              for p in range(self.world)])
+        return srcs, dsts, b - a
 
     def allreduce(self) -> torch.Tensor:
         """Sum of every rank's ``self.part`` (written by the caller on the current
@@ -65,6 +88,32 @@ class TensorParallel:
             _lib.call("h3_peer_reduce_rows", self.dsts, self.srcs, self.world, stream)
         self.px.signal(self.SLOT_SUM, stream)
         self.px.wait(self.SLOT_SUM, stream)
+        return self.sum
+
+    def allreduce_overlapped(self, produce) -> torch.Tensor:
+        """``produce(r0, r1)`` writes rows [r0, r1) of ``self.part`` on the current
+        stream; returns ``self.sum`` (complete on the current stream).
+
+        Per row block: the compute stream produces it and raises this rank's
+        PARTIAL flag; the side stream waits for every peer's PARTIAL flag of that
+        block (the flags are epochs: a later value also covers this block), sums
+        this rank's share into every rank's sum buffer and raises SUM.  The
+        compute stream goes on with the next block meanwhile, and at the end waits
+        for every peer's SUM flag of the last block, which covers all blocks.
+        Buffer reuse is safe for the same reasons as ``allreduce``: nobody writes
+        a partial again before every rank has summed all blocks."""
+        main = torch.cuda.current_stream(self.device)
+        m, s = main.cuda_stream, self.side.cuda_stream
+        for (r0, r1), (srcs, dsts, rows) in zip(self.blocks, self.block_descs):
+            produce(r0, r1)
+            self.px.signal(self.SLOT_PARTIAL, m)
+            self.side.wait_stream(main)
+            self.px.wait(self.SLOT_PARTIAL, s)
+            if rows > 0:
+                _lib.call("h3_peer_reduce_rows", dsts, srcs, self.world, s)
+            self.px.signal(self.SLOT_SUM, s)
+        main.wait_stream(self.side)
+        self.px.wait(self.SLOT_SUM, m)
         return self.sum
 
     def close(self) -> None:
@@ -110,8 +159,10 @@ class TPWorkspace:
 
 def tp_block_forward(x: torch.Tensor, modulation: torch.Tensor, segments: list[Segment], w: BlockWeights,
                      cos: torch.Tensor, sin: torch.Tensor, cfg: BlockConfig, ws: TPWorkspace, tp: TensorParallel,
-                     out: torch.Tensor) -> torch.Tensor:
-    """One block on all tokens x [N, Hd] with this rank's weight slices."""
+                     out: torch.Tensor, overlap: bool = True) -> torch.Tensor:
+    """One block on all tokens x [N, Hd] with this rank's weight slices.  With
+    ``overlap`` the two all-reduces run chunked behind their GEMMs
+    (``TensorParallel.allreduce_overlapped``); the result is the same bits."""
     n, hd = x.shape
     d = cfg.head_dim
     hl = w.w_qkv.shape[0] // (3 * d)
@@ -130,16 +181,23 @@ def tp_block_forward(x: torch.Tensor, modulation: torch.Tensor, segments: list[S
         ops.h3_qk_norm_rope_(ws.k.unsqueeze(1), qkv[:, 1].unsqueeze(1), w.norm_k, cos, sin, cfg.qk_eps)
         v = qkv[:, 2]
     ops.mha_(ws.attn.unsqueeze(0), ws.q.unsqueeze(0), ws.k.unsqueeze(0), v.unsqueeze(0), 1.0 / math.sqrt(d))
-    ops.linear_(tp.part, ws.attn.view(n, hl * d), w.w_o)
-    o = tp.allreduce()
+    attn = ws.attn.view(n, hl * d)
+    if overlap:
+        o = tp.allreduce_overlapped(lambda r0, r1: ops.linear_(tp.part[r0:r1], attn[r0:r1], w.w_o))
+    else:
+        ops.linear_(tp.part, attn, w.w_o)
+        o = tp.allreduce()
     for s in segments:
         r = slice(s.start, s.start + s.length)
         ops.h3_gated_residual_rms_modulate_(ws.residual[r], ws.normalized2[r], x[r], _col(modulation, 2, hd, s),
                                             o[r], w.norm2, _col(modulation, 4, hd, s),
                                             _col(modulation, 3, hd, s), cfg.eps)
     ops.linear_swiglu(ws.normalized2, w.w_gate_up_packed, out=ws.hidden)
-    ops.linear_(tp.part, ws.hidden, w.w_down)
-    mlp = tp.allreduce()
+    if overlap:
+        mlp = tp.allreduce_overlapped(lambda r0, r1: ops.linear_(tp.part[r0:r1], ws.hidden[r0:r1], w.w_down))
+    else:
+        ops.linear_(tp.part, ws.hidden, w.w_down)
+        mlp = tp.allreduce()
     for s in segments:
         r = slice(s.start, s.start + s.length)
         ops.h3_gated_residual_(out[r], ws.residual[r], modulation[s.row, 5 * hd:6 * hd], mlp[r])

@@ -51,6 +51,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
+from .phases import mark
 
 
 @dataclass
@@ -289,6 +290,7 @@ class SequenceParallel:
         # tokens -> heads: block p (heads p*Hl..) of my tokens goes to slot r of rank p,
         # stored by the producing kernels themselves
         from .block import qkv_fused
+        mark("qkv_norm_rope_send")
         if qkv_fused(self.heads, cos):
             # the QKV GEMM's epilogue normalises/rotates q and k and stores every head row
             # into its destination rank's receive buffer (one launch for the whole send)
@@ -304,6 +306,7 @@ class SequenceParallel:
                       sin_d, float(qk_eps), stream)
             _lib.call("h3_copy_blocks", self.dst_v, w, _lib.desc(parts[:, 2].permute(1, 0, 2, 3).flatten(2)),
                       stream)
+        mark("wait_qkv")
         px.signal(self.SLOT_QKV, stream)
         px.wait(self.SLOT_QKV, stream)
         q = self.recv_p2p[0].view(1, w * t, hl, d)
@@ -311,8 +314,10 @@ class SequenceParallel:
         v = self.recv_p2p[2].view(1, w * t, hl, d)[:, :self.valid]
         # heads -> tokens: the attention epilogue stores each output row straight into
         # the return rows of the rank that owns its token (this rank's head slot)
+        mark("attention_send")
         _lib.call("h3_mha_scatter", self.dst_back, w, _lib.desc(q), _lib.desc(kk), _lib.desc(v),
                   1.0 / math.sqrt(d), stream)
+        mark("wait_out")
         px.signal(self.SLOT_OUT, stream)
         px.wait(self.SLOT_OUT, stream)
         return self.back_p2p.view(t, w * hl * d)

@@ -346,12 +346,16 @@ def ulysses_scatter_back(returned: Sequence[torch.Tensor], group_heads: Sequence
 # --------------------------------------------------------------------------
 # DiT block (patches/InfiniLM.patch:1303-1397)
 # --------------------------------------------------------------------------
-def linear(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+def linear(x: torch.Tensor, weight: torch.Tensor, row_exact: bool = True) -> torch.Tensor:
     """y = x W^T, BF16 in/out, fp32 accumulation (no bias on the block linears,
-    patches/InfiniLM.patch:734-741, 1163-1169).  The dot products are summed in
-    float64 and rounded to fp32 once, so a row's result does not depend on how
-    many rows the host BLAS is given (its fp32 kernels change the summation order
-    with the matrix shape), and equals a fp32 accumulation up to its rounding."""
+    patches/InfiniLM.patch:734-741, 1163-1169).  With ``row_exact`` the dot
+    products are summed in float64 and rounded to fp32 once, so a row's result
+    does not depend on how many rows the host BLAS is given (its fp32 kernels
+    change the summation order with the matrix shape) and equals a fp32
+    accumulation up to its rounding; without it, the reference's own CPU
+    composition (an fp32 BLAS product), which the CPU baseline times."""
+    if not row_exact:
+        return _r(x.float() @ weight.float().t())
     return _r((x.double() @ weight.double().t()).float())
 
 

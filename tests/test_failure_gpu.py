@@ -64,3 +64,24 @@ def test_exchange_wait_for_a_silent_peer_times_out():
     finally:
         torch.cuda.synchronize()
         assert lib.h3_ipc_free(ptr) == 0
+
+
+def test_bounded_host_sync_reports_slow_device_work():
+    """The host-side bound on a stream synchronisation: device work that outlasts
+    the bound (here a self-test wait of 300 ms, which itself ends by its own
+    limit) raises DeviceTimeout after ~50 ms instead of blocking the host; a
+    generous bound then succeeds and the device reports the self-test's expiry."""
+    import time
+
+    import h3b200
+    from h3b200.health import DeviceTimeout, bounded_sync
+    lib = h3b200.load()
+    assert lib.h3_device_error() == 0
+    stream = torch.cuda.current_stream()
+    assert lib.h3_selftest_wait_timeout(300_000_000, stream.cuda_stream) == 0
+    t0 = time.monotonic()
+    with pytest.raises(DeviceTimeout):
+        bounded_sync(stream, timeout_s=0.05, what="self-test")
+    assert time.monotonic() - t0 < 0.25
+    bounded_sync(stream, timeout_s=10.0, what="self-test")
+    assert lib.h3_device_error() == H3_ERR_TIMEOUT

@@ -115,7 +115,9 @@ def _worker(rank, world, port, path):
         x = _x(cfg).to(dev)
         out1 = step.forward(x).clone()
         out2 = step.forward(x).clone()
-        res["tp"] = (out1.cpu(), torch.equal(out1, out2))
+        step.stack.tp_overlap = False          # one unchunked all-reduce after each GEMM
+        out3 = step.forward(x).clone()
+        res["tp"] = (out1.cpu(), torch.equal(out1, out2), torch.equal(out1, out3))
         torch.cuda.synchronize()
         dist.barrier()
         step.close()
@@ -205,5 +207,6 @@ def test_tensor_parallel_matches_one(world, tmp_path_factory):
     outs = [r["tp"] for r in runs]
     for r in range(world):
         assert outs[r][1], f"rank {r}: two runs differ"
+        assert outs[r][2], f"rank {r}: the chunked, overlapped all-reduce differs from the unchunked one"
         assert torch.equal(outs[r][0], outs[0][0]), f"rank {r} differs from rank 0"
     assert O.max_abs_rel(outs[0][0], _one_gpu("tp")) <= 2e-2
