@@ -34,7 +34,10 @@
 // thread's commits track only its own MMAs), so one thread's barrier waits
 // overlap the other's issue; the tensor pipe's instruction queue is shallow.
 // Measured on B200 at [1,40,18432,128] this layout runs at ~1220 TFLOP/s against
-// ~1100 for P aliased into S in TMEM; 64-key tiles with double-buffered S (N=64
+// ~1100 for P aliased into S in TMEM, and 936 for P in TMEM with a single in-order
+// issuer (P_t(j) V_j then S_t(j+1)) and 1 in 4 exponentials on the FMA pipe -- there
+// the softmax of tile t waits for two products after its own, so the two Q tiles
+// cannot keep the tensor pipe fed; 64-key tiles with double-buffered S (N=64
 // MMAs run at half rate), a shared P tile, alternating the two softmax groups'
 // exponentials, and moving exponentials to the FMA pipe were all slower.
 //
@@ -519,339 +522,10 @@ __device__ __forceinline__ void fa_cta(const CUtensorMap &tq, const CUtensorMap 
     }
 }
 
-// ---------------------------------------------------------------------------
-// Variant T: P in tensor memory.
-//
-// Per key tile the shared-memory traffic of the kernel above is: S MMAs read Q and
-// K (128 KB for two Q tiles), P V reads P and V (128 KB), the softmax writes P
-// (64 KB) and TMA writes K and V (64 KB): 384 KB against 2048 cycles of MMA, i.e.
-// 188 B/clk where the SM's shared memory delivers 128 B/clk -- the tensor pipe can
-// be busy at most ~2/3 of the time.  Here the softmax writes P (BF16, two per
-// 32-bit column) over the first 64 columns of its own S accumulator with
-// tcgen05.st, and P V takes A from tensor memory: 256 KB per key tile, about what
-// the MMAs need.  The price is the alias: S_t(j+1) may only overwrite S_t's
-// columns after P_t(j) V_j has read them, so one thread issues both products in
-// the order P_t(j) V_j, S_t(j+1) (the tensor pipe executes one thread's MMAs in
-// issue order), and the softmax of tile t for key tile j+1 starts once S_t(j+1)
-// is in -- while the other tile's two products run, which is what keeps the
-// tensor pipe fed (ping-pong between the two Q tiles).  Exponentials alone need as
-// many MUFU cycles as the MMAs need tensor cycles, so H3_ATTN_TMEM_POLY of every 8
-// key pairs of a full tile are exponentiated on the FMA pipe (degree-3 polynomial,
-// exp2_poly2) to leave the MUFU slack.
-// Warp roles (384 threads): 0 TMA Q/K (2-slot K ring), 1 MMA issuer + TMEM owner,
-// 3 TMA V (2-slot V ring), 4..7 / 8..11 softmax + correction + epilogue of Q tile
-// 0 / 1.  Shared memory: Q 64 KB, K 64 KB, V 64 KB.
-// ---------------------------------------------------------------------------
-#ifndef H3_ATTN_TMEM_POLY
-#define H3_ATTN_TMEM_POLY 2
-#endif
-namespace vt {
-constexpr int KS = 2, VS = 2;
-constexpr int OFF_Q = 0;
-constexpr int OFF_K = OFF_Q + NQ * TILE;
-constexpr int OFF_V = OFF_K + KS * TILE;
-constexpr int OFF_BAR = OFF_V + VS * TILE;
-constexpr int NUM_BARS = 1 + 2 * KS + 2 * VS + 3 * NQ;
-constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 16 + 1024;
-static_assert(SMEM_BYTES <= 232448, "shared memory over the sm_100 per-block limit");
-constexpr int POLY = H3_ATTN_TMEM_POLY;
-}  // namespace vt
-
-template <int NQT>
-__device__ __forceinline__ void fa_cta_tmem(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv,
-                                            const CUtensorMap &to, const Params &p, const int h, const int b,
-                                            const int q0) {
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *sQ = smem + vt::OFF_Q;
-    uint8_t *sK = smem + vt::OFF_K;
-    uint8_t *sV = smem + vt::OFF_V;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + vt::OFF_BAR);
-    uint64_t *q_full = bars;
-    uint64_t *k_full = bars + 1;
-    uint64_t *k_empty = k_full + vt::KS;
-    uint64_t *v_full = k_empty + vt::KS;
-    uint64_t *v_empty = v_full + vt::VS;
-    uint64_t *s_full = v_empty + vt::VS;   // [t]: S_t(j) in TMEM (and every earlier MMA of tile t done)
-    uint64_t *p_ready = s_full + NQ;       // [t]: P_t(j) in TMEM, O_t rescaled
-    uint64_t *o_done = p_ready + NQ;       // [t]: the last P_t V has landed in O_t
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + vt::NUM_BARS);
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    constexpr int nq = NQT;
-    const int nkv = p.nkv;
-
-    if (threadIdx.x == 0) {
-        mbar_init(q_full, 1);
-        for (int i = 0; i < vt::KS; ++i) {
-            mbar_init(&k_full[i], 1);
-            mbar_init(&k_empty[i], 1);
-        }
-        for (int i = 0; i < vt::VS; ++i) {
-            mbar_init(&v_full[i], 1);
-            mbar_init(&v_empty[i], 1);
-        }
-        for (int t = 0; t < NQ; ++t) {
-            mbar_init(&s_full[t], 1);
-            mbar_init(&p_ready[t], 128);
-            mbar_init(&o_done[t], 1);
-        }
-        *abort_flag = 0;
-        fence_mbar_init();
-    }
-    if (warp == 1) {
-        tmem_alloc(tmem_slot, TMEM_COLS);
-        tmem_relinquish();
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
-
-    if (warp < 4) {
-        if ((warp == 0 || warp == 3) && lane == 0) {
-            // -------------------------------------------------------- TMA producers
-            const bool kq = warp == 0;   // warp 0: Q and K; warp 3: V
-            if (kq) {
-                tma_prefetch_desc(&tq);
-                tma_prefetch_desc(&tk);
-                mbar_expect_tx(q_full, nq * TILE);
-                for (int t = 0; t < nq; ++t)
-                    for (int hf = 0; hf < 2; ++hf)
-                        tma_load_4d(sQ + t * TILE + hf * HALF, &tq, q_full, hf * 64, q0 + t * BM, h, b);
-            } else {
-                tma_prefetch_desc(&tv);
-            }
-            auto prefetch = [&](int j) {
-                for (int hf = 0; hf < 2; ++hf) tma_prefetch_l2_4d(kq ? &tk : &tv, hf * 64, j * BN, h, b);
-            };
-            for (int j = 1; j < L2_AHEAD && j < nkv; ++j) prefetch(j);
-            uint8_t *ring = kq ? sK : sV;
-            uint64_t *full = kq ? k_full : v_full;
-            uint64_t *empty = kq ? k_empty : v_empty;
-            const CUtensorMap *map = kq ? &tk : &tv;
-            bool ok = true;
-            for (int j = 0; j < nkv && ok; ++j) {
-                if (j + L2_AHEAD < nkv) prefetch(j + L2_AHEAD);
-                const int slot = j & 1, use = j >> 1;   // KS == VS == 2
-                ok = mbar_wait(&empty[slot], (use & 1) ^ 1, abort_flag);
-                if (!ok) break;
-                mbar_expect_tx(&full[slot], TILE);
-                for (int hf = 0; hf < 2; ++hf)
-                    tma_load_4d(ring + slot * TILE + hf * HALF, map, &full[slot], hf * 64, j * BN, h, b);
-            }
-        } else if (warp == 1 && lane == 0) {
-            // -------------------------------------------------------- MMA issuer
-            constexpr uint32_t ID_S = idesc_bf16_f32(BM, BN, false);  // Q (K-major) x K (K-major)
-            constexpr uint32_t ID_PV = idesc_bf16_f32(BM, HD, true);  // P (TMEM) x V (MN-major)
-            const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
-            auto issue_s = [&](int t, int ks) {
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint32_t ka = (kk >> 2) * HALF + (kk & 3) * 32;
-                    umma_ss(tmem + t * BN, smem_desc_sw128(q_base + t * TILE + ka, 16, 1024),
-                            smem_desc_sw128(k_base + ks * TILE + ka, 16, 1024), ID_S, kk > 0 ? 1u : 0u);
-                }
-            };
-            // O_t += P_t V: A = P_t from columns [8 kk, 8 kk + 8) of S_t (16 keys per step)
-            auto issue_pv = [&](int t, int vs, bool acc) {
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk)
-                    umma_ts(tmem + O_COL + t * HD, tmem + t * BN + kk * 8,
-                            smem_desc_sw128(v_base + vs * TILE + kk * 2048, HALF, 1024), ID_PV,
-                            (acc || kk > 0) ? 1u : 0u);
-            };
-            bool ok = mbar_wait(q_full, 0, abort_flag) && mbar_wait(&k_full[0], 0, abort_flag);
-            if (ok) {
-                tc_fence_after();
-                for (int t = 0; t < nq; ++t) {
-                    issue_s(t, 0);
-                    umma_commit(&s_full[t]);
-                }
-                umma_commit(&k_empty[0]);
-            }
-            for (int j = 0; j < nkv && ok; ++j) {
-                const int vs = j & 1, ks = (j + 1) & 1;
-                ok = mbar_wait(&v_full[vs], (j >> 1) & 1, abort_flag);
-                for (int t = 0; t < nq && ok; ++t) {
-                    ok = mbar_wait(&p_ready[t], j & 1, abort_flag);
-                    if (!ok) break;
-                    if (t == 0 && j + 1 < nkv) ok = mbar_wait(&k_full[ks], ((j + 1) >> 1) & 1, abort_flag);
-                    if (!ok) break;
-                    tc_fence_after();
-                    issue_pv(t, vs, j > 0);
-                    if (j + 1 < nkv) {
-                        issue_s(t, ks);          // after P_t(j) V_j in this thread's issue order
-                        umma_commit(&s_full[t]);
-                    } else {
-                        umma_commit(&o_done[t]);
-                    }
-                }
-                if (!ok) break;
-                umma_commit(&v_empty[vs]);
-                if (j + 1 < nkv) umma_commit(&k_empty[ks]);
-            }
-            if (!ok) drain_in_flight();
-        }
-    } else if (((warp - 4) >> 2) < nq) {
-        // ------------------------------------------------------------ softmax / epilogue
-        const int t = (warp - 4) >> 2;
-        const int row = (warp & 3) * 32 + lane;
-        const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-        const uint32_t s_addr = tmem + t * BN + lane_off;
-        const uint32_t o_addr = tmem + O_COL + t * HD + lane_off;
-        const float c = p.scale_log2;
-        float m = -INFINITY, l = 0.f;
-        bool ok = true;
-        for (int j = 0; j < nkv; ++j) {
-            ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, abort_flag));
-            if (!ok) break;
-            tc_fence_after();
-            uint32_t s[BN];
-            tmem_ld32(s_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
-            tmem_ld32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
-            tmem_ld32(s_addr + 64, *reinterpret_cast<uint32_t(*)[32]>(&s[64]));
-            tmem_ld32(s_addr + 96, *reinterpret_cast<uint32_t(*)[32]>(&s[96]));
-            tmem_ld_wait();
-            const int valid = p.Sk - j * BN;
-            const bool full = valid >= BN;
-            if (!full) {
-#pragma unroll
-                for (int i = 0; i < BN; ++i)
-                    if (i >= valid) s[i] = __float_as_uint(-INFINITY);
-            }
-            float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
-#pragma unroll
-            for (int i = 0; i < BN; i += 8) {
-                mx0 = max3f(mx0, __uint_as_float(s[i]), __uint_as_float(s[i + 1]));
-                mx1 = max3f(mx1, __uint_as_float(s[i + 2]), __uint_as_float(s[i + 3]));
-                mx2 = max3f(mx2, __uint_as_float(s[i + 4]), __uint_as_float(s[i + 5]));
-                mx3 = max3f(mx3, __uint_as_float(s[i + 6]), __uint_as_float(s[i + 7]));
-            }
-            const float mnew = fmaxf(max3f(mx0, mx1, mx2), mx3) * c;
-            float alpha = 1.f;
-            bool rescale = false;
-            if (j == 0) {
-                m = mnew;
-            } else if (mnew > m + RESCALE_THRESHOLD) {
-                alpha = ex2(m - mnew);
-                m = mnew;
-                rescale = true;
-            }
-            const float neg_m = -m;
-            const uint64_t c2 = pk2(c, c), nm2 = pk2(neg_m, neg_m);
-            uint64_t rs0 = pk2(0.f, 0.f), rs1 = pk2(0.f, 0.f);
-            // P_t(j) over S_t(j)'s first 64 columns (S is in registers already): column i
-            // holds keys 2i (low half) and 2i + 1; written in two 32-column halves
-#pragma unroll
-            for (int hf = 0; hf < 2; ++hf) {
-                uint32_t w[32];
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int pi = 32 * hf + i;
-                    float x0, x1;   // s * c - m for a key pair, one packed FMA
-                    up2(ffma2(pk2(__uint_as_float(s[2 * pi]), __uint_as_float(s[2 * pi + 1])), c2, nm2), x0, x1);
-                    float p0, p1;
-                    if (full && (i & 7) < vt::POLY) {
-                        exp2_poly2(x0, x1, p0, p1);
-                    } else {
-                        p0 = ex2(x0);
-                        p1 = ex2(x1);
-                    }
-                    if (i & 1) rs1 = fadd2(rs1, pk2(p0, p1));
-                    else rs0 = fadd2(rs0, pk2(p0, p1));
-                    w[i] = pack_bf16x2(p0, p1);
-                }
-                tmem_st32(s_addr + 32 * hf, w);
-            }
-            float r0, r1, r2, r3;
-            up2(rs0, r0, r1);
-            up2(rs1, r2, r3);
-            l = l * alpha + ((r0 + r1) + (r2 + r3));
-            // O_t is idle here: S_t(j) landed after P_t(j-1) V_{j-1} (one issuer, in order),
-            // and P_t(j) V_j waits for this warpgroup's p_ready
-            if (__any_sync(0xffffffffu, rescale)) {
-#pragma unroll 1
-                for (int cc = 0; cc < 4; ++cc) {
-                    uint32_t o[32];
-                    tmem_ld32(o_addr + cc * 32, o);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                    tmem_st32(o_addr + cc * 32, o);
-                }
-            }
-            tmem_st_wait();
-            tc_fence_before();
-            mbar_arrive(&p_ready[t]);
-        }
-        if (ok) ok = mbar_wait(&o_done[t], 0, abort_flag);
-        ok = __all_sync(0xffffffffu, ok);
-        if (ok) {
-            tc_fence_after();
-            const float inv = 1.0f / l;
-            const uint32_t out_tile = smem_u32(sQ + t * TILE);  // Q_t is free once its last P V landed
-#pragma unroll 1
-            for (int cc = 0; cc < 4; ++cc) {
-                uint32_t o[32];
-                tmem_ld32(o_addr + cc * 32, o);
-                tmem_ld_wait();
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int chunk = (cc & 1) * 4 + q;
-                    st_shared_v4(out_tile + (cc >> 1) * HALF + swz(row, chunk),
-                                 pack_bf16x2(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv),
-                                 pack_bf16x2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv),
-                                 pack_bf16x2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv),
-                                 pack_bf16x2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
-                }
-            }
-            if (p.ndst > 0) {
-                named_bar_sync(1 + t, 128);
-                const int cch = row & 15;
-                const uint32_t tile = out_tile + (uint32_t)(cch >> 3) * HALF;
-#pragma unroll 4
-                for (int k = 0; k < BM / 8; ++k) {
-                    const int rr = (row >> 4) + 8 * k;
-                    const int g = q0 + t * BM + rr;
-                    if (g >= p.Sq) break;
-                    const int dq = g / p.rows_per_dst;
-                    const int tl = g - dq * p.rows_per_dst;
-                    const uint4 v = ld_shared_v4(tile + swz(rr, cch & 7));
-                    st_global_v4(p.dst[dq] + (int64_t)tl * p.d_row + (int64_t)h * p.d_head + 8 * cch, v);
-                }
-            } else {
-                fence_proxy_async_smem();
-                named_bar_sync(1 + t, 128);
-                if (row == 0 && q0 + t * BM < p.Sq) {
-                    tma_store_4d(&to, sQ + t * TILE, 0, q0 + t * BM, h, b);
-                    tma_store_4d(&to, sQ + t * TILE + HALF, 64, q0 + t * BM, h, b);
-                    tma_store_commit();
-                    tma_store_wait_all();
-                }
-            }
-        } else {
-            drain_in_flight();
-        }
-    }
-
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 1) {
-        __syncwarp();
-        tc_fence_after();
-        tmem_dealloc(tmem, TMEM_COLS);
-    }
-}
-
 // CTA -> (batch, head, first Q row, Q tiles): CTAs [0, split_from) own a pair of Q
 // tiles, the grid's last pairs run as two one-tile CTAs each.  Each kind runs its
 // own compile-time specialisation of the same tile code (the pair path carries no
-// run-time tile count), and a tile's arithmetic is the same in both.  VARIANT 0:
-// P through shared memory; 1: P in tensor memory.
-template <int VARIANT>
+// run-time tile count), and a tile's arithmetic is the same in both.
 __global__ void __launch_bounds__(THREADS, 1)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                   const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap to, Params p) {
@@ -867,13 +541,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     tile0 += (pair - hb * p.pairs) * NQ;
     const int left = p.tiles - tile0;   // Q tiles of this head from tile0 on
     if (left <= 0) return;              // second half of a split pair past Sq (uniform over the CTA)
-    if (VARIANT == 1) {
-        if (!single && left >= NQ) fa_cta_tmem<NQ>(tq, tk, tv, to, p, h, b, tile0 * BM);
-        else fa_cta_tmem<1>(tq, tk, tv, to, p, h, b, tile0 * BM);
-    } else {
-        if (!single && left >= NQ) fa_cta<NQ>(tq, tk, tv, to, p, h, b, tile0 * BM);
-        else fa_cta<1>(tq, tk, tv, to, p, h, b, tile0 * BM);
-    }
+    if (!single && left >= NQ) fa_cta<NQ>(tq, tk, tv, to, p, h, b, tile0 * BM);
+    else fa_cta<1>(tq, tk, tv, to, p, h, b, tile0 * BM);
 }
 
 }  // namespace attn
@@ -936,25 +605,15 @@ int launch_mha(const h3_tensor *out, const h3_tensor *q, const h3_tensor *k, con
     p.B = B;
     p.nkv = (Sk + attn::BN - 1) / attn::BN;
     p.scale_log2 = scale * 1.4426950408889634f;
-    // kernel variant: P through shared memory (0) or in tensor memory (1); the
-    // environment variable H3_ATTN_VARIANT=smem|tmem picks one (read once)
-    static const int variant = [] {
-        const char *v = getenv("H3_ATTN_VARIANT");
-        return (v && strcmp(v, "tmem") == 0) ? 1 : 0;
-    }();
-    const int smem_bytes = variant == 1 ? attn::vt::SMEM_BYTES : attn::SMEM_BYTES;
-    static std::atomic<bool> attr_set[2][64];
+    static std::atomic<bool> attr_set[64];
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return H3_ERR_UNSUPPORTED;
-    if (!attr_set[variant][dev].load()) {
-        const cudaError_t e =
-            variant == 1 ? cudaFuncSetAttribute(attn::fa_fwd_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                smem_bytes)
-                         : cudaFuncSetAttribute(attn::fa_fwd_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                smem_bytes);
-        if (e != cudaSuccess) return H3_ERR_LAUNCH;
-        attr_set[variant][dev].store(true);
+    if (!attr_set[dev].load()) {
+        if (cudaFuncSetAttribute(attn::fa_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 attn::SMEM_BYTES) != cudaSuccess)
+            return H3_ERR_LAUNCH;
+        attr_set[dev].store(true);
     }
     const int sms = num_sms();
     p.tiles = (Sq + attn::BM - 1) / attn::BM;
@@ -967,10 +626,7 @@ int launch_mha(const h3_tensor *out, const h3_tensor *q, const h3_tensor *k, con
     const int64_t ctas = npairs + split;
     if (ctas > (int64_t)0x7fffffff) return H3_ERR_UNSUPPORTED;
     p.split_from = (int)(npairs - split);
-    if (variant == 1)
-        attn::fa_fwd_kernel<1><<<(unsigned)ctas, attn::THREADS, smem_bytes, stream>>>(tq, tk, tv, to, p);
-    else
-        attn::fa_fwd_kernel<0><<<(unsigned)ctas, attn::THREADS, smem_bytes, stream>>>(tq, tk, tv, to, p);
+    attn::fa_fwd_kernel<<<(unsigned)ctas, attn::THREADS, attn::SMEM_BYTES, stream>>>(tq, tk, tv, to, p);
     return launch_status();
 }
 

@@ -123,7 +123,9 @@ __global__ void __launch_bounds__(EW_THREADS) ew_kernel(EwArgs args, FastDiv div
 // ===========================================================================
 // row ops: RMSNorm, RMSNorm+AdaLN, gated residual + RMSNorm+AdaLN, LN+AdaLN
 // ===========================================================================
-enum { ROW_RMS = 0, ROW_RMS_MOD = 1, ROW_RES_RMS_MOD = 2, ROW_LN_MOD = 3 };
+// ROW_RMS_MOD_SQ: ROW_RMS_MOD with the row's sum of squares taken from per-256-column
+// partial sums (written by a projection epilogue) instead of reduced here.
+enum { ROW_RMS = 0, ROW_RMS_MOD = 1, ROW_RES_RMS_MOD = 2, ROW_LN_MOD = 3, ROW_RMS_MOD_SQ = 4 };
 
 struct RowArgs {
     RowView x, gate, y, scale, shift;   // gate/y only for ROW_RES_RMS_MOD
@@ -131,6 +133,9 @@ struct RowArgs {
     int64_t wsc;
     RowViewMut out, residual;           // residual only for ROW_RES_RMS_MOD
     int64_t rows, n1, C;
+    const float *sq;                    // ROW_RMS_MOD_SQ: [rows, nt] partial sums, row stride ldsq
+    int64_t ldsq;
+    int nt;
     float eps;
 };
 
@@ -220,14 +225,20 @@ __device__ __forceinline__ void row_finish(const RowArgs &args, int64_t row, int
         shift_ln = -mul_rn(r, mean);  // y = x * rstd + (-rstd * mean), fused
     } else {
         float s = 0.f;
+        if (MODE == ROW_RMS_MOD_SQ) {
+            // lane l adds partials l, l + 32, ... in order; then the xor tree
+            const float *sqrow = args.sq + row * args.ldsq;
+            for (int i = lane; i < args.nt; i += 32) s = add_rn(s, sqrow[i]);
+        } else {
 #pragma unroll
-        for (int k = 0; k < VPT; ++k)
+            for (int k = 0; k < VPT; ++k)
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {   // bf16(x^2), summed in fp32 in column order
-                const uint32_t sq = bmul2(w32(v[k], i), w32(v[k], i));
-                s = add_rn(s, blo(sq));
-                s = add_rn(s, bhi(sq));
-            }
+                for (int i = 0; i < 4; ++i) {   // bf16(x^2), summed in fp32 in column order
+                    const uint32_t sq = bmul2(w32(v[k], i), w32(v[k], i));
+                    s = add_rn(s, blo(sq));
+                    s = add_rn(s, bhi(sq));
+                }
+        }
         const float mean = bf(__fdiv_rn(warp_sum(s), (float)C));
         const float var = bf(add_rn(mean, args.eps));
         r = bf(rsqrt_torch(var));
@@ -294,63 +305,12 @@ __global__ void __launch_bounds__(ROW_WARPS * 32) row_kernel(RowArgs args) {
     }
 }
 
-// ===========================================================================
-// RMSNorm + AdaLN from per-tile partial sums of squares (the norm half of the
-// reference's gated residual + RMSNorm + AdaLN, after a projection whose
-// epilogue wrote the residual and its partial sums: gemm EPI_GATED_RES_SQ)
-// ===========================================================================
+// Per-256-column partial sums of squares for ROW_RMS_MOD_SQ (h3_rms_modulate_sq):
 // sq[row][n] = fp32 sum, in column order, of bf16(x^2) over columns
-// [256 n, 256 n + 256) of the row.  The row's total: lane l sums partials
-// l, l + 32, ... in order, then the xor-16/8/4/2/1 tree (every lane ends with the
-// same value).  With the total known up front the pass is element-wise: one warp
-// per (row, 256-column tile), one 16-byte vector per lane, every load issued
-// before the 5-step reduction; no row is held in registers.
+// [256 n, 256 n + 256) of the row, as a projection epilogue writes them
+// (gemm EPI_GATED_RES_SQ).  The row's total: lane l adds partials l, l + 32, ...
+// in order, then the xor-16/8/4/2/1 tree.
 constexpr int SQ_TILE = 256;
-constexpr int SQ_WARPS = 8;
-
-struct SqArgs {
-    RowView x, scale, shift;
-    const __nv_bfloat16 *weight;
-    RowViewMut out;
-    const float *sq;
-    int64_t ldsq;
-    int nt;
-    int64_t rows, n1, C;
-    float eps;
-};
-
-__global__ void __launch_bounds__(SQ_WARPS * 32) rms_modulate_sq_kernel(SqArgs a, uint32_t units) {
-    const int lane = threadIdx.x & 31;
-    const uint32_t u = blockIdx.x * SQ_WARPS + (threadIdx.x >> 5);
-    if (u >= units) return;  // whole warp
-    const int64_t row = u / (uint32_t)a.nt;
-    const int tile = (int)(u - (uint32_t)row * (uint32_t)a.nt);
-    const int64_t vi = (int64_t)tile * (SQ_TILE / 8) + lane;
-    const bool has = vi * 8 < a.C;
-    uint4 x = make_uint4(0, 0, 0, 0), w = x, sc = x, sh = x;
-    if (has) {
-        x = *reinterpret_cast<const uint4 *>(a.x.p + row_offset(a.x.s0, a.x.s1, row, a.n1) + vi * 8);
-        w = *reinterpret_cast<const uint4 *>(a.weight + vi * 8);
-        sc = *reinterpret_cast<const uint4 *>(a.scale.p + row_offset(a.scale.s0, a.scale.s1, row, a.n1) + vi * 8);
-        sh = *reinterpret_cast<const uint4 *>(a.shift.p + row_offset(a.shift.s0, a.shift.s1, row, a.n1) + vi * 8);
-    }
-    const float *sqrow = a.sq + row * a.ldsq;
-    float s = 0.f;
-    for (int i = lane; i < a.nt; i += 32) s = add_rn(s, sqrow[i]);
-    s = warp_sum(s);
-    const float mean = bf(__fdiv_rn(s, (float)a.C));
-    const float var = bf(add_rn(mean, a.eps));
-    const uint32_t r2 = bsplat(bf(rsqrt_torch(var)));
-    if (!has) return;
-    const uint32_t one2 = 0x3f803f80u;  // (1.0, 1.0) in BF16
-    uint4 o;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {       // bf(bf(bf(x*r)*w) * bf(1 + scale)) + shift)
-        const uint32_t n = bmul2(bmul2(w32(x, i), r2), w32(w, i));
-        w32(o, i) = badd2(bmul2(n, badd2(w32(sc, i), one2)), w32(sh, i));
-    }
-    *reinterpret_cast<uint4 *>(a.out.p + row_offset(a.out.s0, a.out.s1, row, a.n1) + vi * 8) = o;
-}
 
 // ===========================================================================
 // per-head q/k RMSNorm + RoPE: a half-warp per 128-wide head row
@@ -721,30 +681,15 @@ extern "C" int h3_rms_modulate_sq(const h3_tensor *y, const h3_tensor *x, const 
              check_same_shape(shift, x));
     const int64_t C = x->shape[x->ndim - 1];
     H3_CHECK(check_weight(weight, C));
-    SqArgs a;
-    lead_dims(x, &a.rows, &a.n1);
-    a.C = C;
+    RowArgs a;
+    bool vec;
+    fill_row_args(a, y, x, weight, scale, shift, eps, &vec);
     a.nt = (int)((C + SQ_TILE - 1) / SQ_TILE);
     if (sq->ndim != 2 || sq->shape[0] != a.rows || sq->shape[1] != a.nt) return H3_ERR_BAD_SHAPE;
     if ((a.nt > 1 && sq->strides[1] != 1) || (a.rows > 1 && sq->strides[0] < a.nt)) return H3_ERR_BAD_LAYOUT;
-    // element-wise 16-byte path only: the operands come from a projection epilogue
-    if (!rows_vectorizable(y, 8) || !rows_vectorizable(x, 8) || !rows_vectorizable(scale, 8) ||
-        !rows_vectorizable(shift, 8) || weight->strides[0] != 1 || !aligned16(weight->data))
-        return H3_ERR_BAD_LAYOUT;
-    if (a.rows == 0 || C == 0) return H3_OK;
-    const int64_t units = a.rows * a.nt;
-    if (units > 0x7fffffffLL - SQ_WARPS) return H3_ERR_UNSUPPORTED;
-    a.x = rowview(x);
-    a.scale = rowview(scale);
-    a.shift = rowview(shift);
-    a.out = rowview_mut(y);
-    a.weight = static_cast<const __nv_bfloat16 *>(weight->data);
     a.sq = static_cast<const float *>(sq->data);
     a.ldsq = sq->strides[0];
-    a.eps = eps;
-    const unsigned grid = (unsigned)((units + SQ_WARPS - 1) / SQ_WARPS);
-    rms_modulate_sq_kernel<<<grid, SQ_WARPS * 32, 0, (cudaStream_t)stream>>>(a, (uint32_t)units);
-    return launch_status();
+    return launch_row<ROW_RMS_MOD_SQ>(a, vec, (cudaStream_t)stream);
 }
 
 static int head_launch(const h3_tensor *out, const h3_tensor *x, const h3_tensor *weight,
