@@ -64,7 +64,8 @@ typedef enum h3_status {
     H3_ERR_LAUNCH = 6,        /* the CUDA launch reported an error               */
     H3_ERR_DRIVER = 7,        /* a driver entry point could not be resolved      */
     H3_ERR_TIMEOUT = 8,       /* a bounded device-side wait gave up              */
-    H3_ERR_INDEX = 9          /* a row index was outside the indexed tensor      */
+    H3_ERR_INDEX = 9,         /* a row index was outside the indexed tensor      */
+    H3_ERR_TOO_LARGE = 10     /* request exceeds the library's static scratch    */
 } h3_status;
 
 /* A strided view.  strides are in ELEMENTS (not bytes); stride 0 broadcasts.
@@ -212,6 +213,30 @@ int h3_linear_gated_residual_rms_modulate(const h3_tensor *residual_out, const h
                                           const h3_tensor *gate, const h3_tensor *weight,
                                           const h3_tensor *scale, const h3_tensor *shift, float eps,
                                           const h3_tensor *workspace, void *stream);
+
+/* Capacity, in floats, of the scratch array behind the _noalloc entry point below
+ * (4 MiB of device memory on every GPU that loads the library, held until exit). */
+#define H3_NOALLOC_SQ_FLOATS (1 << 20)
+
+/* h3_linear_gated_residual_rms_modulate without the workspace argument, for callers
+ * that cannot allocate device memory where they call it: a host framework that owns
+ * every device allocation through its own planned pool, or a plugin boundary whose
+ * host side has no device allocator.  The per-tile sums of squares go to a fixed
+ * array in the library's device image instead (H3_NOALLOC_SQ_FLOATS floats), so a
+ * call needs M * ceil(N / 256) <= H3_NOALLOC_SQ_FLOATS (M = rows of residual_out,
+ * N = rows of w: up to 52428 tokens at width 5120); larger requests return
+ * H3_ERR_TOO_LARGE and launch nothing.  Allocates nothing and frees nothing.  The
+ * first call on a device looks up the array's device address with that device
+ * current; make that first call before any stream capture.  Every call shares the
+ * one array (each call writes every entry it reads, so leftovers of an earlier call
+ * do not matter), hence calls that can overlap on the GPU -- concurrent streams, or
+ * several host threads on one device -- race; serialise them.  No counterpart in the
+ * reference (its op wrappers allocate their outputs and need no scratch). */
+int h3_linear_gated_residual_rms_modulate_noalloc(const h3_tensor *residual_out, const h3_tensor *out,
+                                                  const h3_tensor *x, const h3_tensor *w,
+                                                  const h3_tensor *residual, const h3_tensor *gate,
+                                                  const h3_tensor *weight, const h3_tensor *scale,
+                                                  const h3_tensor *shift, float eps, void *stream);
 
 /* QKV projection with the q/k RMSNorm + RoPE of h3_qk_norm_rope applied in the GEMM
  * epilogue, each head row stored straight to its destination: x [T,K], w [3*H*128, K]

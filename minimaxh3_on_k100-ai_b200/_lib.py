@@ -24,6 +24,7 @@ _STATUS = {
     7: "driver entry point unavailable",
     8: "bounded device wait timed out",
     9: "row index outside the indexed tensor",
+    10: "request exceeds the library's static scratch capacity",
 }
 _DTYPES = {torch.bfloat16: 0, torch.float32: 1, torch.float64: 2, torch.int64: 3}
 
@@ -68,6 +69,7 @@ SIGNATURES = {
     "h3_linear_gated_residual_sq": [P, P, P, P, P, P, _V],
     "h3_rms_modulate_sq": [P, P, P, P, P, P, _F, _V],
     "h3_linear_gated_residual_rms_modulate": [P, P, P, P, P, P, P, P, P, _F, P, _V],
+    "h3_linear_gated_residual_rms_modulate_noalloc": [P, P, P, P, P, P, P, P, P, _F, _V],
     "h3_pack_gate_up": [P, P, _V],
     "h3_linear_qkv_norm_rope": [P, P, P, P, P, _I, P, P, P, P, _F, _V],
     "h3_linear_f32": [P, P, P, P, _V],

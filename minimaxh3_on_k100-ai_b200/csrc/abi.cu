@@ -21,6 +21,7 @@ extern "C" const char *h3_status_string(int status) {
         case H3_ERR_DRIVER: return "driver entry point unavailable";
         case H3_ERR_TIMEOUT: return "bounded device wait timed out";
         case H3_ERR_INDEX: return "row index outside the indexed tensor";
+        case H3_ERR_TOO_LARGE: return "request exceeds the library's static scratch capacity";
         default: return "unknown status";
     }
 }
