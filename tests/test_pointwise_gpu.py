@@ -1,11 +1,13 @@
 """Parity of the fused pointwise kernels (through the C-ABI) with the CPU oracle
 and with the reference's golden outputs.
 
-Tolerance: <= 1 BF16 ulp per element against the CPU oracle for the
+Tolerance: the reference's golden fixtures are matched bit for bit (0 ulp).
+Against the CPU oracle at benchmark sizes: <= 1 BF16 ulp per element for the
 element-wise ops (gated residual and RoPE are bit-exact), and for the
 normalising ops (RMS/LN + AdaLN, q/k norm + RoPE) every element within 3 ulps
 at the magnitude of its last add's operands with >= 99.99 % within 1 ulp of
-the output (see ``assert_close_ulp``).  The reference reaches 0 ulp against
+the output (see ``assert_close_ulp``); the same ops are bit-exact against the
+oracle summed in the kernels' order (test_parity_order_gpu.py).  The reference reaches 0 ulp against
 itself on one device; between CPU and GPU the fp32 sum order of the
 normalisation and fp32 exp differ, which flips single BF16 roundings.  The
 exact-match fraction is also checked so a systematic drift cannot pass.
@@ -94,13 +96,13 @@ def g(t):
 # ---------------------------------------------------------------------------
 def test_golden_rms(h3):
     x, w, eps, _ = GOLDEN["op_rms"]["args"]
-    assert_close_ulp(h3.h3_rms_norm(g(x), g(w), eps), GOLDEN["op_rms"]["reference"], min_exact=0.99)
+    assert torch.equal(h3.h3_rms_norm(g(x), g(w), eps).cpu(), GOLDEN["op_rms"]["reference"])
 
 
 def test_golden_rms_modulate(h3):
     x, w, eps, scale, shift, _ = GOLDEN["op_rms_modulate"]["args"]
     out = h3.h3_rms_modulate(g(x), g(w), g(scale), g(shift), eps)
-    assert_close_ulp(out, GOLDEN["op_rms_modulate"]["reference"], min_exact=0.99)
+    assert torch.equal(out.cpu(), GOLDEN["op_rms_modulate"]["reference"])
 
 
 def test_golden_gated_residual(h3):
@@ -113,7 +115,7 @@ def test_golden_gated_residual_rms_modulate(h3):
     x, gate, y, w, eps, scale, shift, _, _ = GOLDEN["op_gated_residual_rms_modulate"]["args"]
     res, out = h3.h3_gated_residual_rms_modulate(g(x), g(gate), g(y), g(w), g(scale), g(shift), eps)
     assert torch.equal(res.cpu(), GOLDEN["op_gated_residual_rms_modulate"]["residual"])
-    assert_close_ulp(out, GOLDEN["op_gated_residual_rms_modulate"]["reference"], min_exact=0.99)
+    assert torch.equal(out.cpu(), GOLDEN["op_gated_residual_rms_modulate"]["reference"])
 
 
 def test_golden_swiglu(h3):
@@ -132,19 +134,20 @@ def test_golden_qk_norm_rope_send_layout(h3):
     t, p, hs, d = x.shape
     send = torch.empty(p, t, hs, d, dtype=torch.bfloat16, device=DEV)
     h3.h3_qk_norm_rope_(send.permute(1, 0, 2, 3), g(x), g(w), g(cos), g(sin), eps)
-    mag = rope_mag(O.rms_norm(x, w, eps), cos, sin).permute(1, 0, 2, 3)
-    assert_close_ulp(send, GOLDEN["op_qk_norm_rope"]["reference"], min_exact=0.99, mag=mag)
+    assert torch.equal(send.cpu(), GOLDEN["op_qk_norm_rope"]["reference"])
 
 
 @pytest.mark.parametrize("family", ["grid_8_32_32", "integer", "uniform", "fine", "fine64"])
 def test_golden_rope_cache(h3, family):
     e = GOLDEN["rotary_cache"][family]
     out = h3.h3_rope_cache(g(e["positions"]), g(GOLDEN["rotary_cache"]["power"]))
-    assert_close_ulp(out, e["table"], min_exact=0.999)
+    assert torch.equal(out.cpu(), e["table"])
 
 
-def test_rope_cache_integer_grid_bit_exact(h3):
-    """Config-1 grid (8,32,32): integer positions; the table must match exactly."""
+def test_rope_cache_config1_grid_vs_host_fp32_table(h3):
+    """Config-1 grid (8,32,32) against the oracle table built with the host's fp32
+    cos/sin (which can differ from the correctly rounded values by an fp32 ulp):
+    within 1 BF16 ulp.  The bit-exact check is test_parity_order_gpu's."""
     pos = O.grid_positions(8, 32, 32)
     out = h3.h3_rope_cache(g(pos), h3.rope_powers()[:16].contiguous())
     assert_close_ulp(out, O.rotary_cache(pos), min_exact=0.9995)
