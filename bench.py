@@ -405,7 +405,8 @@ def run_ours(args, rank, world, local_rank, group):
                         "bytes_per_launch": int(nbytes),
                         "launches_per_step": len(step.segments) * (2 * args.blocks - 1 if k == "rms_modulate_sq" else 1)}
     per_block = args.blocks
-    phase_line = {n: {"rank0_ms_per_block": round(m / per_block, 3), "max_ms_per_block": round(x / per_block, 3)}
+    phase_line = {n: {"rank0_ms_per_step": round(m, 3), "rank0_ms_per_block": round(m / per_block, 3),
+                      "max_ms_per_block": round(x / per_block, 3)}
                   for n, m, x in zip(names, mine.tolist(), most.tolist())}
     # model FLOPs of the step: all heads' attention over the joint sequence plus the
     # block GEMMs on all tokens (AdaLN GEMVs excluded)
@@ -549,12 +550,16 @@ def run_gemm(args):
     hidden = rnd(n, f) * 50
     res = torch.empty(n, hd, dtype=torch.bfloat16, device=device)
     gate = rnd(hd)
+    sq = torch.empty(ops.sq_partials_shape(n, hd), dtype=torch.float32, device=device)
+    # the epilogues the step uses: the out- and down-projections add the gated
+    # residual and write the per-tile sums of squares for the norm pass after them
     gemms = {
         "qkv": (lambda: ops.linear_(qkv, x, w_qkv), 2.0 * n * 3 * hd * hd),
-        "out": (lambda: ops.linear_(o, x, w_o), 2.0 * n * hd * hd),
+        "out_gated_residual_sq": (lambda: ops.linear_gated_residual_sq(x, w_o, x, gate, out=o, sq=sq),
+                                  2.0 * n * hd * hd),
         "gate_up_swiglu": (lambda: ops.linear_swiglu(x, w_gu_packed, out=hidden), 2.0 * n * 2 * f * hd),
-        "down_gated_residual": (lambda: ops.linear_gated_residual(hidden, w_down, x, gate, out=res),
-                                2.0 * n * hd * f),
+        "down_gated_residual_sq": (lambda: ops.linear_gated_residual_sq(hidden, w_down, x, gate, out=res, sq=sq),
+                                   2.0 * n * hd * f),
     }
     stream = torch.cuda.current_stream(device)
     for fn, _ in gemms.values():

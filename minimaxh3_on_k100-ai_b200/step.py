@@ -22,6 +22,7 @@ from . import _lib, ops
 from .block import (BlockConfig, Segment, Workspace, adaln_modulation, add_bias, block_forward,
                     random_block_weights, random_time_embedder, segments_from_indices, time_embedding)
 from .health import bounded_collective, bounded_sync
+from .phases import mark
 from .ulysses import SequenceParallel, local_rows
 
 # token tags video 0, text 1, audio 2 (patches/InfiniLM.patch:137); adaln row = 3 * timestep_index + tag (:1695-1697)
@@ -143,6 +144,7 @@ class BlockStack:
         """Every block's modulation rows [timesteps*modalities, 6*Hd], computed up
         front (the reference's batched AdaLN, patches/InfiniLM.patch:1718-1761)."""
         bc = self.cfg
+        mark("adaln_modulations")
         if self.world == 1:
             return [adaln_modulation(temb, w, bc) for w in self.weights]
         import torch.distributed as dist

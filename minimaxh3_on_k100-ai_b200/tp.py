@@ -33,6 +33,7 @@ import torch
 
 from . import _lib, ops
 from .block import BlockConfig, BlockWeights, Segment, _col, qkv_fused
+from .phases import mark
 from .ulysses import PeerExchange
 
 
@@ -166,10 +167,12 @@ def tp_block_forward(x: torch.Tensor, modulation: torch.Tensor, segments: list[S
     n, hd = x.shape
     d = cfg.head_dim
     hl = w.w_qkv.shape[0] // (3 * d)
+    mark("norm1")
     for s in segments:
         r = slice(s.start, s.start + s.length)
         ops.h3_rms_modulate_(ws.normalized[r], x[r], w.norm1, _col(modulation, 1, hd, s),
                              _col(modulation, 0, hd, s), cfg.eps)
+    mark("qkv_norm_rope")
     if qkv_fused(hl, cos):
         ops.linear_qkv_norm_rope_([ws.q], [ws.k], [ws.v], ws.normalized, w.w_qkv, w.norm_q, w.norm_k, cos, sin,
                                   cfg.qk_eps)
@@ -180,24 +183,30 @@ def tp_block_forward(x: torch.Tensor, modulation: torch.Tensor, segments: list[S
         ops.h3_qk_norm_rope_(ws.q.unsqueeze(1), qkv[:, 0].unsqueeze(1), w.norm_q, cos, sin, cfg.qk_eps)
         ops.h3_qk_norm_rope_(ws.k.unsqueeze(1), qkv[:, 1].unsqueeze(1), w.norm_k, cos, sin, cfg.qk_eps)
         v = qkv[:, 2]
+    mark("attention")
     ops.mha_(ws.attn.unsqueeze(0), ws.q.unsqueeze(0), ws.k.unsqueeze(0), v.unsqueeze(0), 1.0 / math.sqrt(d))
+    mark("out_proj_allreduce")
     attn = ws.attn.view(n, hl * d)
     if overlap:
         o = tp.allreduce_overlapped(lambda r0, r1: ops.linear_(tp.part[r0:r1], attn[r0:r1], w.w_o))
     else:
         ops.linear_(tp.part, attn, w.w_o)
         o = tp.allreduce()
+    mark("norm2")
     for s in segments:
         r = slice(s.start, s.start + s.length)
         ops.h3_gated_residual_rms_modulate_(ws.residual[r], ws.normalized2[r], x[r], _col(modulation, 2, hd, s),
                                             o[r], w.norm2, _col(modulation, 4, hd, s),
                                             _col(modulation, 3, hd, s), cfg.eps)
+    mark("gate_up_swiglu")
     ops.linear_swiglu(ws.normalized2, w.w_gate_up_packed, out=ws.hidden)
+    mark("down_allreduce")
     if overlap:
         mlp = tp.allreduce_overlapped(lambda r0, r1: ops.linear_(tp.part[r0:r1], ws.hidden[r0:r1], w.w_down))
     else:
         ops.linear_(tp.part, ws.hidden, w.w_down)
         mlp = tp.allreduce()
+    mark("residual")
     for s in segments:
         r = slice(s.start, s.start + s.length)
         ops.h3_gated_residual_(out[r], ws.residual[r], modulation[s.row, 5 * hd:6 * hd], mlp[r])
