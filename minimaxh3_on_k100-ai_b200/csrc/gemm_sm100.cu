@@ -39,10 +39,21 @@ constexpr int B_BYTES = BN * BK * 2;  // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int THREADS = 256;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr int GROUP_N = 16;
+#ifndef H3_GEMM_GROUP_N
+#define H3_GEMM_GROUP_N 16
+#endif
+constexpr int GROUP_N = H3_GEMM_GROUP_N;   // column tiles per raster group
 constexpr int OFF_BAR = STAGES * STAGE_BYTES;
 constexpr int NUM_BARS = 2 * STAGES + 4;
 constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 16 + 1024;
+// EPI_QKV stages each epilogue warp's 32 head rows (8 KB) in shared memory, so that
+// the stores to the destination (often a peer's receive buffer over NVLink) go out
+// as whole 256-byte rows, 16 lanes per row, instead of 16-byte pieces of 32 rows
+constexpr int QKV_STAGE_WARP = 32 * 256;
+constexpr int OFF_QKV_STAGE = (OFF_BAR + NUM_BARS * 8 + 16 + 127) / 128 * 128;
+constexpr int SMEM_BYTES_QKV = OFF_QKV_STAGE + 4 * QKV_STAGE_WARP + 1024;
+static_assert(SMEM_BYTES_QKV <= 232448, "shared memory over the sm_100 per-block limit");
+__host__ __device__ constexpr int smem_bytes(int epi) { return epi == 3 ? SMEM_BYTES_QKV : SMEM_BYTES; }
 
 // EPI_GATED_RES_SQ: EPI_GATED_RES, plus the tile's share of the output row's sum
 // of squares for the RMSNorm that follows (sq[row][n] = fp32 sum over the tile's
@@ -86,6 +97,15 @@ __device__ __forceinline__ void tile_coords(const Params &p, int tile, int &m, i
 
 __device__ __forceinline__ void st_global_v4(void *ptr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(ptr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr)
+                 : "memory");
+    return v;
 }
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
@@ -224,8 +244,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         for (int i = 0; i < 16; ++i)   // the linear's BF16 output
                             xw[16 * cc + i] = pack2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
                     }
-                    if (!row_ok) continue;
-                    if (part < 2) {
+                    if (row_ok && part < 2) {
                         // RMSNorm over the head with the exact summation tree of the q/k
                         // kernel (16 partial sums of 8 columns, then a xor-8/4/2/1 tree)
                         float s16[16];
@@ -263,10 +282,30 @@ __global__ void __launch_bounds__(THREADS, 1)
                             xw[j + QKV_HW] = badd2(bmul2(b, cw[j]), bmul2(a, sw[j]));
                         }
                     }
-                    __nv_bfloat16 *dst = p.dst[part][dp] + (int64_t)row * p.drow + (int64_t)hloc * p.dhead;
+                    // this lane's row into the warp's staging rows (16-byte chunk c of row r at
+                    // chunk c ^ (r & 7): each 8-lane phase of a store or load hits 8 distinct
+                    // bank groups), then whole rows out: store q covers rows 2q and 2q + 1 of
+                    // the warp, 16 lanes (256 contiguous bytes) per row
+                    const uint32_t stage = smem_u32(smem + OFF_QKV_STAGE + wq * QKV_STAGE_WARP);
+                    if (row_ok) {
 #pragma unroll
-                    for (int q = 0; q < 16; ++q)
-                        st_global_v4(dst + 8 * q, xw[4 * q], xw[4 * q + 1], xw[4 * q + 2], xw[4 * q + 3]);
+                        for (int q = 0; q < 16; ++q)
+                            st_shared_v4(stage + lane * 256 + ((q ^ (lane & 7)) << 4), xw[4 * q], xw[4 * q + 1],
+                                         xw[4 * q + 2], xw[4 * q + 3]);
+                    }
+                    __syncwarp();
+                    const int c = lane & 15;
+#pragma unroll 4
+                    for (int q = 0; q < 16; ++q) {
+                        const int r = 2 * q + (lane >> 4);
+                        const int grow = m * BM + wq * 32 + r;
+                        if (grow < p.M) {
+                            const uint4 v = ld_shared_v4(stage + r * 256 + ((c ^ (r & 7)) << 4));
+                            st_global_v4(p.dst[part][dp] + (int64_t)grow * p.drow + (int64_t)hloc * p.dhead + 8 * c,
+                                         v.x, v.y, v.z, v.w);
+                        }
+                    }
+                    __syncwarp();   // the staging rows are rewritten by the next head
                 }
             } else if (EPI == EPI_SWIGLU) {
                 // accumulator columns [0,128) = up, [128,256) = gate of features n*128 + c
@@ -406,12 +445,12 @@ int launch_gemm(const h3_tensor *x, const h3_tensor *w, gemm::Params &p, cudaStr
     if (dev < 0 || dev >= 64) return H3_ERR_UNSUPPORTED;
     if (!attr_set[EPI][dev].load()) {
         if (cudaFuncSetAttribute(gemm::gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 gemm::SMEM_BYTES) != cudaSuccess)
+                                 gemm::smem_bytes(EPI)) != cudaSuccess)
             return H3_ERR_LAUNCH;
         attr_set[EPI][dev].store(true);
     }
     const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
-    gemm::gemm_kernel<EPI><<<grid, gemm::THREADS, gemm::SMEM_BYTES, stream>>>(ta, tb, p);
+    gemm::gemm_kernel<EPI><<<grid, gemm::THREADS, gemm::smem_bytes(EPI), stream>>>(ta, tb, p);
     return launch_status();
 }
 
