@@ -45,6 +45,7 @@ extern "C" {
 #define H3_MAX_DIMS 4
 #define H3_EXCHANGE_MAX_RANKS 8
 #define H3_EXCHANGE_SLOTS 4
+#define H3_MAX_SEGMENTS 4   /* modulation segments one *_segmented launch can take */
 #define H3_IPC_HANDLE_BYTES 64
 
 typedef enum h3_dtype {
@@ -202,6 +203,21 @@ int h3_linear_gated_residual_sq(const h3_tensor *out, const h3_tensor *sq, const
  * h3_gated_residual_rms_modulate (InfiniCore.patch:179-181, 992-1004). */
 int h3_rms_modulate_sq(const h3_tensor *y, const h3_tensor *x, const h3_tensor *sq, const h3_tensor *weight,
                        const h3_tensor *scale, const h3_tensor *shift, float eps, void *stream);
+
+/* Per-segment forms, one launch for all of a rank's modulation segments (the block's
+ * segmented application of the AdaLN rows, forward_segmented InfiniLM.patch:1353-1397,
+ * MiniMaxH3ModulationSegment :2041-2045): rows are split into nseg <= H3_MAX_SEGMENTS
+ * consecutive segments of seg_rows[s] rows (summing to M); segment s uses the
+ * contiguous [N] row gates[s] (resp. scales[s], shifts[s]).  Arithmetic per row is that
+ * of the single-segment entry points, so the result equals one launch per segment bit
+ * for bit.  sq may be NULL: then h3_linear_gated_residual_segmented writes no partial
+ * sums and h3_rms_modulate_segmented reduces the row itself (as h3_rms_modulate). */
+int h3_linear_gated_residual_segmented(const h3_tensor *out, const h3_tensor *sq, const h3_tensor *x,
+                                       const h3_tensor *w, const h3_tensor *residual, const h3_tensor *gates,
+                                       const int64_t *seg_rows, int32_t nseg, void *stream);
+int h3_rms_modulate_segmented(const h3_tensor *y, const h3_tensor *x, const h3_tensor *sq,
+                              const h3_tensor *weight, const h3_tensor *scales, const h3_tensor *shifts,
+                              const int64_t *seg_rows, int32_t nseg, float eps, void *stream);
 
 /* The out-projection fused with h3_gated_residual_rms_modulate (InfiniLM.patch:866 then
  * :1377-1390): residual_out = bf16(residual + bf16(gate * bf16(x w^T))) and

@@ -68,6 +68,8 @@ SIGNATURES = {
     "h3_linear_gated_residual": [P, P, P, P, P, _V],
     "h3_linear_gated_residual_sq": [P, P, P, P, P, P, _V],
     "h3_rms_modulate_sq": [P, P, P, P, P, P, _F, _V],
+    "h3_linear_gated_residual_segmented": [P, P, P, P, P, P, ctypes.POINTER(ctypes.c_int64), _I, _V],
+    "h3_rms_modulate_segmented": [P, P, P, P, P, P, ctypes.POINTER(ctypes.c_int64), _I, _F, _V],
     "h3_linear_gated_residual_rms_modulate": [P, P, P, P, P, P, P, P, P, _F, P, _V],
     "h3_linear_gated_residual_rms_modulate_noalloc": [P, P, P, P, P, P, P, P, P, _F, _V],
     "h3_pack_gate_up": [P, P, _V],

@@ -11,7 +11,9 @@ Follows ``MiniMaxH3TransformerBlock::forward_segmented`` (patches/InfiniLM.patch
                  n2  = RMSNorm + AdaLN of res from those sums                  (K8b, element-wise)
                  h   = swiglu(n2 W_up^T, n2 W_gate^T)   (fused epilogue)       (K10+K9)
     per segment  out = bf16(res + bf16(gate_mlp * bf16(h W_down^T)))  + sums of squares (K10+K7)
-    (the next block's K6 then reads out's sums instead of reducing its rows again)
+    (the next block's K6 then reads out's sums instead of reducing its rows again;
+    the "per segment" ops run as one launch over up to 4 segments, each row picking
+    its segment's modulation row)
 
 Modulation columns are ordered shift_msa, scale_msa, gate_msa, shift_mlp,
 scale_mlp, gate_mlp (:1313-1318); a segment's row is broadcast over its tokens
@@ -134,6 +136,22 @@ def _col(modulation: torch.Tensor, index: int, hidden: int, seg: Segment) -> tor
     return row.unsqueeze(0).expand(seg.length, hidden)
 
 
+MAX_SEGMENTS = 4   # modulation segments one segmented launch takes (H3_MAX_SEGMENTS)
+
+
+def _one_launch_segments(segments: list[Segment], tokens: int) -> list[int] | None:
+    """Segment lengths when the segments tile [0, tokens) in order and are few enough
+    for the one-launch (segmented) kernels, else None."""
+    if not segments or len(segments) > MAX_SEGMENTS:
+        return None
+    start = 0
+    for sg in segments:
+        if sg.start != start or sg.length < 0:
+            return None
+        start += sg.length
+    return [sg.length for sg in segments] if start == tokens else None
+
+
 def block_forward(x: torch.Tensor, modulation: torch.Tensor, segments: list[Segment], w: BlockWeights,
                   cos: torch.Tensor, sin: torch.Tensor, cfg: BlockConfig, ws: Workspace,
                   out: torch.Tensor | None = None, sp=None, x_sq: torch.Tensor | None = None,
@@ -154,15 +172,22 @@ def block_forward(x: torch.Tensor, modulation: torch.Tensor, segments: list[Segm
     t, hd = x.shape
     h, d = cfg.heads, cfg.head_dim
     out = ws.out[0] if out is None else out
+    # the norms and gated-residual projections run once over all segments when they fit
+    # the segmented launches (segment s uses modulation row s's column blocks)
+    lengths = _one_launch_segments(segments, t) if fused_norms else None
+    rows = (lambda i: [modulation[sg.row, i * hd:(i + 1) * hd] for sg in segments])  # noqa: E731
     mark("norm1")
-    for s in segments:
-        r = slice(s.start, s.start + s.length)
-        if fused_norms and x_sq is not None:
-            ops.h3_rms_modulate_sq_(ws.normalized[r], x[r], x_sq[r], w.norm1, _col(modulation, 1, hd, s),
-                                    _col(modulation, 0, hd, s), cfg.eps)
-        else:
-            ops.h3_rms_modulate_(ws.normalized[r], x[r], w.norm1, _col(modulation, 1, hd, s),
-                                 _col(modulation, 0, hd, s), cfg.eps)
+    if lengths is not None:
+        ops.h3_rms_modulate_segmented_(ws.normalized, x, x_sq, w.norm1, rows(1), rows(0), lengths, cfg.eps)
+    else:
+        for s in segments:
+            r = slice(s.start, s.start + s.length)
+            if fused_norms and x_sq is not None:
+                ops.h3_rms_modulate_sq_(ws.normalized[r], x[r], x_sq[r], w.norm1, _col(modulation, 1, hd, s),
+                                        _col(modulation, 0, hd, s), cfg.eps)
+            else:
+                ops.h3_rms_modulate_(ws.normalized[r], x[r], w.norm1, _col(modulation, 1, hd, s),
+                                     _col(modulation, 0, hd, s), cfg.eps)
     if sp is None or sp.world == 1:
         mark("qkv_norm_rope")
         if qkv_fused(h, cos):
@@ -182,7 +207,11 @@ def block_forward(x: torch.Tensor, modulation: torch.Tensor, segments: list[Segm
     else:
         attn_flat = sp.attention(ws.normalized, w.w_qkv, w.norm_q, w.norm_k, cos, sin, cfg.qk_eps)
     mark("out_proj_norm")
-    if fused_norms:
+    if lengths is not None:
+        ops.linear_gated_residual_segmented(attn_flat, w.w_o, x, rows(2), lengths, out=ws.residual, sq=ws.sq)
+        ops.h3_rms_modulate_segmented_(ws.normalized2, ws.residual, ws.sq, w.norm2, rows(4), rows(3), lengths,
+                                       cfg.eps)
+    elif fused_norms:
         for s in segments:
             r = slice(s.start, s.start + s.length)
             ops.linear_gated_residual_sq(attn_flat[r], w.w_o, x[r], modulation[s.row, 2 * hd:3 * hd],
@@ -199,6 +228,9 @@ def block_forward(x: torch.Tensor, modulation: torch.Tensor, segments: list[Segm
     mark("gate_up_swiglu")
     ops.linear_swiglu(ws.normalized2, w.w_gate_up_packed, out=ws.hidden)
     mark("down_gated_residual")
+    if lengths is not None:
+        ops.linear_gated_residual_segmented(ws.hidden, w.w_down, ws.residual, rows(5), lengths, out=out, sq=out_sq)
+        return out
     for s in segments:
         r = slice(s.start, s.start + s.length)
         gate_mlp = modulation[s.row, 5 * hd:6 * hd]

@@ -77,6 +77,11 @@ struct Params {
     int64_t ldg;            // 0 broadcasts one gate row
     float *sq;              // EPI_GATED_RES_SQ: [M, ceil(N / BN)] fp32 partial sums of squares
     int64_t ldsq;
+    // gated residual with per-segment gate rows (nseg > 0): rows [seg_end[s-1], seg_end[s])
+    // use the gate row gates[s] (one modulation row per segment, as the block applies them)
+    int nseg;
+    int seg_end[H3_MAX_SEGMENTS];
+    const __nv_bfloat16 *gates[H3_MAX_SEGMENTS];
     // EPI_QKV: accumulator column c = part * hcols + head * 128 + d (part 0/1/2 = q/k/v);
     // head h goes to destination h / hpd, head slot h % hpd
     int hcols, hpd;
@@ -338,6 +343,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
             } else {
                 float ssq = 0.f;   // EPI_GATED_RES_SQ: this row's sum of bf16(out^2) over the tile
+                // this row's gate row: strided view, or its segment's modulation row
+                const __nv_bfloat16 *grow_ptr = p.gate + (int64_t)row * p.ldg;
+                if (p.nseg > 0) {
+                    int s = 0;
+                    while (s + 1 < p.nseg && row >= p.seg_end[s]) ++s;
+                    grow_ptr = p.gates[s];
+                }
 #pragma unroll 1
                 for (int cc = 0; cc < BN / 32; ++cc) {
                     uint32_t v[32];
@@ -352,7 +364,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                                 w[i] = pack2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
                         } else {  // EPI_GATED_RES, EPI_GATED_RES_SQ
                             const __nv_bfloat16 *rp = p.res + (int64_t)row * p.ldr + col;
-                            const __nv_bfloat16 *gp = p.gate + (int64_t)row * p.ldg + col;
+                            const __nv_bfloat16 *gp = grow_ptr + col;
 #pragma unroll
                             for (int q = 0; q < 4; ++q) {
                                 const uint4 r4 = *reinterpret_cast<const uint4 *>(rp + 8 * q);
@@ -501,27 +513,48 @@ namespace {
 // out = bf16(residual + bf16(gate * bf16(x w^T))); with sq, also the per-tile
 // partial sums of squares of out (EPI_GATED_RES_SQ)
 int gated_residual_gemm(const h3_tensor *out, const h3_tensor *x, const h3_tensor *w, const h3_tensor *residual,
-                        const h3_tensor *gate, const h3_tensor *sq, cudaStream_t stream) {
+                        const h3_tensor *gate, const h3_tensor *sq, cudaStream_t stream,
+                        const h3_tensor *gates = nullptr, const int64_t *seg_rows = nullptr, int nseg = 0) {
     H3_CHECK(check_gemm_operands(out, x, w));
     H3_CHECK(check_bf16(residual));
-    H3_CHECK(check_bf16(gate));
     if (out->shape[0] != x->shape[0] || out->shape[1] != w->shape[0]) return H3_ERR_BAD_SHAPE;
     H3_CHECK(check_same_shape(residual, out));
-    H3_CHECK(check_same_shape(gate, out));
     if (out->shape[1] % 32 != 0) return H3_ERR_UNSUPPORTED;
-    if (residual->strides[1] != 1 || gate->strides[1] != 1 || !aligned16(residual->data) || !aligned16(gate->data) ||
-        residual->strides[0] % 8 != 0 || gate->strides[0] % 8 != 0)
+    if (residual->strides[1] != 1 || !aligned16(residual->data) || residual->strides[0] % 8 != 0)
         return H3_ERR_BAD_LAYOUT;
     gemm::Params p{};
     p.M = (int)x->shape[0];
     p.N = (int)w->shape[0];
     p.K = (int)x->shape[1];
+    if (nseg > 0) {
+        // one contiguous gate row [N] per segment of consecutive rows
+        if (!gates || !seg_rows) return H3_ERR_NULL;
+        if (nseg > H3_MAX_SEGMENTS) return H3_ERR_UNSUPPORTED;
+        int64_t end = 0;
+        for (int i = 0; i < nseg; ++i) {
+            H3_CHECK(check_bf16(&gates[i]));
+            if (gates[i].ndim != 1 || gates[i].shape[0] != out->shape[1]) return H3_ERR_BAD_SHAPE;
+            if ((out->shape[1] > 1 && gates[i].strides[0] != 1) || !aligned16(gates[i].data)) return H3_ERR_BAD_LAYOUT;
+            if (seg_rows[i] < 0) return H3_ERR_BAD_SHAPE;
+            end += seg_rows[i];
+            p.seg_end[i] = (int)end;
+            p.gates[i] = static_cast<const __nv_bfloat16 *>(gates[i].data);
+        }
+        if (end != out->shape[0]) return H3_ERR_BAD_SHAPE;
+        p.nseg = nseg;
+        p.gate = p.gates[0];
+        p.ldg = 0;
+    } else {
+        H3_CHECK(check_bf16(gate));
+        H3_CHECK(check_same_shape(gate, out));
+        if (gate->strides[1] != 1 || !aligned16(gate->data) || gate->strides[0] % 8 != 0) return H3_ERR_BAD_LAYOUT;
+        p.gate = static_cast<const __nv_bfloat16 *>(gate->data);
+        p.ldg = gate->strides[0];
+    }
     p.out = static_cast<__nv_bfloat16 *>(out->data);
     p.ldo = out->strides[0];
     p.res = static_cast<const __nv_bfloat16 *>(residual->data);
     p.ldr = residual->strides[0];
-    p.gate = static_cast<const __nv_bfloat16 *>(gate->data);
-    p.ldg = gate->strides[0];
     if (!sq) return launch_gemm<gemm::EPI_GATED_RES>(x, w, p, stream);
     H3_CHECK(check_desc(sq, H3_F32));
     const int64_t nt = (out->shape[1] + gemm::BN - 1) / gemm::BN;
@@ -537,6 +570,14 @@ int gated_residual_gemm(const h3_tensor *out, const h3_tensor *x, const h3_tenso
 extern "C" int h3_linear_gated_residual(const h3_tensor *out, const h3_tensor *x, const h3_tensor *w,
                                         const h3_tensor *residual, const h3_tensor *gate, void *stream) {
     return gated_residual_gemm(out, x, w, residual, gate, nullptr, (cudaStream_t)stream);
+}
+
+extern "C" int h3_linear_gated_residual_segmented(const h3_tensor *out, const h3_tensor *sq, const h3_tensor *x,
+                                                  const h3_tensor *w, const h3_tensor *residual,
+                                                  const h3_tensor *gates, const int64_t *seg_rows, int32_t nseg,
+                                                  void *stream) {
+    if (nseg < 1) return H3_ERR_BAD_SHAPE;
+    return gated_residual_gemm(out, x, w, residual, nullptr, sq, (cudaStream_t)stream, gates, seg_rows, nseg);
 }
 
 extern "C" int h3_linear_gated_residual_sq(const h3_tensor *out, const h3_tensor *sq, const h3_tensor *x,

@@ -136,6 +136,11 @@ struct RowArgs {
     const float *sq;                    // ROW_RMS_MOD_SQ: [rows, nt] partial sums, row stride ldsq
     int64_t ldsq;
     int nt;
+    // per-segment modulation rows (nseg > 0): rows [seg_end[s-1], seg_end[s]) use the
+    // contiguous scale / shift rows seg_scale[s] / seg_shift[s]
+    int nseg;
+    int64_t seg_end[H3_MAX_SEGMENTS];
+    const __nv_bfloat16 *seg_scale[H3_MAX_SEGMENTS], *seg_shift[H3_MAX_SEGMENTS];
     float eps;
 };
 
@@ -247,8 +252,15 @@ __device__ __forceinline__ void row_finish(const RowArgs &args, int64_t row, int
     // ---- normalise, weight, modulate, store ----
     const __nv_bfloat16 *srow = nullptr, *hrow = nullptr;
     if (MODE != ROW_RMS) {
-        srow = args.scale.p + row_offset(args.scale.s0, args.scale.s1, row, args.n1);
-        hrow = args.shift.p + row_offset(args.shift.s0, args.shift.s1, row, args.n1);
+        if (args.nseg > 0) {
+            int s = 0;
+            while (s + 1 < args.nseg && row >= args.seg_end[s]) ++s;
+            srow = args.seg_scale[s];
+            hrow = args.seg_shift[s];
+        } else {
+            srow = args.scale.p + row_offset(args.scale.s0, args.scale.s1, row, args.n1);
+            hrow = args.shift.p + row_offset(args.shift.s0, args.shift.s1, row, args.n1);
+        }
     }
     __nv_bfloat16 *orow = args.out.p + row_offset(args.out.s0, args.out.s1, row, args.n1);
     const uint32_t r2 = bsplat(r);
@@ -607,6 +619,10 @@ static int fill_row_args(RowArgs &a, const h3_tensor *out, const h3_tensor *x, c
     lead_dims(out, &a.rows, &a.n1);
     a.C = out->shape[out->ndim - 1];
     a.eps = eps;
+    a.sq = nullptr;
+    a.ldsq = 0;
+    a.nt = 0;
+    a.nseg = 0;
     *vec = rows_vectorizable(out, 8) && rows_vectorizable(x, 8) && (!scale || rows_vectorizable(scale, 8)) &&
            (!shift || rows_vectorizable(shift, 8)) &&
            (!weight || (weight->strides[0] == 1 && aligned16(weight->data)));
@@ -684,6 +700,49 @@ extern "C" int h3_rms_modulate_sq(const h3_tensor *y, const h3_tensor *x, const 
     RowArgs a;
     bool vec;
     fill_row_args(a, y, x, weight, scale, shift, eps, &vec);
+    a.nt = (int)((C + SQ_TILE - 1) / SQ_TILE);
+    if (sq->ndim != 2 || sq->shape[0] != a.rows || sq->shape[1] != a.nt) return H3_ERR_BAD_SHAPE;
+    if ((a.nt > 1 && sq->strides[1] != 1) || (a.rows > 1 && sq->strides[0] < a.nt)) return H3_ERR_BAD_LAYOUT;
+    a.sq = static_cast<const float *>(sq->data);
+    a.ldsq = sq->strides[0];
+    return launch_row<ROW_RMS_MOD_SQ>(a, vec, (cudaStream_t)stream);
+}
+
+extern "C" int h3_rms_modulate_segmented(const h3_tensor *y, const h3_tensor *x, const h3_tensor *sq,
+                                         const h3_tensor *weight, const h3_tensor *scales, const h3_tensor *shifts,
+                                         const int64_t *seg_rows, int32_t nseg, float eps, void *stream) {
+    H3_CHECK(check_bf16(y) ?: check_bf16(x));
+    H3_CHECK(check_rank(x, 2, 2) ?: check_same_shape(y, x));
+    if (!scales || !shifts || !seg_rows) return H3_ERR_NULL;
+    if (nseg < 1) return H3_ERR_BAD_SHAPE;
+    if (nseg > H3_MAX_SEGMENTS) return H3_ERR_UNSUPPORTED;
+    const int64_t C = x->shape[1];
+    H3_CHECK(check_weight(weight, C));
+    RowArgs a;
+    bool vec;
+    fill_row_args(a, y, x, weight, nullptr, nullptr, eps, &vec);
+    int64_t end = 0;
+    for (int i = 0; i < nseg; ++i) {
+        for (const h3_tensor *t : {&scales[i], &shifts[i]}) {
+            H3_CHECK(check_bf16(t));
+            if (t->ndim != 1 || t->shape[0] != C) return H3_ERR_BAD_SHAPE;
+            if ((C > 1 && t->strides[0] != 1) || !aligned16(t->data)) return H3_ERR_BAD_LAYOUT;
+        }
+        if (seg_rows[i] < 0) return H3_ERR_BAD_SHAPE;
+        end += seg_rows[i];
+        a.seg_end[i] = end;
+        a.seg_scale[i] = static_cast<const __nv_bfloat16 *>(scales[i].data);
+        a.seg_shift[i] = static_cast<const __nv_bfloat16 *>(shifts[i].data);
+    }
+    if (end != a.rows) return H3_ERR_BAD_SHAPE;
+    a.nseg = nseg;
+    // the segment rows are contiguous: the strided load path reads them with stride 1
+    a.scale.p = a.seg_scale[0];
+    a.shift.p = a.seg_shift[0];
+    a.scale.s0 = a.scale.s1 = a.shift.s0 = a.shift.s1 = 0;
+    a.scale.sc = a.shift.sc = 1;
+    if (!sq) return launch_row<ROW_RMS_MOD>(a, vec, (cudaStream_t)stream);
+    H3_CHECK(check_desc(sq, H3_F32));
     a.nt = (int)((C + SQ_TILE - 1) / SQ_TILE);
     if (sq->ndim != 2 || sq->shape[0] != a.rows || sq->shape[1] != a.nt) return H3_ERR_BAD_SHAPE;
     if ((a.nt > 1 && sq->strides[1] != 1) || (a.rows > 1 && sq->strides[0] < a.nt)) return H3_ERR_BAD_LAYOUT;

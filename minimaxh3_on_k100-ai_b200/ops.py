@@ -14,6 +14,7 @@ them (patches/InfiniLM.patch:1360-1364).
 """
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -29,7 +30,8 @@ __all__ = [
     "linear", "linear_", "linear_swiglu", "linear_gated_residual", "pack_gate_up",
     "linear_f32", "linear_f32_", "gather_rows", "gather_rows_", "index_copy_rows_", "silu", "silu_",
     "linear_qkv_norm_rope_", "linear_gated_residual_sq", "h3_rms_modulate_sq_",
-    "linear_gated_residual_rms_modulate", "sq_partials_shape",
+    "linear_gated_residual_rms_modulate", "sq_partials_shape", "linear_gated_residual_segmented",
+    "h3_rms_modulate_segmented_",
 ]
 
 
@@ -276,6 +278,36 @@ def h3_rms_modulate_sq_(out, x, sq, weight, scale, shift, eps):
     scale, shift = _rowlike(scale, x), _rowlike(shift, x)
     require_cuda(out, x, sq, weight, scale, shift)
     call("h3_rms_modulate_sq", desc(out), desc(x), desc(sq), desc(weight), desc(scale), desc(shift), float(eps),
+         stream_of(x))
+    return out
+
+
+def _segments(rows, lengths):
+    if len(rows) != len(lengths) or not rows:
+        raise ValueError("one modulation row per segment")
+    return _desc_array(rows), (ctypes.c_int64 * len(lengths))(*[int(n) for n in lengths]), len(rows)
+
+
+def linear_gated_residual_segmented(x, weight, residual, gates, lengths, out=None, sq=None):
+    """out = bf16(residual + bf16(gate_s * (x W^T))) with gate row ``gates[s]`` for the
+    ``lengths[s]`` rows of segment s (consecutive, one launch); with ``sq``, also the
+    per-tile sums of squares of out."""
+    if out is None:
+        out = torch.empty_like(residual)
+    g, n, k = _segments(gates, lengths)
+    require_cuda(out, sq, x, weight, residual, *gates)
+    call("h3_linear_gated_residual_segmented", desc(_flat(out)), desc(sq), desc(_flat(x)), desc(weight),
+         desc(_flat(residual)), g, n, k, stream_of(x))
+    return out
+
+
+def h3_rms_modulate_segmented_(out, x, sq, weight, scales, shifts, lengths, eps):
+    """h3_rms_modulate_ with scale/shift rows per segment of consecutive rows (one
+    launch); with ``sq`` the row sums of squares come from the partials."""
+    sc, n, k = _segments(scales, lengths)
+    sh, _, _ = _segments(shifts, lengths)
+    require_cuda(out, x, sq, weight, *scales, *shifts)
+    call("h3_rms_modulate_segmented", desc(out), desc(x), desc(sq), desc(weight), sc, sh, n, k, float(eps),
          stream_of(x))
     return out
 

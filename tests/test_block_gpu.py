@@ -147,3 +147,16 @@ def test_block_full_size_sampled_rows(h3, video_grid, cond):
     print(f"PARITY op=block tokens={n} sampled_rows={len(rows)} max_abs_rel={err:.3e}")
     assert err <= 2e-2
     assert h3.load().h3_device_error() == 0
+
+
+def test_block_one_launch_per_op_equals_per_segment_launches(h3, monkeypatch):
+    """The block's norms and gated-residual projections run once over all modulation
+    segments; forcing one launch per segment gives the same bits."""
+    import h3b200.block as B
+    from h3b200.block import BlockConfig
+    cfg = BlockConfig(hidden=1024, heads=8, ffn=2816)
+    out, _, (x, mod, w, cos, sin, ws, segs) = _run_block(h3, cfg, 640, [(0, 500, 0), (500, 12, 2), (512, 128, 1)], 3,
+                                                         seed=4)
+    monkeypatch.setattr(B, "MAX_SEGMENTS", 0)
+    per_segment = B.block_forward(x.to(DEV), mod.to(DEV), segs, w, cos.to(DEV), sin.to(DEV), cfg, ws).clone()
+    assert torch.equal(out, per_segment)

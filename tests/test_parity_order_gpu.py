@@ -163,3 +163,43 @@ def test_sq_entry_points_reject_bad_partials(h3):
     with pytest.raises(ValueError):   # wrong dtype
         h3.h3_rms_modulate_sq_(x.clone(), x, torch.zeros(16, 2, dtype=torch.float64, device=DEV), w, w, w, 1e-6)
     assert h3.load().h3_device_error() == 0
+
+
+# ---------------------------------------------------------------------------
+# one launch over all modulation segments == one launch per segment
+# ---------------------------------------------------------------------------
+def test_segmented_launches_equal_per_segment(h3):
+    m, n, k = 1000, 1280, 512
+    a, wt, res, _, nw, _, _ = [t.to(DEV) for t in _proj_case(m, n, k, 8)]
+    g = torch.Generator().manual_seed(9)
+    table = (torch.randn(3, 6 * n, generator=g) * 0.3).bfloat16().to(DEV)
+    lengths = [600, 13, 387]
+    starts = [0, 600, 613]
+    row = lambda s, i: table[s, i * n:(i + 1) * n]  # noqa: E731
+    # projection + gated residual (+ sums of squares)
+    seg_out = torch.empty(m, n, dtype=torch.bfloat16, device=DEV)
+    seg_sq = torch.empty(m, (n + 255) // 256, dtype=torch.float32, device=DEV)
+    h3.linear_gated_residual_segmented(a, wt, res, [row(s, 2) for s in range(3)], lengths, out=seg_out, sq=seg_sq)
+    plain = torch.empty_like(seg_out)
+    h3.linear_gated_residual_segmented(a, wt, res, [row(s, 2) for s in range(3)], lengths, out=plain)
+    ref_out, ref_sq = torch.empty_like(seg_out), torch.empty_like(seg_sq)
+    for s, (st, ln) in enumerate(zip(starts, lengths)):
+        r = slice(st, st + ln)
+        h3.linear_gated_residual_sq(a[r], wt, res[r], row(s, 2), out=ref_out[r], sq=ref_sq[r])
+    assert torch.equal(seg_out, ref_out) and torch.equal(seg_sq, ref_sq) and torch.equal(plain, ref_out)
+    # norm pass, from the partials and with its own reduction
+    for sq in (seg_sq, None):
+        seg = h3.h3_rms_modulate_segmented_(torch.empty_like(seg_out), seg_out, sq, nw,
+                                            [row(s, 1) for s in range(3)], [row(s, 0) for s in range(3)], lengths,
+                                            1e-6)
+        ref = torch.empty_like(seg_out)
+        for s, (st, ln) in enumerate(zip(starts, lengths)):
+            r = slice(st, st + ln)
+            if sq is None:
+                h3.h3_rms_modulate_(ref[r], seg_out[r], nw, row(s, 1), row(s, 0), 1e-6)
+            else:
+                h3.h3_rms_modulate_sq_(ref[r], seg_out[r], sq[r], nw, row(s, 1), row(s, 0), 1e-6)
+        assert torch.equal(seg, ref)
+    with pytest.raises(ValueError):   # the lengths must cover every row
+        h3.linear_gated_residual_segmented(a, wt, res, [row(0, 2)], [999], out=torch.empty_like(seg_out))
+    assert h3.load().h3_device_error() == 0
