@@ -259,7 +259,8 @@ int h3_linear_gated_residual_rms_modulate_noalloc(const h3_tensor *residual_out,
  * (rows [q | k | v], head-major), q_dsts / k_dsts / v_dsts arrays of ndst descriptors
  * [T, hpd, 128] (same strides; H = ndst * hpd, H even), head h to destination
  * h / hpd, slot h % hpd.  Destinations may be peers' receive buffers (the Ulysses
- * send).  cos/sin [T, 48].  Equal bit for bit to h3_linear followed by h3_qk_norm_rope. */
+ * send).  cos/sin [T, half], half = 48 (reference layout) or 64 (full-D 44/42/42 layout).
+ * Equal bit for bit to h3_linear followed by h3_qk_norm_rope. */
 int h3_linear_qkv_norm_rope(const h3_tensor *x, const h3_tensor *w, const h3_tensor *q_dsts,
                             const h3_tensor *k_dsts, const h3_tensor *v_dsts, int32_t ndst,
                             const h3_tensor *norm_q, const h3_tensor *norm_k, const h3_tensor *cos,

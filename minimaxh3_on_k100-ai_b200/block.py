@@ -126,8 +126,9 @@ class Workspace:
 
 def qkv_fused(heads: int, cos: torch.Tensor) -> bool:
     """Whether the QKV projection can carry the q/k norm + RoPE in its epilogue
-    (two heads per 256-column tile, the reference's 48 rotated pairs)."""
-    return heads % 2 == 0 and cos.shape[-1] == 48
+    (two heads per 256-column tile; the reference's 48 rotated pairs, or the 64 of
+    the full-D 44/42/42 layout)."""
+    return heads % 2 == 0 and cos.shape[-1] in (48, 64)
 
 
 def _col(modulation: torch.Tensor, index: int, hidden: int, seg: Segment) -> torch.Tensor:

@@ -56,13 +56,14 @@ constexpr int QKV_STAGE_WARP = 32 * 256;
 constexpr int OFF_QKV_STAGE = (OFF_BAR + NUM_BARS * 8 + 16 + 127) / 128 * 128;
 constexpr int SMEM_BYTES_QKV = OFF_QKV_STAGE + 4 * QKV_STAGE_WARP + 1024;
 static_assert(SMEM_BYTES_QKV <= 232448, "shared memory over the sm_100 per-block limit");
-__host__ __device__ constexpr int smem_bytes(int epi) { return epi == 3 ? SMEM_BYTES_QKV : SMEM_BYTES; }
+__host__ __device__ constexpr int smem_bytes(int epi) { return (epi == 3 || epi == 5) ? SMEM_BYTES_QKV : SMEM_BYTES; }
 
 // EPI_GATED_RES_SQ: EPI_GATED_RES, plus the tile's share of the output row's sum
 // of squares for the RMSNorm that follows (sq[row][n] = fp32 sum over the tile's
 // columns, in column order, of bf16(out^2)), so the norm pass needs no reduction.
-enum Epi { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_GATED_RES = 2, EPI_QKV = 3, EPI_GATED_RES_SQ = 4 };
-constexpr int NUM_EPI = 5;
+// EPI_QKV64: EPI_QKV for 64 rotated pairs (the full-D 44/42/42 RoPE layout).
+enum Epi { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_GATED_RES = 2, EPI_QKV = 3, EPI_GATED_RES_SQ = 4, EPI_QKV64 = 5 };
+constexpr int NUM_EPI = 6;
 constexpr int QKV_HALF = 48;              // rotated pairs per head (3 axes x 16 frequencies)
 constexpr int QKV_HW = QKV_HALF / 2;      // ... as packed BF16x2 words
 
@@ -221,12 +222,13 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint32_t tbase = tmem + acc * BN + lane_off;
             const int row = m * BM + wq * 32 + lane;
             const bool row_ok = row < p.M;
-            if (EPI == EPI_QKV) {
+            if (EPI == EPI_QKV || EPI == EPI_QKV64) {
                 // the tile's 256 columns are two heads of one part; this thread owns one token
-                uint32_t cw[QKV_HW], sw[QKV_HW];
+                constexpr int HW = (EPI == EPI_QKV64 ? 64 : QKV_HALF) / 2;   // rotated pairs as BF16x2 words
+                uint32_t cw[HW], sw[HW];
                 if (row_ok) {
 #pragma unroll
-                    for (int q = 0; q < QKV_HW / 4; ++q) {
+                    for (int q = 0; q < HW / 4; ++q) {
                         const uint4 c4 = *reinterpret_cast<const uint4 *>(p.cos + (int64_t)row * p.cs0 + 8 * q);
                         const uint4 s4 = *reinterpret_cast<const uint4 *>(p.sin + (int64_t)row * p.ss0 + 8 * q);
 #pragma unroll
@@ -284,10 +286,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                         }
                         // RoPE: y0 = bf(bf(a*c) + bf(-b*s)), y1 = bf(bf(b*c) + bf(a*s))
 #pragma unroll
-                        for (int j = 0; j < QKV_HW; ++j) {
-                            const uint32_t a = xw[j], b = xw[j + QKV_HW];
+                        for (int j = 0; j < HW; ++j) {
+                            const uint32_t a = xw[j], b = xw[j + HW];
                             xw[j] = badd2(bmul2(a, cw[j]), bmul2(bneg2(b), sw[j]));
-                            xw[j + QKV_HW] = badd2(bmul2(b, cw[j]), bmul2(a, sw[j]));
+                            xw[j + HW] = badd2(bmul2(b, cw[j]), bmul2(a, sw[j]));
                         }
                     }
                     // this lane's row into the warp's staging rows (16-byte chunk c of row r at
@@ -642,7 +644,8 @@ extern "C" int h3_linear_qkv_norm_rope(const h3_tensor *x, const h3_tensor *w, c
     for (const h3_tensor *cs : {cos, sin}) {
         H3_CHECK(check_bf16(cs));
         if (cs->ndim != 2 || cs->shape[0] != T) return H3_ERR_BAD_SHAPE;
-        if (cs->shape[1] != gemm::QKV_HALF) return H3_ERR_UNSUPPORTED;
+        if (cs->shape[1] != gemm::QKV_HALF && cs->shape[1] != 64) return H3_ERR_UNSUPPORTED;
+        if (cs->shape[1] != cos->shape[1]) return H3_ERR_BAD_SHAPE;
         if (cs->strides[1] != 1 || (T > 1 && cs->strides[0] % 8 != 0) || !aligned16(cs->data)) return H3_ERR_BAD_LAYOUT;
     }
     p.M = (int)T;
@@ -659,6 +662,7 @@ extern "C" int h3_linear_qkv_norm_rope(const h3_tensor *x, const h3_tensor *w, c
     p.cs0 = cos->strides[0];
     p.ss0 = sin->strides[0];
     p.eps = eps;
+    if (cos->shape[1] == 64) return launch_gemm<gemm::EPI_QKV64>(x, w, p, (cudaStream_t)stream);
     return launch_gemm<gemm::EPI_QKV>(x, w, p, (cudaStream_t)stream);
 }
 

@@ -133,10 +133,12 @@ def test_bad_k_rejected(h3):
         h3.linear(x, torch.zeros(32, 64, dtype=torch.bfloat16, device=DEV))
 
 
+@pytest.mark.parametrize("sections", [(16, 16, 16), (22, 21, 21)], ids=["half48", "half64"])
 @pytest.mark.parametrize("T,H,K,ndst", [(300, 4, 512, 1), (1000, 40, 5120, 1), (257, 8, 256, 2), (130, 10, 640, 5)])
-def test_qkv_norm_rope_epilogue_equals_unfused(T, H, K, ndst):
+def test_qkv_norm_rope_epilogue_equals_unfused(T, H, K, ndst, sections):
     """The QKV GEMM with q/k RMSNorm + RoPE in its epilogue, each head stored to its
-    destination, equals h3_linear followed by h3_qk_norm_rope bit for bit."""
+    destination, equals h3_linear followed by h3_qk_norm_rope bit for bit, for the
+    reference's 48 rotated pairs and the 64 of the full-D layout."""
     import h3b200
     from h3b200 import ops
     from oracle import h3_oracle as O
@@ -145,8 +147,9 @@ def test_qkv_norm_rope_epilogue_equals_unfused(T, H, K, ndst):
     w = (torch.randn(3 * H * 128, K, device="cuda") * K ** -0.5).bfloat16()
     nq = (torch.randn(128, device="cuda") * 0.1 + 1).bfloat16()
     nk = (torch.randn(128, device="cuda") * 0.1 + 1).bfloat16()
-    table = O.rotary_cache(O.grid_positions(1, 1, T)).cuda()
-    cos, sin = table[:, :48], table[:, 48:]
+    table = O.rotary_cache(O.grid_positions(1, 1, T), sections).cuda()
+    half = table.shape[1] // 2
+    cos, sin = table[:, :half], table[:, half:]
     hpd = H // ndst
     outs = [[torch.empty(T, hpd, 128, dtype=torch.bfloat16, device="cuda") for _ in range(ndst)] for _ in range(3)]
     ops.linear_qkv_norm_rope_(outs[0], outs[1], outs[2], x, w, nq, nk, cos, sin, 1e-6)
