@@ -51,6 +51,9 @@ def parse():
     p.add_argument("--workload", choices=["step", "attention", "pointwise", "gemm"], default="step",
                    help="step: BASELINE config 5 (default, the headline); attention: config 2; "
                         "pointwise: config 1 op set; gemm: the block's four projections at config 3")
+    p.add_argument("--gemm-variant", type=int, choices=[0, 1, 2], default=0,
+                   help="projection tile form: 0 chosen per launch (default), 1 single-CTA 128-row tiles, "
+                        "2 CTA-pair 256-row tiles")
     return p.parse_args()
 
 
@@ -827,6 +830,9 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "ours" and args.gemm_variant:
+        import h3b200
+        h3b200.load().h3_gemm_variant(args.gemm_variant)
     if args.workload != "step" and args.impl == "ours":
         if rank == 0:
             runner = {"attention": run_attention, "pointwise": run_pointwise, "gemm": run_gemm}[args.workload]

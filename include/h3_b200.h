@@ -21,6 +21,7 @@
  *   h3_timestep_embedding          InfiniCore.patch:223-252 (infiniopTimestepEmbedding C API)
  *   h3_linear*                     InfiniCore.patch:1231-1292 (linear.cc) + the fused
  *                                  epilogues of InfiniLM.patch:1172-1179, 1377-1394
+ *   h3_adaln_projection            InfiniLM.patch:1260-1279 (AdaLN projection linear + bias)
  *   h3_linear_f32                  linear_forward on the F32 modules (proj_in, audio_proj_in,
  *                                  proj_out, audio_proj_out, time embedder),
  *                                  InfiniLM.patch:1501-1517, 1662-1664, 1812-1814
@@ -94,6 +95,14 @@ int h3_device_error(void);
  * the kernel ends normally, and the next h3_device_error() returns
  * H3_ERR_TIMEOUT.  No fault, trap or hang is involved.  No reference counterpart. */
 int h3_selftest_wait_timeout(uint64_t limit_ns, void *stream);
+
+/* Tile form of the projections (every h3_linear* entry point): 0 = chosen per
+ * launch (CTA-pair 256-row tiles unless they pad M by more than 1/64 over
+ * 128-row tiles), 1 = single-CTA 128-row tiles, 2 = CTA-pair tiles.  Both forms
+ * give bitwise the same results.  Returns the previous setting, or
+ * H3_ERR_BAD_SHAPE for a value outside 0..2 (setting unchanged).  A tuning and
+ * test hook; no reference counterpart. */
+int h3_gemm_variant(int variant);
 
 /* ---------------- fused pointwise ops (BF16, reference rounding) ---------------- */
 
@@ -269,6 +278,15 @@ int h3_linear_qkv_norm_rope(const h3_tensor *x, const h3_tensor *w, const h3_ten
 /* Reorder the [up; gate] rows of a gate_up weight [2F,K] into 128-row blocks
  * [up_0 | gate_0 | up_1 | gate_1 ...] consumed by h3_linear_swiglu. */
 int h3_pack_gate_up(const h3_tensor *dst, const h3_tensor *src, void *stream);
+
+/* AdaLN projection of the blocks' conditioning (MiniMaxH3AdaLNProjection::forward,
+ * InfiniLM.patch:1260-1279, its linear + bias): y [M,N] = bf16(bf16(x w^T) + bias)
+ * for M <= 4 rows of x [M,K] against w [N,K], all BF16; bias [N] may be NULL.  A
+ * weight-streaming kernel with fp32 accumulation (fixed order: each lane's 16-byte
+ * chunks in order, then a xor tree over the warp), so a column slice of w gives
+ * bitwise the same columns.  K a multiple of 8, rows 16-byte aligned. */
+int h3_adaln_projection(const h3_tensor *y, const h3_tensor *x, const h3_tensor *w, const h3_tensor *bias,
+                        void *stream);
 
 /* ---------------- model wrapper ops (outside the block loop) ---------------- */
 

@@ -296,11 +296,19 @@ def add_bias(y: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
 
 def adaln_modulation(temb: torch.Tensor, w: BlockWeights, cfg: BlockConfig) -> torch.Tensor:
     """[N*modalities, 6*Hd] BF16 modulation rows of one block: silu(temb) -> bf16,
-    projected by the block's AdaLN linear (tcgen05 GEMM) plus bias
+    projected by the block's AdaLN linear plus bias
     (MiniMaxH3AdaLNProjection::forward, patches/InfiniLM.patch:1260-1279)."""
     activated = ops.silu(temb, dtype=torch.bfloat16)
-    mod = add_bias(ops.linear(activated, w.w_adaln), w.b_adaln)
-    return mod.view(temb.shape[0] * cfg.modalities, 6 * cfg.hidden)
+    return adaln_project(activated, w.w_adaln, w.b_adaln).view(temb.shape[0] * cfg.modalities, 6 * cfg.hidden)
+
+
+def adaln_project(activated: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+    """bf16(bf16(activated W^T) + bias): the weight-streaming kernel for the usual
+    few conditioning rows, else the tcgen05 GEMM and the bias pass.  (The two sum
+    the K products in different orders; every rank takes the same branch.)"""
+    if activated.shape[0] <= ops.ADALN_MAX_ROWS:
+        return ops.adaln_projection(activated, weight, bias)
+    return add_bias(ops.linear(activated, weight), bias)
 
 
 def segments_from_indices(indices) -> list[Segment]:

@@ -36,36 +36,48 @@
 namespace h3 {
 namespace gemm {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int BM = 128, BN = 256, BK = 64;
 constexpr int A_BYTES = BM * BK * 2;  // 16 KB
-constexpr int B_BYTES = BN * BK * 2;  // 32 KB
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int THREADS = 256;
 constexpr uint32_t TMEM_COLS = 512;
 #ifndef H3_GEMM_GROUP_N
 #define H3_GEMM_GROUP_N 8
 #endif
 constexpr int GROUP_N = H3_GEMM_GROUP_N;   // column tiles per raster group
-constexpr int OFF_BAR = STAGES * STAGE_BYTES;
-constexpr int NUM_BARS = 2 * STAGES + 4;
-constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 16 + 1024;
 // EPI_QKV stages each epilogue warp's 32 head rows (8 KB) in shared memory, so that
 // the stores to the destination (often a peer's receive buffer over NVLink) go out
 // as whole 256-byte rows, 16 lanes per row, instead of 16-byte pieces of 32 rows
 constexpr int QKV_STAGE_WARP = 32 * 256;
-constexpr int OFF_QKV_STAGE = (OFF_BAR + NUM_BARS * 8 + 16 + 127) / 128 * 128;
-constexpr int SMEM_BYTES_QKV = OFF_QKV_STAGE + 4 * QKV_STAGE_WARP + 1024;
-static_assert(SMEM_BYTES_QKV <= 232448, "shared memory over the sm_100 per-block limit");
-__host__ __device__ constexpr int smem_bytes(int epi) { return (epi == 3 || epi == 5) ? SMEM_BYTES_QKV : SMEM_BYTES; }
+
+// Shared-memory layout of one CTA.  PAIR: a CTA pair (cluster of 2, tcgen05
+// cta_group::2) owns a 256 x 256 output tile; each CTA loads its own 128 A rows
+// and half (128) of the tile's 256 W rows per K step -- 32 KB instead of 48 KB
+// per CTA, which leaves room for 6 ring slots -- and keeps its 128 output rows
+// in its own TMEM.
+template <bool PAIR>
+struct Cfg {
+    static constexpr int STAGES = PAIR ? 6 : 4;
+    static constexpr int B_ROWS = PAIR ? BN / 2 : BN;   // W rows this CTA loads per K step
+    static constexpr int STAGE_BYTES = A_BYTES + B_ROWS * BK * 2;
+    static constexpr int ROWS = PAIR ? 2 * BM : BM;     // output rows per tile
+    static constexpr int OFF_BAR = STAGES * STAGE_BYTES;
+    static constexpr int NUM_BARS = 2 * STAGES + 4;
+    static constexpr int SMEM = OFF_BAR + NUM_BARS * 8 + 16 + 1024;
+    static constexpr int OFF_QKV_STAGE = (OFF_BAR + NUM_BARS * 8 + 16 + 127) / 128 * 128;
+    static constexpr int SMEM_QKV = OFF_QKV_STAGE + 4 * QKV_STAGE_WARP + 1024;
+    static_assert(SMEM_QKV <= 232448, "shared memory over the sm_100 per-block limit");
+};
+template <bool PAIR>
+__host__ __device__ constexpr int smem_bytes(int epi) {
+    return (epi == 3 || epi == 5) ? Cfg<PAIR>::SMEM_QKV : Cfg<PAIR>::SMEM;
+}
 
 // EPI_GATED_RES_SQ: EPI_GATED_RES, plus the tile's share of the output row's sum
 // of squares for the RMSNorm that follows (sq[row][n] = fp32 sum over the tile's
 // columns, in column order, of bf16(out^2)), so the norm pass needs no reduction.
 // EPI_QKV64: EPI_QKV for 64 rotated pairs (the full-D 44/42/42 RoPE layout).
 enum Epi { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_GATED_RES = 2, EPI_QKV = 3, EPI_GATED_RES_SQ = 4, EPI_QKV64 = 5 };
-constexpr int NUM_EPI = 6;
 constexpr int QKV_HALF = 48;              // rotated pairs per head (3 axes x 16 frequencies)
-constexpr int QKV_HW = QKV_HALF / 2;      // ... as packed BF16x2 words
 
 struct Params {
     int M, N, K;            // N: accumulator columns (weight rows)
@@ -121,21 +133,31 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
     return *reinterpret_cast<uint32_t *>(&v);
 }
 
-template <int EPI>
+template <int EPI, bool PAIR>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, Params p) {
+    using C = Cfg<PAIR>;
+    constexpr int STAGES = C::STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::OFF_BAR);
     uint64_t *full = bars;
     uint64_t *empty = bars + STAGES;
     uint64_t *acc_full = bars + 2 * STAGES;
     uint64_t *acc_empty = acc_full + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + NUM_BARS);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + C::NUM_BARS);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kblocks = p.K / BK;
+    // PAIR: CTA `rank` of the pair; tiles are dealt to pairs.  The leader (rank 0)
+    // holds the ring's full barriers (both CTAs' TMA bytes count there) and the
+    // accumulator-empty barriers (both CTAs' epilogue warps arrive there) and
+    // issues the MMAs; each CTA's empty and accumulator-full barriers get the
+    // leader's commits.
+    const uint32_t rank = PAIR ? cluster_ctarank() : 0;
+    const int first_tile = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+    const int tile_step = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -144,17 +166,23 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&acc_full[a], 1);
-            mbar_init(&acc_empty[a], 128);
+            mbar_init(&acc_empty[a], PAIR ? 8 : 128);   // PAIR: one arrival per epilogue warp of the pair
         }
         *abort_flag = 0;
         fence_mbar_init();
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, TMEM_COLS);
-        tmem_relinquish();
+        if (PAIR) {
+            tmem_alloc_pair(tmem_slot, TMEM_COLS);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(tmem_slot, TMEM_COLS);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
-    __syncthreads();
+    if (PAIR) cluster_sync();   // the peer's barriers are initialised before any remote arrive
+    else __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
@@ -164,29 +192,46 @@ __global__ void __launch_bounds__(THREADS, 1)
             tma_prefetch_desc(&tb);
             uint32_t it = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+            for (int tile = first_tile; tile < p.num_tiles && ok; tile += tile_step) {
                 int m, n;
                 tile_coords(p, tile, m, n);
                 for (int kb = 0; kb < kblocks; ++kb, ++it) {
                     const uint32_t slot = it % STAGES, use = it / STAGES;
                     ok = mbar_wait(&empty[slot], (use & 1) ^ 1, abort_flag);
                     if (!ok) break;
-                    uint8_t *sa = smem + slot * STAGE_BYTES;
-                    mbar_expect_tx(&full[slot], STAGE_BYTES);
-                    tma_load_2d(sa, &ta, &full[slot], kb * BK, m * BM);
-                    tma_load_2d(sa + A_BYTES, &tb, &full[slot], kb * BK, n * BN);
+                    uint8_t *sa = smem + slot * C::STAGE_BYTES;
+                    if (PAIR) {
+                        // both CTAs' bytes complete the leader's barrier, whose arrival
+                        // (with the pair's byte count) the leader makes
+                        const uint32_t fb = mapa_shared(&full[slot], 0);
+                        if (rank == 0) mbar_expect_tx(&full[slot], 2 * C::STAGE_BYTES);
+                        tma_load_2d_pair(sa, &ta, fb, kb * BK, m * C::ROWS + (int)rank * BM);
+                        tma_load_2d_pair(sa + A_BYTES, &tb, fb, kb * BK, n * BN + (int)rank * C::B_ROWS);
+                    } else {
+                        mbar_expect_tx(&full[slot], C::STAGE_BYTES);
+                        tma_load_2d(sa, &ta, &full[slot], kb * BK, m * BM);
+                        tma_load_2d(sa + A_BYTES, &tb, &full[slot], kb * BK, n * BN);
+                    }
                 }
+            }
+            // the leader's last commits arrive on this CTA's empty barriers: wait for
+            // them, so that none lands after the CTA has exited
+            for (uint32_t i = 0; i < STAGES && ok; ++i) {
+                if (it < i + 1) break;
+                const uint32_t u = it - 1 - i;
+                ok = mbar_wait(&empty[u % STAGES], (u / STAGES) & 1, abort_flag);
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN, false);
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t IDESC = idesc_bf16_f32(C::ROWS, BN, false);
             const uint32_t base = smem_u32(smem);
             uint32_t it = 0, lt = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++lt) {
+            for (int tile = first_tile; tile < p.num_tiles && ok; tile += tile_step, ++lt) {
                 const uint32_t acc = lt & 1, use = lt >> 1;
-                ok = mbar_wait(&acc_empty[acc], (use & 1) ^ 1, abort_flag);
+                ok = PAIR ? mbar_wait_cluster(&acc_empty[acc], (use & 1) ^ 1, abort_flag)
+                          : mbar_wait(&acc_empty[acc], (use & 1) ^ 1, abort_flag);
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t d = tmem + acc * BN;
@@ -195,15 +240,28 @@ __global__ void __launch_bounds__(THREADS, 1)
                     ok = mbar_wait(&full[slot], (it / STAGES) & 1, abort_flag);
                     if (!ok) break;
                     tc_fence_after();
-                    const uint32_t sa = base + slot * STAGE_BYTES, sb = sa + A_BYTES;
+                    const uint32_t sa = base + slot * C::STAGE_BYTES, sb = sa + A_BYTES;
 #pragma unroll
-                    for (int kk = 0; kk < BK / 16; ++kk)
-                        umma_ss(d, smem_desc_sw128(sa + kk * 32, 16, 1024), smem_desc_sw128(sb + kk * 32, 16, 1024),
-                                IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
-                    umma_commit(&empty[slot]);
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        const uint64_t da = smem_desc_sw128(sa + kk * 32, 16, 1024);
+                        const uint64_t db = smem_desc_sw128(sb + kk * 32, 16, 1024);
+                        if (PAIR) umma_ss_pair(d, da, db, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+                        else umma_ss(d, da, db, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    if (PAIR) {
+                        umma_commit_pair(smem_u32(&empty[slot]));
+                        umma_commit_pair(mapa_shared(&empty[slot], 1));
+                    } else {
+                        umma_commit(&empty[slot]);
+                    }
                 }
                 if (!ok) break;
-                umma_commit(&acc_full[acc]);
+                if (PAIR) {
+                    umma_commit_pair(smem_u32(&acc_full[acc]));
+                    umma_commit_pair(mapa_shared(&acc_full[acc], 1));
+                } else {
+                    umma_commit(&acc_full[acc]);
+                }
             }
             if (!ok) drain_in_flight();
         }
@@ -212,7 +270,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
         uint32_t lt = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++lt) {
+        for (int tile = first_tile; tile < p.num_tiles; tile += tile_step, ++lt) {
             int m, n;
             tile_coords(p, tile, m, n);
             const uint32_t acc = lt & 1;
@@ -220,7 +278,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (!ok) break;
             tc_fence_after();
             const uint32_t tbase = tmem + acc * BN + lane_off;
-            const int row = m * BM + wq * 32 + lane;
+            const int row0 = m * C::ROWS + (int)rank * BM;   // this CTA's first output row
+            const int row = row0 + wq * 32 + lane;
             const bool row_ok = row < p.M;
             if (EPI == EPI_QKV || EPI == EPI_QKV64) {
                 // the tile's 256 columns are two heads of one part; this thread owns one token
@@ -296,7 +355,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     // chunk c ^ (r & 7): each 8-lane phase of a store or load hits 8 distinct
                     // bank groups), then whole rows out: store q covers rows 2q and 2q + 1 of
                     // the warp, 16 lanes (256 contiguous bytes) per row
-                    const uint32_t stage = smem_u32(smem + OFF_QKV_STAGE + wq * QKV_STAGE_WARP);
+                    const uint32_t stage = smem_u32(smem + C::OFF_QKV_STAGE + wq * QKV_STAGE_WARP);
                     if (row_ok) {
 #pragma unroll
                         for (int q = 0; q < 16; ++q)
@@ -308,7 +367,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll 4
                     for (int q = 0; q < 16; ++q) {
                         const int r = 2 * q + (lane >> 4);
-                        const int grow = m * BM + wq * 32 + r;
+                        const int grow = row0 + wq * 32 + r;
                         if (grow < p.M) {
                             const uint4 v = ld_shared_v4(stage + r * 256 + ((c ^ (r & 7)) << 4));
                             st_global_v4(p.dst[part][dp] + (int64_t)grow * p.drow + (int64_t)hloc * p.dhead + 8 * c,
@@ -395,17 +454,25 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (EPI == EPI_GATED_RES_SQ && row_ok) p.sq[(int64_t)row * p.ldsq + n] = ssq;
             }
             tc_fence_before();
-            mbar_arrive(&acc_empty[acc]);
+            if (PAIR) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(mapa_shared(&acc_empty[acc], 0));
+            } else {
+                mbar_arrive(&acc_empty[acc]);
+            }
         }
         if (!ok) drain_in_flight();
     }
 
+    __syncwarp();
     tc_fence_before();
-    __syncthreads();
+    if (PAIR) cluster_sync();   // neither CTA leaves while the pair's MMAs or arrivals may touch it
+    else __syncthreads();
     if (warp == 1) {
         __syncwarp();
         tc_fence_after();
-        tmem_dealloc(tmem, TMEM_COLS);
+        if (PAIR) tmem_dealloc_pair(tmem, TMEM_COLS);
+        else tmem_dealloc(tmem, TMEM_COLS);
     }
 }
 
@@ -446,29 +513,74 @@ int mat_tmap(CUtensorMap *map, const h3_tensor *t, uint32_t box_rows) {
     return make_tmap_bf16(map, t->data, 2, dims, strides, box);
 }
 
+// Which tile form the projections use: 0 chooses per launch, 1 forces single-CTA
+// 128-row tiles, 2 forces CTA-pair 256-row tiles (h3_gemm_variant).
+std::atomic<int> g_gemm_variant{0};
+
+// The pair form halves each SM's W traffic but pads M to 256 rows: chosen unless
+// that pads more rows than the single form by over 1/64 of the product.
+bool use_pair(int M) {
+    const int v = g_gemm_variant.load();
+    if (v == 1) return false;
+    if (v == 2) return true;
+    const int64_t pad2 = (int64_t)(M + 255) / 256 * 256, pad1 = (int64_t)(M + 127) / 128 * 128;
+    return pad2 * 64 <= pad1 * 65;
+}
+
+template <int EPI, bool PAIR>
+int launch_form(const CUtensorMap &ta, const CUtensorMap &tb, gemm::Params &p, cudaStream_t stream) {
+    using C = gemm::Cfg<PAIR>;
+    constexpr int smem = gemm::smem_bytes<PAIR>(EPI);
+    auto kernel = gemm::gemm_kernel<EPI, PAIR>;
+    p.num_m = (p.M + C::ROWS - 1) / C::ROWS;
+    p.num_n = (p.N + gemm::BN - 1) / gemm::BN;
+    p.num_tiles = p.num_m * p.num_n;
+    // per device: 0 = not set up yet, else 1 + the number of CTAs (single) or
+    // CTA pairs (PAIR) that are resident at once
+    static std::atomic<int> resident[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return H3_ERR_UNSUPPORTED;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(gemm::THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = PAIR ? attr : nullptr;
+    cfg.numAttrs = PAIR ? 1 : 0;
+    if (resident[dev].load() == 0) {
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+            return H3_ERR_LAUNCH;
+        int n = num_sms();
+        if (PAIR) {
+            cfg.gridDim = dim3(2 * (n / 2));
+            int clusters = 0;
+            if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess || clusters < 1)
+                return H3_ERR_LAUNCH;
+            n = clusters;
+        }
+        resident[dev].store(1 + n);
+    }
+    const int slots = resident[dev].load() - 1;
+    const int units = p.num_tiles < slots ? p.num_tiles : slots;
+    cfg.gridDim = dim3(PAIR ? 2 * units : units);
+    if (cudaLaunchKernelEx(&cfg, kernel, ta, tb, p) != cudaSuccess) return H3_ERR_LAUNCH;
+    return launch_status();
+}
+
 template <int EPI>
 int launch_gemm(const h3_tensor *x, const h3_tensor *w, gemm::Params &p, cudaStream_t stream) {
     // an empty product launches nothing (a tensor map cannot describe a zero extent)
     if (p.M == 0 || p.N == 0) return H3_OK;
+    const bool pair = use_pair(p.M);
     CUtensorMap ta, tb;
     H3_CHECK(mat_tmap(&ta, x, gemm::BM));
-    H3_CHECK(mat_tmap(&tb, w, gemm::BN));
-    p.num_m = (p.M + gemm::BM - 1) / gemm::BM;
-    p.num_n = (p.N + gemm::BN - 1) / gemm::BN;
-    p.num_tiles = p.num_m * p.num_n;
-    static std::atomic<bool> attr_set[gemm::NUM_EPI][64];
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64) return H3_ERR_UNSUPPORTED;
-    if (!attr_set[EPI][dev].load()) {
-        if (cudaFuncSetAttribute(gemm::gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 gemm::smem_bytes(EPI)) != cudaSuccess)
-            return H3_ERR_LAUNCH;
-        attr_set[EPI][dev].store(true);
-    }
-    const int grid = p.num_tiles < num_sms() ? p.num_tiles : num_sms();
-    gemm::gemm_kernel<EPI><<<grid, gemm::THREADS, gemm::smem_bytes(EPI), stream>>>(ta, tb, p);
-    return launch_status();
+    H3_CHECK(mat_tmap(&tb, w, pair ? gemm::Cfg<true>::B_ROWS : gemm::Cfg<false>::B_ROWS));
+    return pair ? launch_form<EPI, true>(ta, tb, p, stream) : launch_form<EPI, false>(ta, tb, p, stream);
 }
 
 int check_gemm_operands(const h3_tensor *y, const h3_tensor *x, const h3_tensor *w) {
@@ -680,6 +792,11 @@ extern "C" int h3_pack_gate_up(const h3_tensor *dst, const h3_tensor *src, void 
         static_cast<__nv_bfloat16 *>(dst->data), dst->strides[0], static_cast<const __nv_bfloat16 *>(src->data),
         src->strides[0], F, K);
     return launch_status();
+}
+
+extern "C" int h3_gemm_variant(int variant) {
+    if (variant < 0 || variant > 2) return H3_ERR_BAD_SHAPE;
+    return g_gemm_variant.exchange(variant);
 }
 
 extern "C" unsigned int h3_gemm_device_error_read_and_clear(void) {

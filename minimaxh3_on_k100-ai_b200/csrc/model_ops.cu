@@ -11,6 +11,8 @@
 //   h3_index_copy_rows index_copy of text/video/audio embeddings into the packed
 //                      sequence :1685-1690
 //   h3_silu            op::silu (fp32) followed by cast_to :1267-1268, 1511, 1535
+//   h3_adaln_projection MiniMaxH3AdaLNProjection::forward's linear + bias
+//                      (:1260-1279) for its few conditioning rows
 #include <math.h>
 #include <stdint.h>
 
@@ -124,6 +126,70 @@ __global__ void __launch_bounds__(256) linear_f32_gemv_kernel(LinArgs a) {
             const float v = a.b ? __fadd_rn(acc[m], a.b[n]) : acc[m];
             if (a.y_bf16) static_cast<__nv_bfloat16 *>(a.y)[m * a.sy + n] = __float2bfloat16_rn(v);
             else static_cast<float *>(a.y)[m * a.sy + n] = v;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// AdaLN projection: y[M,N] = bf16(bf16(x[M,K] w[N,K]^T) + b[N]), all BF16, M <=
+// ADALN_ROWS.  The weight (6 x modalities x Hd rows of Hd) is read once and is
+// the whole cost, so this is a streaming kernel: a warp per weight row, each
+// lane 16-byte chunks lane, lane + 32, ... of it (512 contiguous bytes per warp
+// load, ADALN_UNROLL loads in flight per lane), fp32 products accumulated in
+// chunk order per lane, then a xor-16/8/4/2/1 tree.  The grid covers every SM
+// however the rows are split across ranks (a GEMM tile grid over 11520 rows,
+// one rank's share on 8 GPUs, fills 45 SMs).
+// ---------------------------------------------------------------------------
+constexpr int ADALN_ROWS = 4;
+constexpr int ADALN_UNROLL = 5;
+
+struct AdaArgs {
+    const __nv_bfloat16 *x, *w, *b;
+    __nv_bfloat16 *y;
+    int64_t M, N, K, sx, sw, sy;
+};
+
+__global__ void __launch_bounds__(256) adaln_projection_kernel(AdaArgs a) {
+    const int64_t n = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (n >= a.N) return;
+    const uint4 *wr = reinterpret_cast<const uint4 *>(a.w + n * a.sw);
+    const int64_t chunks = a.K / 8;
+    float acc[ADALN_ROWS] = {};
+    for (int64_t c0 = lane; c0 < chunks; c0 += 32 * ADALN_UNROLL) {
+        uint4 wv[ADALN_UNROLL];
+#pragma unroll
+        for (int u = 0; u < ADALN_UNROLL; ++u) {
+            const int64_t c = c0 + 32 * u;
+            if (c < chunks) wv[u] = __ldcs(wr + c);   // streamed once: keep it out of L2's way
+        }
+#pragma unroll
+        for (int u = 0; u < ADALN_UNROLL; ++u) {
+            const int64_t c = c0 + 32 * u;
+            if (c >= chunks) break;
+            const __nv_bfloat16 *we = reinterpret_cast<const __nv_bfloat16 *>(&wv[u]);
+#pragma unroll
+            for (int m = 0; m < ADALN_ROWS; ++m) {
+                if (m < a.M) {
+                    const uint4 xv = __ldg(reinterpret_cast<const uint4 *>(a.x + m * a.sx) + c);
+                    const __nv_bfloat16 *xe = reinterpret_cast<const __nv_bfloat16 *>(&xv);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        acc[m] = fmaf(__bfloat162float(xe[e]), __bfloat162float(we[e]), acc[m]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < ADALN_ROWS; ++m) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc[m] = __fadd_rn(acc[m], __shfl_xor_sync(0xffffffffu, acc[m], o));
+    }
+    if (lane == 0) {
+        for (int m = 0; m < ADALN_ROWS && m < a.M; ++m) {
+            float v = __bfloat162float(__float2bfloat16_rn(acc[m]));   // the linear's BF16 output
+            if (a.b) v = __fadd_rn(v, __bfloat162float(a.b[n]));        // + bias, one BF16 rounding
+            a.y[m * a.sy + n] = __float2bfloat16_rn(v);
         }
     }
 }
@@ -248,6 +314,34 @@ extern "C" int h3_linear_f32(const h3_tensor *y, const h3_tensor *x, const h3_te
     }
     const dim3 grid((unsigned)((N + mops::LT - 1) / mops::LT), (unsigned)((M + mops::LT - 1) / mops::LT));
     mops::linear_f32_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(a);
+    return launch_status();
+}
+
+extern "C" int h3_adaln_projection(const h3_tensor *y, const h3_tensor *x, const h3_tensor *w,
+                                   const h3_tensor *bias, void *stream) {
+    H3_CHECK(check_desc(y, H3_BF16));
+    H3_CHECK(check_desc(x, H3_BF16));
+    H3_CHECK(check_desc(w, H3_BF16));
+    if (x->ndim != 2 || w->ndim != 2 || y->ndim != 2) return H3_ERR_BAD_SHAPE;
+    const int64_t M = x->shape[0], K = x->shape[1], N = w->shape[0];
+    if (w->shape[1] != K || y->shape[0] != M || y->shape[1] != N) return H3_ERR_BAD_SHAPE;
+    if (M > mops::ADALN_ROWS) return H3_ERR_UNSUPPORTED;
+    if (bias) {
+        H3_CHECK(check_desc(bias, H3_BF16));
+        if (bias->ndim != 1 || bias->shape[0] != N) return H3_ERR_BAD_SHAPE;
+        if (bias->strides[0] != 1 && N > 1) return H3_ERR_BAD_LAYOUT;
+    }
+    if (!dense_rows_2d(x) || !dense_rows_2d(w) || !dense_rows_2d(y)) return H3_ERR_BAD_LAYOUT;
+    // 16-byte chunks of every weight and input row
+    if (K % 8 != 0 || !aligned16(x->data) || !aligned16(w->data)) return H3_ERR_BAD_LAYOUT;
+    if ((M > 1 && x->strides[0] % 8 != 0) || (N > 1 && w->strides[0] % 8 != 0)) return H3_ERR_BAD_LAYOUT;
+    if (M == 0 || N == 0) return H3_OK;
+    if ((N + 7) / 8 > 0x7fffffff) return H3_ERR_UNSUPPORTED;
+    mops::AdaArgs a{static_cast<const __nv_bfloat16 *>(x->data), static_cast<const __nv_bfloat16 *>(w->data),
+                    bias ? static_cast<const __nv_bfloat16 *>(bias->data) : nullptr,
+                    static_cast<__nv_bfloat16 *>(y->data), M, N, K,
+                    M > 1 ? x->strides[0] : K, N > 1 ? w->strides[0] : K, M > 1 ? y->strides[0] : N};
+    mops::adaln_projection_kernel<<<(unsigned)((N + 7) / 8), 256, 0, (cudaStream_t)stream>>>(a);
     return launch_status();
 }
 

@@ -47,8 +47,20 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
 #ifndef H3_MBAR_SUSPEND_NS
 #define H3_MBAR_SUSPEND_NS 0   // 0: the hardware's default suspend limit for try_wait
 #endif
+// CLUSTER: acquire at cluster scope, for a barrier that a CTA-pair peer arrives on
+template <bool CLUSTER = false>
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
+    if (CLUSTER) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        return ok != 0;
+    }
 #if H3_MBAR_SUSPEND_NS > 0
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -71,15 +83,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // Bounded wait for the phase with the given parity to complete.  Returns false
 // (and flags the device error word) if it did not complete within H3_WAIT_NS,
 // or as soon as another role of the same CTA has raised `*abort`.
+template <bool CLUSTER = false>
 __device__ __forceinline__ bool mbar_wait_ns(uint64_t *bar, uint32_t parity, volatile int *abort,
                                              uint64_t limit_ns) {
     const uint32_t a = smem_u32(bar);
-    if (mbar_try_wait(a, parity)) return true;
+    if (mbar_try_wait<CLUSTER>(a, parity)) return true;
     const uint64_t start = globaltimer();
     while (true) {
 #pragma unroll 1
         for (int i = 0; i < 256; ++i)
-            if (mbar_try_wait(a, parity)) return true;
+            if (mbar_try_wait<CLUSTER>(a, parity)) return true;
         if (abort && *abort) return false;
         if (globaltimer() - start > limit_ns) {
             atomicOr(&g_h3_device_error, 1u);
@@ -90,6 +103,32 @@ __device__ __forceinline__ bool mbar_wait_ns(uint64_t *bar, uint32_t parity, vol
 }
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort = nullptr) {
     return mbar_wait_ns(bar, parity, abort, H3_WAIT_NS);
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, volatile int *abort = nullptr) {
+    return mbar_wait_ns<true>(bar, parity, abort, H3_WAIT_NS);
+}
+
+// ----------------------------------------------------------------------------
+// thread-block clusters (CTA pairs)
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// every thread of every CTA of the cluster (a superset of __syncthreads)
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// the shared::cluster address of the object at the same offset in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t mapa_shared(const void *p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+// arrive on an mbarrier anywhere in the cluster (release at cluster scope)
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 // After an abort: give copies and MMAs already in flight time to land before
@@ -129,6 +168,16 @@ __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, u
         "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
         "[%6];" ::"r"(smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+        : "memory");
+}
+// CTA-pair form: the box lands in this CTA's shared memory and its bytes are
+// counted on the mbarrier at `cluster_bar`, which may be the pair leader's
+__device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *map, uint32_t cluster_bar, int c0,
+                                                 int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+        "%3}], [%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(cluster_bar)
         : "memory");
 }
 // Bring a box of the tensor into L2 ahead of its tma_load_4d (no shared-memory write, no barrier).
@@ -196,6 +245,38 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
 // mbarrier arrives once all previously issued tcgen05 async ops of this thread complete
 __device__ __forceinline__ void umma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// CTA-pair (cta_group::2) forms.  TMEM is allocated by one warp of each CTA of
+// the pair (same warp, same slot offset); the pair leader issues the MMAs, which
+// read A rows [0,128) and B rows [0,N/2) from its own shared memory and the rest
+// from the peer's at the same offsets, and write D rows [0,128) to its TMEM and
+// [128,256) to the peer's.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *dst_smem, uint32_t ncols) {  // whole warp
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {  // whole warp
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {  // whole warp
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void umma_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// arrive on the mbarrier at `cluster_bar` (this CTA's or the peer's) once the
+// pair MMAs issued so far by this thread complete
+__device__ __forceinline__ void umma_commit_pair(uint32_t cluster_bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_bar)
                  : "memory");
 }
 

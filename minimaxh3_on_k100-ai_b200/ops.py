@@ -31,7 +31,7 @@ __all__ = [
     "linear_f32", "linear_f32_", "gather_rows", "gather_rows_", "index_copy_rows_", "silu", "silu_",
     "linear_qkv_norm_rope_", "linear_gated_residual_sq", "h3_rms_modulate_sq_",
     "linear_gated_residual_rms_modulate", "sq_partials_shape", "linear_gated_residual_segmented",
-    "h3_rms_modulate_segmented_",
+    "h3_rms_modulate_segmented_", "adaln_projection", "ADALN_MAX_ROWS",
 ]
 
 
@@ -328,6 +328,21 @@ def linear_gated_residual_rms_modulate(x, weight, residual, gate, norm_weight, s
          desc(weight), desc(r2), desc(g2), desc(norm_weight), desc(sc), desc(sh), float(eps), desc(workspace),
          stream_of(x))
     return residual_out, out
+
+
+ADALN_MAX_ROWS = 4
+
+
+def adaln_projection(x, weight, bias=None, out=None):
+    """[M, N] = bf16(bf16(x W^T) + bias) for M <= 4 conditioning rows (the AdaLN
+    projection's linear + bias, patches/InfiniLM.patch:1260-1279), a
+    weight-streaming kernel; a column slice of W gives bitwise the same columns."""
+    x2 = _flat(x)
+    if out is None:
+        out = torch.empty(x2.shape[0], weight.shape[0], dtype=torch.bfloat16, device=x.device)
+    require_cuda(out, x2, weight, bias)
+    call("h3_adaln_projection", desc(out), desc(x2), desc(weight), desc(bias), stream_of(x))
+    return out
 
 
 # ---------------------------------------------------------------------------

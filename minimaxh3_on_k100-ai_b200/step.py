@@ -19,7 +19,7 @@ from dataclasses import dataclass, field
 import torch
 
 from . import _lib, ops
-from .block import (BlockConfig, Segment, Workspace, adaln_modulation, add_bias, block_forward,
+from .block import (BlockConfig, Segment, Workspace, adaln_modulation, adaln_project, block_forward,
                     random_block_weights, random_time_embedder, segments_from_indices, time_embedding)
 from .health import bounded_collective, bounded_sync
 from .phases import mark
@@ -149,7 +149,7 @@ class BlockStack:
             return [adaln_modulation(temb, w, bc) for w in self.weights]
         import torch.distributed as dist
         activated = ops.silu(temb, dtype=torch.bfloat16)
-        local = torch.stack([add_bias(ops.linear(activated, w.w_adaln), w.b_adaln) for w in self.weights])
+        local = torch.stack([adaln_project(activated, w.w_adaln, w.b_adaln) for w in self.weights])
         gathered = torch.empty((self.world,) + tuple(local.shape), dtype=local.dtype, device=local.device)
         if local.is_cuda and torch.cuda.is_current_stream_capturing():
             dist.all_gather_into_tensor(gathered, local, group=self.group)   # recorded into the graph

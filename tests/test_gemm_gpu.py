@@ -164,3 +164,79 @@ def test_qkv_norm_rope_epilogue_equals_unfused(T, H, K, ndst, sections):
         assert torch.equal(outs[1][p], ref_k[:, 0, hs]), f"k block {p}"
         assert torch.equal(outs[2][p], qkv[:, 2, hs]), f"v block {p}"
     assert h3b200.load().h3_device_error() == 0
+
+
+def _with_variant(h3, variant, fn):
+    lib = h3.load()
+    prev = lib.h3_gemm_variant(variant)
+    assert prev in (0, 1, 2)
+    try:
+        out = fn()
+        torch.cuda.synchronize()
+        return out
+    finally:
+        lib.h3_gemm_variant(prev)
+
+
+@pytest.mark.parametrize("M", [1, 100, 128, 129, 256, 300, 1000, 2368, 4736, 18944])
+@pytest.mark.parametrize("epi", ["linear", "swiglu", "gated_sq", "segmented", "qkv"])
+def test_pair_tiles_equal_single_tiles(h3, M, epi):
+    """The CTA-pair form (256-row tiles over two SMs, cta_group::2) gives the same
+    bits as single-CTA 128-row tiles, for every epilogue, M not a multiple of 256
+    included (rows of the peer CTA past M, a tile whose peer rows are all past M)."""
+    from h3b200 import ops
+    torch.manual_seed(M)
+    K = 5120 if M >= 4736 else 512
+    x = torch.randn(M, K, device=DEV).bfloat16()
+    if epi == "linear":
+        w = (torch.randn(768, K, device=DEV) * K ** -0.5).bfloat16()
+        run = lambda: ops.linear(x, w)
+    elif epi == "swiglu":
+        w = ops.pack_gate_up((torch.randn(1024, K, device=DEV) * K ** -0.5).bfloat16())
+        run = lambda: ops.linear_swiglu(x, w)
+    elif epi in ("gated_sq", "segmented"):
+        N = 1280
+        w = (torch.randn(N, K, device=DEV) * K ** -0.5).bfloat16()
+        res = torch.randn(M, N, device=DEV).bfloat16()
+        if epi == "gated_sq":
+            gate = torch.randn(M, N, device=DEV).bfloat16()
+            run = lambda: ops.linear_gated_residual_sq(x, w, res, gate)
+        else:
+            gates = [torch.randn(N, device=DEV).bfloat16() for _ in range(2)]
+            lengths = [M // 3, M - M // 3]
+
+            def run():
+                sq = torch.empty(ops.sq_partials_shape(M, N), dtype=torch.float32, device=DEV)
+                return ops.linear_gated_residual_segmented(x, w, res, gates, lengths, sq=sq), sq
+    else:
+        H = 4
+        w = (torch.randn(3 * H * 128, K, device=DEV) * K ** -0.5).bfloat16()
+        nq = (torch.randn(128, device=DEV) * 0.1 + 1).bfloat16()
+        nk = (torch.randn(128, device=DEV) * 0.1 + 1).bfloat16()
+        table = O.rotary_cache(O.grid_positions(1, 1, M)).to(DEV)
+        cos, sin = table[:, :48], table[:, 48:]
+
+        def run():
+            outs = [[torch.empty(M, H, 128, dtype=torch.bfloat16, device=DEV)] for _ in range(3)]
+            ops.linear_qkv_norm_rope_(outs[0], outs[1], outs[2], x, w, nq, nk, cos, sin, 1e-6)
+            return tuple(o[0] for o in outs)
+    single = _with_variant(h3, 1, run)
+    pair = _with_variant(h3, 2, run)
+    flat = lambda r: r if isinstance(r, tuple) else (r,)
+    for a, b in zip(flat(single), flat(pair)):
+        if isinstance(a, tuple):
+            for u, v in zip(a, b):
+                assert torch.equal(u, v)
+        else:
+            assert torch.equal(a, b)
+    assert h3.load().h3_device_error() == 0
+
+
+def test_gemm_variant_rejects_bad_value(h3):
+    lib = h3.load()
+    prev = lib.h3_gemm_variant(0)
+    try:
+        assert lib.h3_gemm_variant(3) < 0
+        assert lib.h3_gemm_variant(0) == 0
+    finally:
+        lib.h3_gemm_variant(prev)
