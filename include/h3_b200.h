@@ -99,9 +99,9 @@ int h3_selftest_wait_timeout(uint64_t limit_ns, void *stream);
 /* Tile form of the projections (every h3_linear* entry point): 0 = chosen per
  * launch (CTA-pair 256-row tiles unless they pad M by more than 1/64 over
  * 128-row tiles), 1 = single-CTA 128-row tiles, 2 = CTA-pair tiles.  Both forms
- * give bitwise the same results.  Returns the previous setting, or
- * H3_ERR_BAD_SHAPE for a value outside 0..2 (setting unchanged).  A tuning and
- * test hook; no reference counterpart. */
+ * give bitwise the same results.  Returns the previous setting, or -1 for a
+ * value outside 0..2 (setting unchanged).  A tuning and test hook; no reference
+ * counterpart. */
 int h3_gemm_variant(int variant);
 
 /* ---------------- fused pointwise ops (BF16, reference rounding) ---------------- */

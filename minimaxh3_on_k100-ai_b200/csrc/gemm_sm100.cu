@@ -795,7 +795,7 @@ extern "C" int h3_pack_gate_up(const h3_tensor *dst, const h3_tensor *src, void 
 }
 
 extern "C" int h3_gemm_variant(int variant) {
-    if (variant < 0 || variant > 2) return H3_ERR_BAD_SHAPE;
+    if (variant < 0 || variant > 2) return -1;
     return g_gemm_variant.exchange(variant);
 }
 

@@ -236,7 +236,8 @@ def test_gemm_variant_rejects_bad_value(h3):
     lib = h3.load()
     prev = lib.h3_gemm_variant(0)
     try:
-        assert lib.h3_gemm_variant(3) < 0
+        assert lib.h3_gemm_variant(3) == -1
+        assert lib.h3_gemm_variant(-1) == -1
         assert lib.h3_gemm_variant(0) == 0
     finally:
         lib.h3_gemm_variant(prev)
