@@ -22,7 +22,12 @@ from . import _lib, ops
 from .block import (BlockConfig, Segment, Workspace, adaln_modulation, adaln_project, block_forward,
                     random_block_weights, random_time_embedder, segments_from_indices, time_embedding)
 from .health import bounded_collective, bounded_sync
+from . import phases
 from .phases import mark
+
+# the phases that launch the attention kernel (one GPU / tensor parallel, and the
+# sequence-parallel block, whose attention also stores the return rows)
+ATTENTION_PHASES = ("attention", "attention_send")
 from .ulysses import SequenceParallel, local_rows
 
 # token tags video 0, text 1, audio 2 (patches/InfiniLM.patch:137); adaln row = 3 * timestep_index + tag (:1695-1697)
@@ -228,7 +233,7 @@ class DiTStep:
         self.sp = self.stack.sequence_parallel(cfg.tokens, self.local)
         self.timestep = torch.full((1,), cfg.timestep, dtype=torch.float32, device=self.device)
         self.x_dev = torch.empty(self.local, bc.hidden, dtype=torch.bfloat16, device=self.device)
-        self.graph, self.graph_out = None, None
+        self.graph, self.graph_out, self.graph_marks = None, None, []
 
     def modulations(self, timestep: torch.Tensor) -> list[torch.Tensor]:
         """Every block's modulation rows [timesteps*modalities, 6*Hd], computed up
@@ -251,13 +256,23 @@ class DiTStep:
         torch.cuda.synchronize(self.device)
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
-            out = self.forward(self.x_dev)
-        self.graph, self.graph_out = graph, out
+            # event record nodes around each attention launch (2 per block): after a
+            # replay, graph_attention_ms() reads that replay's attention time
+            with phases.capturing(ATTENTION_PHASES) as marks:
+                out = self.forward(self.x_dev)
+        self.graph, self.graph_out, self.graph_marks = graph, out, marks
+
+    def graph_attention_ms(self) -> tuple[float, int]:
+        """(device ms of all attention launches, number of launches) in the last
+        replay of the captured step."""
+        t = phases.totals(self.graph_marks, ATTENTION_PHASES)
+        n = sum(1 for name, _ in self.graph_marks if name in ATTENTION_PHASES)
+        return sum(t.values()), n
 
     def release_graph(self) -> None:
         """Drop the graph (required before destroying a process group whose
         collectives it holds)."""
-        self.graph, self.graph_out = None, None
+        self.graph, self.graph_out, self.graph_marks = None, None, []
 
     def close(self) -> None:
         """Release the peer-exchange buffers (every rank, after the last step)."""
