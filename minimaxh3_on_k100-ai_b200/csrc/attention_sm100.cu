@@ -108,37 +108,6 @@ constexpr int NUM_BARS = 1 + 2 * KSLOTS + 2 * VSLOTS_1 + 4 * NQ;
 constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 16 + 1024;  // + tmem slot, abort flag, alignment slack
 static_assert(SMEM_BYTES <= 232448, "shared memory over the sm_100 per-block limit");
 
-// CTA-pair form (PAIR): a cluster of two CTAs runs M=256 tcgen05.mma.cta_group::2
-// products -- each CTA's two Q tiles are the A rows of its half, and every K and V
-// tile is split between the two: this CTA holds keys [64 r, 64 r + 64) of a K tile
-// (the S product's N half) and dims [64 r, 64 r + 64) of a V tile (the P V
-// product's N half).  Per SM that halves the K/V bytes loaded and the B-operand
-// bytes the tensor core reads from shared memory per product (M=128 N=128 SS
-// products need about the whole shared-memory read port at full rate), and frees
-// 48 KB for deeper K/V rings.
-#ifndef H3_ATTN_PAIR_KSLOTS
-#define H3_ATTN_PAIR_KSLOTS 2
-#endif
-#ifndef H3_ATTN_PAIR_VSLOTS
-#define H3_ATTN_PAIR_VSLOTS 2
-#endif
-template <bool PAIR>
-struct Lay {
-    static constexpr int KROWS = PAIR ? BN / 2 : BN;          // keys of a K tile held by this CTA
-    static constexpr int KTILE = KROWS * HD * 2;              // its bytes: two 64-dim halves
-    static constexpr int KHALF = KTILE / 2;
-    static constexpr int VTILE = PAIR ? TILE / 2 : TILE;      // PAIR: this CTA's 64 of the 128 dims
-    static constexpr int KS = PAIR ? H3_ATTN_PAIR_KSLOTS : KSLOTS;
-    static constexpr int VS = PAIR ? H3_ATTN_PAIR_VSLOTS : VSLOTS;
-    static constexpr int VS1 = PAIR ? VS : VSLOTS_1;          // V barrier pairs
-    static constexpr int OFF_K = OFF_P + NQ * TILE;
-    static constexpr int OFF_V = OFF_K + KS * KTILE;
-    static constexpr int OFF_BAR = OFF_V + VS * VTILE;
-    static constexpr int NUM_BARS = 1 + 2 * KS + 2 * VS1 + 4 * NQ;
-    static constexpr int SMEM = OFF_BAR + NUM_BARS * 8 + 16 + 1024;
-    static_assert(SMEM <= 232448, "shared memory over the sm_100 per-block limit");
-};
-
 struct Params {
     int Sq, Sk, H, B;
     int nkv;
@@ -153,7 +122,6 @@ struct Params {
     int rows_per_dst;
     int64_t d_row, d_head;
     __nv_bfloat16 *dst[H3_EXCHANGE_MAX_RANKS];
-    int units;       // PAIR: CTA pairs per (batch, head), each owning 4 consecutive Q tiles
 };
 
 __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
@@ -234,32 +202,28 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk) {
     return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
-// The work of one CTA on NQT (1 or 2) Q tiles starting at row q0 of (batch b, head h);
-// PAIR (NQT 2 only): one CTA of a cluster pair, the leader (rank 0) issuing the pair's
-// MMAs and holding the barriers they wait on.
-template <int NQT, bool PAIR>
+// The work of one CTA on NQT (1 or 2) Q tiles starting at row q0 of (batch b, head h).
+template <int NQT>
 __device__ __forceinline__ void fa_cta(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv,
                                        const CUtensorMap &to, const Params &p, const int h, const int b,
                                        const int q0) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    using L = Lay<PAIR>;
-    static_assert(!PAIR || NQT == NQ, "the pair form runs two Q tiles per CTA");
     uint8_t *sQ = smem + OFF_Q;
     uint8_t *sP = smem + OFF_P;
-    uint8_t *sK = smem + L::OFF_K;
-    uint8_t *sV = smem + L::OFF_V;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::OFF_BAR);
+    uint8_t *sK = smem + OFF_K;
+    uint8_t *sV = smem + OFF_V;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + OFF_BAR);
     uint64_t *q_full = bars;
     uint64_t *k_full = bars + 1;
-    uint64_t *k_empty = k_full + L::KS;
-    uint64_t *v_full = k_empty + L::KS;
-    uint64_t *v_empty = v_full + L::VS1;
-    uint64_t *s_full = v_empty + L::VS1;    // [t]: S_t(j) in TMEM
+    uint64_t *k_empty = k_full + KSLOTS;
+    uint64_t *v_full = k_empty + KSLOTS;
+    uint64_t *v_empty = v_full + VSLOTS_1;
+    uint64_t *s_full = v_empty + VSLOTS_1;  // [t]: S_t(j) in TMEM
     uint64_t *s_free = s_full + NQ;         // [t]: softmax t has read S_t(j)
     uint64_t *p_ready = s_free + NQ;        // [t]: P_t(j) in shared memory, O_t rescaled
     uint64_t *o_done = p_ready + NQ;        // [t]: P_t(j) V_j has landed in O_t
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + L::NUM_BARS);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + NUM_BARS);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -270,53 +234,34 @@ __device__ __forceinline__ void fa_cta(const CUtensorMap &tq, const CUtensorMap 
     // tile's does not, so a one-tile CTA double-buffers V, its second slot in the
     // unused Q tile 1.  V_j goes to slot vslot(j), its use count there is vuse(j).
     constexpr bool v2 = NQT == 1 && VSLOTS == 1;
-    auto vslot = [&](int j) { return v2 ? (j & 1) : j % L::VS; };
-    auto vuse = [&](int j) { return v2 ? (j >> 1) : j / L::VS; };
-    // PAIR: the leader's barriers count both CTAs' TMA bytes (q/k/v full) and both
-    // CTAs' softmax warps (s_free, p_ready: one arrival per warp); the leader's
-    // commits go to both CTAs' copies of the others
-    const uint32_t rank = PAIR ? cluster_ctarank() : 0;
-    auto lead = [&](uint64_t *bar) { return mapa_shared(bar, 0); };
-    auto commit_all = [&](uint64_t *bar) {
-        if (PAIR) {
-            umma_commit_pair(smem_u32(bar));
-            umma_commit_pair(mapa_shared(bar, 1));
-        } else {
-            umma_commit(bar);
-        }
-    };
+    auto vslot = [&](int j) { return v2 ? (j & 1) : j % VSLOTS; };
+    auto vuse = [&](int j) { return v2 ? (j >> 1) : j / VSLOTS; };
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        for (int i = 0; i < L::KS; ++i) {
+        for (int i = 0; i < KSLOTS; ++i) {
             mbar_init(&k_full[i], 1);
             mbar_init(&k_empty[i], 1);
         }
-        for (int i = 0; i < L::VS1; ++i) {
+        for (int i = 0; i < VSLOTS_1; ++i) {
             mbar_init(&v_full[i], 1);
             mbar_init(&v_empty[i], 1);
         }
         for (int t = 0; t < NQ; ++t) {
             mbar_init(&s_full[t], 1);
-            mbar_init(&s_free[t], PAIR ? 8 : 128);
-            mbar_init(&p_ready[t], PAIR ? 8 : 128);
+            mbar_init(&s_free[t], 128);
+            mbar_init(&p_ready[t], 128);
             mbar_init(&o_done[t], 1);
         }
         *abort_flag = 0;
         fence_mbar_init();
     }
     if (warp == 1) {
-        if (PAIR) {
-            tmem_alloc_pair(tmem_slot, TMEM_COLS);
-            tmem_relinquish_pair();
-        } else {
-            tmem_alloc(tmem_slot, TMEM_COLS);
-            tmem_relinquish();
-        }
+        tmem_alloc(tmem_slot, TMEM_COLS);
+        tmem_relinquish();
     }
     tc_fence_before();
-    if (PAIR) cluster_sync();   // the peer's barriers are initialised before any remote arrive
-    else __syncthreads();
+    __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
@@ -324,127 +269,91 @@ __device__ __forceinline__ void fa_cta(const CUtensorMap &tq, const CUtensorMap 
         if ((warp == 0 || warp == 3) && lane == 0) {
             // -------------------------------------------------------- TMA producers
             const bool kq = warp == 0;   // warp 0: Q and K; warp 3: V
-            // a box into this CTA's shared memory, its bytes counted on `full` (PAIR: the leader's)
-            auto load_box = [&](uint8_t *dst, const CUtensorMap *m, uint64_t *full, int c0, int c1) {
-                if (PAIR) tma_load_4d_pair(dst, m, lead(full), c0, c1, h, b);
-                else tma_load_4d(dst, m, full, c0, c1, h, b);
-            };
             if (kq) {
                 tma_prefetch_desc(&tq);
                 tma_prefetch_desc(&tk);
-                if (rank == 0) mbar_expect_tx(q_full, (PAIR ? 2 : 1) * nq * TILE);
+                mbar_expect_tx(q_full, nq * TILE);
                 for (int t = 0; t < nq; ++t)
-                    for (int hf = 0; hf < 2; ++hf) load_box(sQ + t * TILE + hf * HALF, &tq, q_full, hf * 64, q0 + t * BM);
+                    for (int hf = 0; hf < 2; ++hf)
+                        tma_load_4d(sQ + t * TILE + hf * HALF, &tq, q_full, hf * 64, q0 + t * BM, h, b);
             } else {
                 tma_prefetch_desc(&tv);
             }
-            // this CTA's part of key tile j: K rows (PAIR: its 64 of the 128 keys, both
-            // dim halves), V rows (PAIR: all 128 keys, its dim half)
-            const int krow = PAIR ? (int)rank * L::KROWS : 0;
             // use u of a slot waits for the release of use u - 1
-            auto load_tile = [&](bool is_k, uint8_t *dst, uint64_t *full, uint64_t *empty, int use, int j) -> bool {
+            auto load_tile = [&](const CUtensorMap *m, uint8_t *dst, uint64_t *full, uint64_t *empty, int use,
+                                 int row0) -> bool {
                 if (!mbar_wait(empty, (use & 1) ^ 1, abort_flag)) return false;
-                const int bytes = is_k ? L::KTILE : L::VTILE;
-                if (rank == 0) mbar_expect_tx(full, (PAIR ? 2 : 1) * bytes);
-                if (is_k) {
-                    for (int hf = 0; hf < 2; ++hf) load_box(dst + hf * L::KHALF, &tk, full, hf * 64, j * BN + krow);
-                } else if (PAIR) {
-                    load_box(dst, &tv, full, (int)rank * 64, j * BN);
-                } else {
-                    for (int hf = 0; hf < 2; ++hf) load_box(dst + hf * HALF, &tv, full, hf * 64, j * BN);
-                }
+                mbar_expect_tx(full, TILE);
+                for (int hf = 0; hf < 2; ++hf) tma_load_4d(dst + hf * HALF, m, full, hf * 64, row0, h, b);
                 return true;
             };
             // K/V tiles are requested L2_AHEAD key tiles before their load, so the load
             // itself hits in L2 rather than waiting for HBM (or the other die)
             auto prefetch = [&](int j) {
-                if (kq) {
-                    for (int hf = 0; hf < 2; ++hf) tma_prefetch_l2_4d(&tk, hf * 64, j * BN + krow, h, b);
-                } else if (PAIR) {
-                    tma_prefetch_l2_4d(&tv, (int)rank * 64, j * BN, h, b);
-                } else {
-                    for (int hf = 0; hf < 2; ++hf) tma_prefetch_l2_4d(&tv, hf * 64, j * BN, h, b);
-                }
+                for (int hf = 0; hf < 2; ++hf) tma_prefetch_l2_4d(kq ? &tk : &tv, hf * 64, j * BN, h, b);
             };
             for (int j = 1; j < L2_AHEAD && j < nkv; ++j) prefetch(j);
             bool ok = true;
             for (int j = 0; j < nkv && ok; ++j) {
                 if (j + L2_AHEAD < nkv) prefetch(j + L2_AHEAD);
                 if (kq) {
-                    const int ks = j % L::KS;
-                    ok = load_tile(true, sK + ks * L::KTILE, &k_full[ks], &k_empty[ks], j / L::KS, j);
+                    const int ks = j % KSLOTS;
+                    ok = load_tile(&tk, sK + ks * TILE, &k_full[ks], &k_empty[ks], j / KSLOTS, j * BN);
                 } else {
                     const int vs = vslot(j);
-                    uint8_t *dst = v2 ? (vs ? sQ + TILE : sV) : sV + vs * L::VTILE;
-                    ok = load_tile(false, dst, &v_full[vs], &v_empty[vs], vuse(j), j);
+                    uint8_t *dst = v2 ? (vs ? sQ + TILE : sV) : sV + vs * TILE;
+                    ok = load_tile(&tv, dst, &v_full[vs], &v_empty[vs], vuse(j), j * BN);
                 }
             }
-            if (PAIR) {
-                // the leader's last commits arrive on this CTA's empty barriers: wait for
-                // them, so that none lands after the CTA has exited
-                const int slots = kq ? L::KS : L::VS;
-                for (int i = 0; i < slots && ok; ++i) {
-                    const int j = nkv - 1 - i;
-                    if (j < 0) break;
-                    ok = kq ? mbar_wait(&k_empty[j % L::KS], (j / L::KS) & 1, abort_flag)
-                            : mbar_wait(&v_empty[vslot(j)], vuse(j) & 1, abort_flag);
-                }
-            }
-        } else if ((warp == 1 || warp == 2) && lane == 0 && rank == 0) {
+        } else if ((warp == 1 || warp == 2) && lane == 0) {
             // -------------------------------------------------------- MMA issuers
-            constexpr int MR = PAIR ? 2 * BM : BM;                   // rows of one product
-            constexpr uint32_t ID_S = idesc_bf16_f32(MR, BN, false);  // Q (K-major) x K (K-major)
-            constexpr uint32_t ID_PV = idesc_bf16_f32(MR, HD, true);  // P (K-major) x V (MN-major)
+            constexpr uint32_t ID_S = idesc_bf16_f32(BM, BN, false);  // Q (K-major) x K (K-major)
+            constexpr uint32_t ID_PV = idesc_bf16_f32(BM, HD, true);  // P (K-major) x V (MN-major)
             const uint32_t q_base = smem_u32(sQ), p_base = smem_u32(sP), k_base = smem_u32(sK),
                            v_base = smem_u32(sV);
-            // D[t] = A_t (128 x 128 per CTA, K-major, 128B swizzle) x B (this CTA's rows of it)
+            // D[t] = A_t (128 x 128, K-major, 128B swizzle) x B (128 x 128)
             auto issue = [&](uint32_t d, uint32_t a, uint32_t bsrc, bool pv, bool acc) {
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
                     const uint32_t ka = (kk >> 2) * HALF + (kk & 3) * 32;
                     const uint64_t bdesc = pv ? smem_desc_sw128(bsrc + kk * 2048, HALF, 1024)
-                                              : smem_desc_sw128(bsrc + (kk >> 2) * L::KHALF + (kk & 3) * 32, 16, 1024);
-                    const uint64_t adesc = smem_desc_sw128(a + ka, 16, 1024);
-                    const uint32_t idesc = pv ? ID_PV : ID_S;
-                    if (PAIR) umma_ss_pair(d, adesc, bdesc, idesc, (acc || kk > 0) ? 1u : 0u);
-                    else umma_ss(d, adesc, bdesc, idesc, (acc || kk > 0) ? 1u : 0u);
+                                              : smem_desc_sw128(bsrc + ka, 16, 1024);
+                    umma_ss(d, smem_desc_sw128(a + ka, 16, 1024), bdesc, pv ? ID_PV : ID_S,
+                            (acc || kk > 0) ? 1u : 0u);
                 }
-            };
-            auto wait_lead = [&](uint64_t *bar, uint32_t parity) {   // barriers the peer arrives on
-                return PAIR ? mbar_wait_cluster(bar, parity, abort_flag) : mbar_wait(bar, parity, abort_flag);
             };
             bool ok = true;
             if (warp == 1) {
                 // S_t(j) = Q_t K_j^T, issued as soon as softmax t has read S_t(j-1)
                 ok = mbar_wait(q_full, 0, abort_flag);
                 for (int j = 0; j < nkv && ok; ++j) {
-                    const int ks = j % L::KS;
-                    ok = mbar_wait(&k_full[ks], (j / L::KS) & 1, abort_flag);
+                    const int ks = j % KSLOTS;
+                    ok = mbar_wait(&k_full[ks], (j / KSLOTS) & 1, abort_flag);
                     for (int t = 0; t < nq && ok; ++t) {
-                        if (j > 0) ok = wait_lead(&s_free[t], (j - 1) & 1);
+                        if (j > 0) ok = mbar_wait(&s_free[t], (j - 1) & 1, abort_flag);
                         if (!ok) break;
                         tc_fence_after();
-                        issue(tmem + t * BN, q_base + t * TILE, k_base + ks * L::KTILE, false, false);
-                        commit_all(&s_full[t]);
+                        issue(tmem + t * BN, q_base + t * TILE, k_base + ks * TILE, false, false);
+                        umma_commit(&s_full[t]);
                     }
                     if (!ok) break;
-                    commit_all(&k_empty[ks]);
+                    umma_commit(&k_empty[ks]);
                 }
             } else {
                 // O_t += P_t(j) V_j once softmax t has written P_t(j)
                 for (int j = 0; j < nkv && ok; ++j) {
                     const int vs = vslot(j);
-                    const uint32_t vb = v2 ? (vs ? q_base + TILE : v_base) : v_base + vs * L::VTILE;
+                    const uint32_t vb = v2 ? (vs ? q_base + TILE : v_base) : v_base + vs * TILE;
                     ok = mbar_wait(&v_full[vs], vuse(j) & 1, abort_flag);
                     for (int t = 0; t < nq && ok; ++t) {
-                        ok = wait_lead(&p_ready[t], j & 1);
+                        ok = mbar_wait(&p_ready[t], j & 1, abort_flag);
                         if (!ok) break;
                         tc_fence_after();
                         issue(tmem + O_COL + t * HD, p_base + t * TILE, vb, true, j > 0);
-                        commit_all(&o_done[t]);
+                        umma_commit(&o_done[t]);
                     }
                     if (!ok) break;
-                    commit_all(&v_empty[vs]);
+                    umma_commit(&v_empty[vs]);
                 }
             }
             if (!ok) drain_in_flight();
@@ -472,12 +381,7 @@ __device__ __forceinline__ void fa_cta(const CUtensorMap &tq, const CUtensorMap 
             tmem_ld_wait();
             // S_t(j) is in registers: the tensor core may overwrite it with S_t(j+1)
             tc_fence_before();
-            if (PAIR) {
-                __syncwarp();
-                if (lane == 0) mbar_arrive_cluster(lead(&s_free[t]));
-            } else {
-                mbar_arrive(&s_free[t]);
-            }
+            mbar_arrive(&s_free[t]);
             const int valid = p.Sk - j * BN;
             const bool full = valid >= BN;
             if (!full) {
@@ -553,17 +457,9 @@ __device__ __forceinline__ void fa_cta(const CUtensorMap &tq, const CUtensorMap 
                 for (int q = 0; q < 8; ++q)
                     st_shared_v4(p_tile + hf * HALF + swz(row, q), w[32 * hf + 4 * q], w[32 * hf + 4 * q + 1],
                                  w[32 * hf + 4 * q + 2], w[32 * hf + 4 * q + 3]);
-            if (PAIR) {
-                // the leader's MMA reads this CTA's P tile through the pair
-                fence_proxy_async_all();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive_cluster(lead(&p_ready[t]));
-            } else {
-                fence_proxy_async_smem();
-                tc_fence_before();
-                mbar_arrive(&p_ready[t]);
-            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            mbar_arrive(&p_ready[t]);
         }
         if (ok) ok = mbar_wait(&o_done[t], (nkv - 1) & 1, abort_flag);
         ok = __all_sync(0xffffffffu, ok);
@@ -617,15 +513,12 @@ __device__ __forceinline__ void fa_cta(const CUtensorMap &tq, const CUtensorMap 
         }
     }
 
-    __syncwarp();
     tc_fence_before();
-    if (PAIR) cluster_sync();   // neither CTA leaves while the pair's MMAs or arrivals may touch it
-    else __syncthreads();
+    __syncthreads();
     if (warp == 1) {
         __syncwarp();
         tc_fence_after();
-        if (PAIR) tmem_dealloc_pair(tmem, TMEM_COLS);
-        else tmem_dealloc(tmem, TMEM_COLS);
+        tmem_dealloc(tmem, TMEM_COLS);
     }
 }
 
@@ -648,23 +541,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     tile0 += (pair - hb * p.pairs) * NQ;
     const int left = p.tiles - tile0;   // Q tiles of this head from tile0 on
     if (left <= 0) return;              // second half of a split pair past Sq (uniform over the CTA)
-    if (!single && left >= NQ) fa_cta<NQ, false>(tq, tk, tv, to, p, h, b, tile0 * BM);
-    else fa_cta<1, false>(tq, tk, tv, to, p, h, b, tile0 * BM);
-}
-
-// CTA-pair form: cluster u of 2 owns Q tiles [4 u', 4 u' + 4) of its (batch, head)
-// (u' = u modulo p.units); CTA rank r takes tiles 4 u' + 2 r and + 1.  A tile past Sq
-// is still computed (its rows load as zeros and are never stored): both CTAs of a
-// pair take part in every product.
-__global__ void __launch_bounds__(THREADS, 1)
-    fa_fwd_pair_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                       const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap to, Params p) {
-    const int unit = (int)(blockIdx.x >> 1);
-    const int rank = (int)cluster_ctarank();
-    const int hb = unit / p.units;
-    const int h = hb % p.H, b = hb / p.H;
-    const int tile0 = (unit - hb * p.units) * 4 + rank * NQ;
-    fa_cta<NQ, true>(tq, tk, tv, to, p, h, b, tile0 * BM);
+    if (!single && left >= NQ) fa_cta<NQ>(tq, tk, tv, to, p, h, b, tile0 * BM);
+    else fa_cta<1>(tq, tk, tv, to, p, h, b, tile0 * BM);
 }
 
 }  // namespace attn
@@ -700,12 +578,6 @@ int check_attn_operand(const h3_tensor *t) {
 
 namespace {
 
-// Which form the attention launches use: 0 chosen per launch, 1 one CTA per SM
-// (pairs of Q tiles, a short last wave as one-tile CTAs), 2 CTA pairs (h3_attention_variant).
-std::atomic<int> g_attn_variant{0};
-
-bool attn_use_pair() { return g_attn_variant.load() != 1; }
-
 // Shared launcher: `out` is the output view, or null with p.ndst > 0 (scatter).
 int launch_mha(const h3_tensor *out, const h3_tensor *q, const h3_tensor *k, const h3_tensor *v, float scale,
                attn::Params &p, cudaStream_t stream) {
@@ -721,10 +593,9 @@ int launch_mha(const h3_tensor *out, const h3_tensor *q, const h3_tensor *k, con
     const int B = (int)q->shape[0], Sq = (int)q->shape[1], H = (int)q->shape[2], Sk = (int)k->shape[1];
     if (B == 0 || Sq == 0 || H == 0) return H3_OK;
     if (Sk == 0) return H3_ERR_BAD_SHAPE;
-    const bool pair = attn_use_pair();
     CUtensorMap tq, tk, tv, to;
     H3_CHECK(attn_tmap(&tq, q, attn::BM));
-    H3_CHECK(attn_tmap(&tk, k, pair ? attn::Lay<true>::KROWS : attn::BN));
+    H3_CHECK(attn_tmap(&tk, k, attn::BN));
     H3_CHECK(attn_tmap(&tv, v, attn::BN));
     if (out) H3_CHECK(attn_tmap(&to, out, attn::BM));
     else to = tq;   // unused by the scatter epilogue
@@ -734,39 +605,10 @@ int launch_mha(const h3_tensor *out, const h3_tensor *q, const h3_tensor *k, con
     p.B = B;
     p.nkv = (Sk + attn::BN - 1) / attn::BN;
     p.scale_log2 = scale * 1.4426950408889634f;
+    static std::atomic<bool> attr_set[64];
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return H3_ERR_UNSUPPORTED;
-    p.tiles = (Sq + attn::BM - 1) / attn::BM;
-    if (pair) {
-        static std::atomic<bool> pair_attr[64];
-        constexpr int smem = attn::Lay<true>::SMEM;
-        if (!pair_attr[dev].load()) {
-            if (cudaFuncSetAttribute(attn::fa_fwd_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-                cudaSuccess)
-                return H3_ERR_LAUNCH;
-            pair_attr[dev].store(true);
-        }
-        p.units = (p.tiles + 2 * attn::NQ - 1) / (2 * attn::NQ);
-        const int64_t ctas = 2 * (int64_t)p.units * H * B;
-        if (ctas > (int64_t)0x7fffffff) return H3_ERR_UNSUPPORTED;
-        cudaLaunchConfig_t cfg = {};
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 2;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = 1;
-        cfg.gridDim = dim3((unsigned)ctas);
-        cfg.blockDim = dim3(attn::THREADS);
-        cfg.dynamicSmemBytes = smem;
-        cfg.stream = stream;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        if (cudaLaunchKernelEx(&cfg, attn::fa_fwd_pair_kernel, tq, tk, tv, to, p) != cudaSuccess)
-            return H3_ERR_LAUNCH;
-        return launch_status();
-    }
-    static std::atomic<bool> attr_set[64];
     if (!attr_set[dev].load()) {
         if (cudaFuncSetAttribute(attn::fa_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  attn::SMEM_BYTES) != cudaSuccess)
@@ -774,6 +616,7 @@ int launch_mha(const h3_tensor *out, const h3_tensor *q, const h3_tensor *k, con
         attr_set[dev].store(true);
     }
     const int sms = num_sms();
+    p.tiles = (Sq + attn::BM - 1) / attn::BM;
     p.pairs = (p.tiles + attn::NQ - 1) / attn::NQ;
     const int64_t npairs = (int64_t)p.pairs * H * B;
     // one CTA per SM: a last wave of r <= SMs/2 pairs finishes sooner as 2r one-tile CTAs
@@ -821,11 +664,6 @@ extern "C" int h3_mha_scatter(const h3_tensor *dsts, int32_t ndst, const h3_tens
     p.d_row = d0->strides[0];
     p.d_head = d0->strides[1];
     return launch_mha(nullptr, q, k, v, scale, p, (cudaStream_t)stream);
-}
-
-extern "C" int h3_attention_variant(int variant) {
-    if (variant < 0 || variant > 2) return -1;
-    return g_attn_variant.exchange(variant);
 }
 
 // device error word of this translation unit (bounded waits in the attention kernel)

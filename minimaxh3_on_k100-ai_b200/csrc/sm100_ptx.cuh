@@ -145,9 +145,6 @@ __device__ __forceinline__ void drain_in_flight() {
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
-// this thread's generic-proxy writes, in any state space, before later async-proxy
-// accesses (e.g. a CTA-pair MMA issued by the peer CTA reading this CTA's tile)
-__device__ __forceinline__ void fence_proxy_async_all() { asm volatile("fence.proxy.async;" ::: "memory"); }
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
@@ -181,14 +178,6 @@ __device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *m
         "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
         "%3}], [%4];" ::"r"(smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(cluster_bar)
-        : "memory");
-}
-__device__ __forceinline__ void tma_load_4d_pair(void *dst, const CUtensorMap *map, uint32_t cluster_bar, int c0,
-                                                 int c1, int c2, int c3) {
-    asm volatile(
-        "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
-        "%3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(cluster_bar)
         : "memory");
 }
 // Bring a box of the tensor into L2 ahead of its tma_load_4d (no shared-memory write, no barrier).

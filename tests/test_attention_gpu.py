@@ -127,32 +127,12 @@ def test_bad_shapes(h3):
         h3.mha(q, q, q)
 
 
-class _variant:
-    """Run the attention launches in one form (0 per launch, 1 one CTA per SM, 2 CTA pairs)."""
-
-    def __init__(self, h3, v):
-        self.lib, self.v = h3.load(), v
-
-    def __enter__(self):
-        self.prev = self.lib.h3_attention_variant(self.v)
-        assert self.prev in (0, 1, 2)
-
-    def __exit__(self, *exc):
-        self.lib.h3_attention_variant(self.prev)
-
-
 def test_one_tile_ctas_equal_pairs(h3):
     """When the grid's last wave would hold at most half as many Q-tile pairs as
-    there are SMs, those pairs run as one-tile CTAs (the one-CTA-per-SM form).
-    158 heads of two tiles put the last 10 pairs (on a 148-SM B200) in one-tile
-    CTAs, and every single-head call of two tiles runs one-tile CTAs; each tile's
-    arithmetic is the same either way, so every head agrees bitwise with its
-    single-head call."""
-    with _variant(h3, 1):
-        _one_tile_ctas_equal_pairs(h3)
-
-
-def _one_tile_ctas_equal_pairs(h3):
+    there are SMs, those pairs run as one-tile CTAs.  158 heads of two tiles put
+    the last 10 pairs (on a 148-SM B200) in one-tile CTAs, and every single-head
+    call of two tiles runs one-tile CTAs; each tile's arithmetic is the same
+    either way, so every head agrees bitwise with its single-head call."""
     torch.manual_seed(31)
     Sq, Sk, H = 256, 1000, 158
     q = torch.randn(1, Sq, H, 128, dtype=torch.bfloat16, device=DEV)
@@ -168,36 +148,3 @@ def _one_tile_ctas_equal_pairs(h3):
     out3 = h3.mha(q3, k, v)
     assert torch.equal(out3, out[:, :129])
     assert h3.load().h3_device_error() == 0
-
-
-@pytest.mark.parametrize("B,Sq,Sk,H", [(1, 128, 128, 1), (1, 200, 136, 3), (2, 333, 333, 2), (1, 1000, 777, 2),
-                                       (1, 130, 40, 2), (1, 64, 100, 1), (1, 513, 1000, 5),
-                                       (1, 4736, 4736, 5), (1, 18944, 18944, 2)])
-def test_pair_ctas_equal_single_ctas(h3, B, Sq, Sk, H):
-    """The CTA-pair form (M=256 cta_group::2 products, each CTA holding half of every
-    K and V tile) gives the same bits as one CTA per SM, for Q tiles past Sq inside a
-    pair's four, key counts that are not whole tiles, and several heads and batches."""
-    torch.manual_seed(B * 7 + Sq + Sk + H)
-    q = torch.randn(B, Sq, H, 128, dtype=torch.bfloat16, device=DEV)
-    k = torch.randn(B, Sk, H, 128, dtype=torch.bfloat16, device=DEV)
-    v = torch.randn(B, Sk, H, 128, dtype=torch.bfloat16, device=DEV)
-    with _variant(h3, 1):
-        single = h3.mha(q, k, v)
-        torch.cuda.synchronize()
-    with _variant(h3, 2):
-        pair = h3.mha(q, k, v)
-        torch.cuda.synchronize()
-    assert torch.equal(single, pair)
-    rows = torch.linspace(0, Sq - 1, min(Sq, 64), device=DEV).long()
-    _check(pair, q, k, v, rows=rows, mean_err=1e-3)
-    assert h3.load().h3_device_error() == 0
-
-
-def test_attention_variant_rejects_bad_value(h3):
-    lib = h3.load()
-    prev = lib.h3_attention_variant(0)
-    try:
-        assert lib.h3_attention_variant(3) == -1
-        assert lib.h3_attention_variant(0) == 0
-    finally:
-        lib.h3_attention_variant(prev)
