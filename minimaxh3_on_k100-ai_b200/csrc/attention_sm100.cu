@@ -39,7 +39,12 @@
 // the softmax of tile t waits for two products after its own, so the two Q tiles
 // cannot keep the tensor pipe fed; 64-key tiles with double-buffered S (N=64
 // MMAs run at half rate), a shared P tile, alternating the two softmax groups'
-// exponentials, and moving exponentials to the FMA pipe were all slower.
+// exponentials, and moving exponentials to the FMA pipe were all slower.  So was
+// a CTA-pair form (clusters of 2, tcgen05 cta_group::2 M=256 products, each CTA
+// holding half of every K and V tile, which halves the B-operand bytes the tensor
+// core reads from shared memory): 824 TFLOP/s against 1199-1235, with 2 or 3 ring
+// slots for K and V alike -- every key tile's S and P V products then wait on
+// both CTAs' softmax warps through barriers on the other SM.
 //
 // The running max is updated lazily (only when it grows by more than 2^8 in the
 // exp2 domain), so O is rescaled rarely.  Numerator and denominator use the same
