@@ -54,9 +54,6 @@ def parse():
     p.add_argument("--gemm-variant", type=int, choices=[0, 1, 2], default=0,
                    help="projection tile form: 0 chosen per launch (default), 1 single-CTA 128-row tiles, "
                         "2 CTA-pair 256-row tiles")
-    p.add_argument("--attn-variant", type=int, choices=[0, 1, 2], default=0,
-                   help="attention form: 0 chosen per launch (default), 1 one softmax thread per row, "
-                        "2 two softmax threads per row")
     return p.parse_args()
 
 
@@ -852,10 +849,9 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.impl == "ours" and (args.gemm_variant or args.attn_variant):
+    if args.impl == "ours" and args.gemm_variant:
         import h3b200
         h3b200.load().h3_gemm_variant(args.gemm_variant)
-        h3b200.load().h3_attention_variant(args.attn_variant)
     if args.workload != "step" and args.impl == "ours":
         if rank == 0:
             runner = {"attention": run_attention, "pointwise": run_pointwise, "gemm": run_gemm}[args.workload]

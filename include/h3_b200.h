@@ -104,13 +104,6 @@ int h3_selftest_wait_timeout(uint64_t limit_ns, void *stream);
  * counterpart. */
 int h3_gemm_variant(int variant);
 
-/* Form of the attention launches (h3_mha, h3_mha_scatter): 0 = chosen per launch,
- * 1 = one softmax thread per query row (384 threads per CTA), 2 = two softmax
- * threads per row, each on half the keys (640 threads).  Both forms give bitwise
- * the same results.  Returns the previous setting, or -1 for a value outside 0..2
- * (setting unchanged).  A tuning and test hook; no reference counterpart. */
-int h3_attention_variant(int variant);
-
 /* ---------------- fused pointwise ops (BF16, reference rounding) ---------------- */
 
 /* y = staged-BF16 RMSNorm(x) * weight over the last axis.  x, y [S,C] or [B,S,C]; weight [C]. */

@@ -51,7 +51,6 @@ SIGNATURES = {
     "h3_device_error": [],
     "h3_selftest_wait_timeout": [ctypes.c_uint64, _V],
     "h3_gemm_variant": [ctypes.c_int],
-    "h3_attention_variant": [ctypes.c_int],
     "h3_adaln_projection": [P, P, P, P, _V],
     "h3_rms_norm": [P, P, P, _F, _V],
     "h3_swiglu": [P, P, P, _V],

@@ -102,6 +102,35 @@ constexpr float RESCALE_THRESHOLD = 8.0f;     // log2 domain
 #define H3_ATTN_POLY_PAIRS 0   // measured fastest on B200 (the softmax warps are latency-bound)
 #endif
 constexpr int POLY_PAIRS = H3_ATTN_POLY_PAIRS; // of every 8 key pairs, exponentiated on the FMA pipe
+#ifndef H3_ATTN_SUM_GROUPS
+#define H3_ATTN_SUM_GROUPS 2
+#endif
+// The row sum of a key tile is taken in SUM_GROUPS groups of consecutive key pairs,
+// each with two packed fp32x2 accumulators (even / odd pairs), and each group keeps
+// its own running sum across key tiles; short addition chains leave the scheduler
+// room to overlap the exponentials (measured: one group of 64 pairs ran ~1200-1235
+// TFLOP/s at [1,40,18432,128], two groups of 32 ~1315)
+constexpr int SUM_GROUPS = H3_ATTN_SUM_GROUPS;
+constexpr int GROUP_PAIRS = BN / 2 / SUM_GROUPS;
+#ifndef H3_ATTN_MAX_BF16
+#define H3_ATTN_MAX_BF16 0
+#endif
+// Register split (setmaxnreg): the load / MMA warpgroup gives registers to the two
+// softmax warpgroups.  0 = off.  CTRL_REGS * 128 + 2 * SOFTMAX_REGS * 128 may not
+// exceed the registers the CTA is launched with (its per-thread count x 384); the
+// host checks that before the first launch, since a setmaxnreg.inc that the pool
+// cannot satisfy waits forever.
+#ifndef H3_ATTN_SOFTMAX_REGS
+#define H3_ATTN_SOFTMAX_REGS 0
+#endif
+#ifndef H3_ATTN_CTRL_REGS
+#define H3_ATTN_CTRL_REGS 40
+#endif
+constexpr int SOFTMAX_REGS = H3_ATTN_SOFTMAX_REGS;
+constexpr int CTRL_REGS = H3_ATTN_CTRL_REGS;
+static_assert(SOFTMAX_REGS == 0 || (SOFTMAX_REGS % 8 == 0 && CTRL_REGS % 8 == 0 && CTRL_REGS >= 24 &&
+                                    SOFTMAX_REGS <= 256 && CTRL_REGS * 128 + 2 * SOFTMAX_REGS * 128 <= 65536),
+              "register split out of range");
 
 constexpr int OFF_Q = 0;
 constexpr int OFF_P = OFF_Q + NQ * TILE;
@@ -112,26 +141,6 @@ constexpr int VSLOTS_1 = VSLOTS > 2 ? VSLOTS : 2;  // V barriers: a one-tile CTA
 constexpr int NUM_BARS = 1 + 2 * KSLOTS + 2 * VSLOTS_1 + 4 * NQ;
 constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 16 + 1024;  // + tmem slot, abort flag, alignment slack
 static_assert(SMEM_BYTES <= 232448, "shared memory over the sm_100 per-block limit");
-
-// SPLIT: 16 softmax warps (640 threads), two per row quarter of each Q tile, each
-// taking half the row's keys and O columns -- twice the warps per SM sub-partition
-// to hide the softmax's dependent-instruction latency.  The two halves of a row
-// exchange their maxima each key tile through XMAX (BF16, rounded up; two parity
-// buffers) and at the end their sums through the then idle P tile, with one
-// mbarrier per row quarter (X_BARS); a tile's output staging ends on an mbarrier
-// (E_BARS).  Its shared memory has no room for alignment slack: the kernel checks
-// that the dynamic shared memory starts on a 1024-byte boundary.
-constexpr int THREADS_SPLIT = 640;
-template <bool SPLIT>
-struct Lay {
-    static constexpr int X_BARS = SPLIT ? NQ * 4 : 0;
-    static constexpr int E_BARS = SPLIT ? NQ : 0;
-    static constexpr int NUM_BARS_ALL = NUM_BARS + X_BARS + E_BARS;
-    static constexpr int OFF_XMAX = (OFF_BAR + NUM_BARS_ALL * 8 + 16 + 15) / 16 * 16;
-    static constexpr int XMAX_BYTES = SPLIT ? 2 * NQ * 2 * BM * 2 : 0;   // [parity][tile][half][row] BF16
-    static constexpr int SMEM = SPLIT ? OFF_XMAX + XMAX_BYTES : SMEM_BYTES;
-    static_assert(SMEM <= 232448, "shared memory over the sm_100 per-block limit");
-};
 
 struct Params {
     int Sq, Sk, H, B;
@@ -234,15 +243,13 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk) {
     return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
-// The work of one CTA on NQT (1 or 2) Q tiles starting at row q0 of (batch b, head h);
-// SPLIT: the 640-thread form with two softmax threads per row.
-template <int NQT, bool SPLIT>
+// The work of one CTA on NQT (1 or 2) Q tiles starting at row q0 of (batch b, head h).
+template <int NQT>
 __device__ __forceinline__ void fa_cta(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv,
                                        const CUtensorMap &to, const Params &p, const int h, const int b,
                                        const int q0) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    using L = Lay<SPLIT>;
     uint8_t *sQ = smem + OFF_Q;
     uint8_t *sP = smem + OFF_P;
     uint8_t *sK = smem + OFF_K;
@@ -257,9 +264,7 @@ __device__ __forceinline__ void fa_cta(const CUtensorMap &tq, const CUtensorMap 
     uint64_t *s_free = s_full + NQ;         // [t]: softmax t has read S_t(j)
     uint64_t *p_ready = s_free + NQ;        // [t]: P_t(j) in shared memory, O_t rescaled
     uint64_t *o_done = p_ready + NQ;        // [t]: P_t(j) V_j has landed in O_t
-    uint64_t *x_bar = o_done + NQ;          // SPLIT [t][quarter]: the row halves' exchange
-    uint64_t *e_bar = x_bar + L::X_BARS;    // SPLIT [t]: the output tile is staged
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + L::NUM_BARS_ALL);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + NUM_BARS);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -285,12 +290,10 @@ __device__ __forceinline__ void fa_cta(const CUtensorMap &tq, const CUtensorMap 
         }
         for (int t = 0; t < NQ; ++t) {
             mbar_init(&s_full[t], 1);
-            mbar_init(&s_free[t], SPLIT ? 256 : 128);
-            mbar_init(&p_ready[t], SPLIT ? 256 : 128);
+            mbar_init(&s_free[t], 128);
+            mbar_init(&p_ready[t], 128);
             mbar_init(&o_done[t], 1);
         }
-        for (int i = 0; i < L::X_BARS; ++i) mbar_init(&x_bar[i], 2);   // one arrival per warp
-        for (int i = 0; i < L::E_BARS; ++i) mbar_init(&e_bar[i], 8);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -302,6 +305,10 @@ __device__ __forceinline__ void fa_cta(const CUtensorMap &tq, const CUtensorMap 
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    if (SOFTMAX_REGS > 0) {   // warpgroup-uniform: warps 0-3, 4-7, 8-11
+        if (warp < 4) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(CTRL_REGS));
+        else asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(SOFTMAX_REGS));
+    }
 
     if (warp < 4) {
         if ((warp == 0 || warp == 3) && lane == 0) {
@@ -396,71 +403,53 @@ __device__ __forceinline__ void fa_cta(const CUtensorMap &tq, const CUtensorMap 
             }
             if (!ok) drain_in_flight();
         }
-    } else if (((warp - 4) >> (SPLIT ? 3 : 2)) < nq) {
+    } else if (((warp - 4) >> 2) < nq) {
         // ------------------------------------------------------------ softmax / epilogue
-        // A thread owns a row of its Q tile (SPLIT: half a row, keys and O columns
-        // [64 hh, 64 hh + 64); the two threads of a row agree on its max through
-        // shared memory each key tile).  The row sum is kept per 64-key half (l0,
-        // l1, each in a fixed pair order) in both forms, so they give the same bits.
-        const int t = (warp - 4) >> (SPLIT ? 3 : 2);
-        const int hh = SPLIT ? ((warp - 4) >> 2) & 1 : 0;
-        constexpr int NC = SPLIT ? BN / 2 : BN;      // S columns per thread
+        const int t = (warp - 4) >> 2;
         const int row = (warp & 3) * 32 + lane;
         const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-        const uint32_t s_addr = tmem + t * BN + lane_off + (uint32_t)(hh * NC);
+        const uint32_t s_addr = tmem + t * BN + lane_off;
         const uint32_t o_addr = tmem + O_COL + t * HD + lane_off;
         const uint32_t p_tile = smem_u32(sP + t * TILE);
-        uint16_t *xmax = SPLIT ? reinterpret_cast<uint16_t *>(smem + L::OFF_XMAX) : nullptr;  // [2][NQ][2][128]
-        uint64_t *xb = x_bar + t * 4 + (warp & 3);    // SPLIT: this row quarter's two warps
-        // SPLIT: hand this half's value to the other half of the row and take its
-        // value (exchange k of the row quarter's barrier); `bits` are its upper 16 bits
-        auto exchange = [&](uint32_t bits, int k, bool &okk) -> uint32_t {
-            uint16_t *buf = xmax + ((k & 1) * NQ + t) * 2 * BM;
-            buf[hh * BM + row] = (uint16_t)bits;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(xb);
-            okk = __all_sync(0xffffffffu, mbar_wait(xb, k & 1, abort_flag));
-            return buf[(1 - hh) * BM + row];
-        };
         const float c = p.scale_log2;
-        float m = -INFINITY, l0 = 0.f, l1 = 0.f;
+        float m = -INFINITY;
+        float l[SUM_GROUPS];
+#pragma unroll
+        for (int g = 0; g < SUM_GROUPS; ++g) l[g] = 0.f;
         bool ok = true;
         for (int j = 0; j < nkv; ++j) {
             ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, abort_flag));
             if (!ok) break;
             tc_fence_after();
-            uint32_t s[NC];
-#pragma unroll
-            for (int q = 0; q < NC / 32; ++q)
-                tmem_ld32(s_addr + 32 * q, *reinterpret_cast<uint32_t(*)[32]>(&s[32 * q]));
+            uint32_t s[BN];
+            tmem_ld32(s_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
+            tmem_ld32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
+            tmem_ld32(s_addr + 64, *reinterpret_cast<uint32_t(*)[32]>(&s[64]));
+            tmem_ld32(s_addr + 96, *reinterpret_cast<uint32_t(*)[32]>(&s[96]));
             tmem_ld_wait();
             // S_t(j) is in registers: the tensor core may overwrite it with S_t(j+1)
             tc_fence_before();
             mbar_arrive(&s_free[t]);
-            const int valid = p.Sk - j * BN - hh * NC;
-            const bool full = valid >= NC;
+            const int valid = p.Sk - j * BN;
+            const bool full = valid >= BN;
             if (!full) {
 #pragma unroll
-                for (int i = 0; i < NC; ++i)
+                for (int i = 0; i < BN; ++i)
                     if (i >= valid) s[i] = __float_as_uint(-INFINITY);
             }
             float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
-            for (int i = 0; i < NC; i += 8) {
+            for (int i = 0; i < BN; i += 8) {
                 mx0 = max3f(mx0, __uint_as_float(s[i]), __uint_as_float(s[i + 1]));
                 mx1 = max3f(mx1, __uint_as_float(s[i + 2]), __uint_as_float(s[i + 3]));
                 mx2 = max3f(mx2, __uint_as_float(s[i + 4]), __uint_as_float(s[i + 5]));
                 mx3 = max3f(mx3, __uint_as_float(s[i + 6]), __uint_as_float(s[i + 7]));
             }
-            // the row max rounded up to BF16 (the max only sets the exponent's offset; a
-            // BF16 value lets the two halves of a row agree on it through 2 bytes)
-            float rmax = bf16_round_up(fmaxf(max3f(mx0, mx1, mx2), mx3));
-            if (SPLIT) {
-                const uint32_t other = exchange(__float_as_uint(rmax) >> 16, j, ok);
-                if (!ok) break;
-                rmax = fmaxf(rmax, __uint_as_float(other << 16));
-            }
-            const float mnew = rmax * c;
+#if H3_ATTN_MAX_BF16
+            const float mnew = bf16_round_up(fmaxf(max3f(mx0, mx1, mx2), mx3)) * c;
+#else
+            const float mnew = fmaxf(max3f(mx0, mx1, mx2), mx3) * c;
+#endif
             float alpha = 1.f;
             bool rescale = false;
             if (j == 0) {
@@ -472,14 +461,13 @@ __device__ __forceinline__ void fa_cta(const CUtensorMap &tq, const CUtensorMap 
             }
             const float neg_m = -m;
             const uint64_t c2 = pk2(c, c), nm2 = pk2(neg_m, neg_m);
-            uint32_t w[NC / 2];
-            float hs[NC / 64];   // sums of this thread's 64-key halves
+            uint32_t w[BN / 2];
 #pragma unroll
-            for (int g = 0; g < NC / 64; ++g) {
+            for (int g = 0; g < SUM_GROUPS; ++g) {
                 uint64_t rs0 = pk2(0.f, 0.f), rs1 = pk2(0.f, 0.f);
 #pragma unroll
-                for (int ii = 0; ii < 32; ++ii) {
-                    const int i = 32 * g + ii;
+                for (int ii = 0; ii < GROUP_PAIRS; ++ii) {
+                    const int i = g * GROUP_PAIRS + ii;
                     float x0, x1;   // s * c - m for a key pair, one packed FMA
                     up2(ffma2(pk2(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])), c2, nm2), x0, x1);
                     float p0, p1;
@@ -496,14 +484,7 @@ __device__ __forceinline__ void fa_cta(const CUtensorMap &tq, const CUtensorMap 
                 float r0, r1, r2, r3;
                 up2(rs0, r0, r1);
                 up2(rs1, r2, r3);
-                hs[g] = (r0 + r1) + (r2 + r3);
-            }
-            if (SPLIT) {
-                if (hh == 0) l0 = l0 * alpha + hs[0];
-                else l1 = l1 * alpha + hs[0];
-            } else {
-                l0 = l0 * alpha + hs[0];
-                l1 = l1 * alpha + hs[NC / 64 - 1];
+                l[g] = l[g] * alpha + ((r0 + r1) + (r2 + r3));
             }
             // P_t(j-1) V_{j-1} must have read the P tile (and landed in O_t) before P_t(j)
             // overwrites it or O_t is rescaled
@@ -515,7 +496,7 @@ __device__ __forceinline__ void fa_cta(const CUtensorMap &tq, const CUtensorMap 
             if (__any_sync(0xffffffffu, rescale)) {
                 tc_fence_after();
 #pragma unroll 1
-                for (int cc = hh * (NC / 32); cc < (hh + 1) * (NC / 32); ++cc) {
+                for (int cc = 0; cc < 4; ++cc) {
                     uint32_t o[32];
                     tmem_ld32(o_addr + cc * 32, o);
                     tmem_ld_wait();
@@ -527,35 +508,26 @@ __device__ __forceinline__ void fa_cta(const CUtensorMap &tq, const CUtensorMap 
             }
             // P_t(j): this thread's row, keys [64 hf + 8 q, +8) in 16-byte chunk q of half hf
 #pragma unroll
-            for (int g = 0; g < NC / 64; ++g)
+            for (int hf = 0; hf < 2; ++hf)
 #pragma unroll
                 for (int q = 0; q < 8; ++q)
-                    st_shared_v4(p_tile + (hh + g) * HALF + swz(row, q), w[32 * g + 4 * q], w[32 * g + 4 * q + 1],
-                                 w[32 * g + 4 * q + 2], w[32 * g + 4 * q + 3]);
+                    st_shared_v4(p_tile + hf * HALF + swz(row, q), w[32 * hf + 4 * q], w[32 * hf + 4 * q + 1],
+                                 w[32 * hf + 4 * q + 2], w[32 * hf + 4 * q + 3]);
             fence_proxy_async_smem();
             tc_fence_before();
             mbar_arrive(&p_ready[t]);
         }
         if (ok) ok = mbar_wait(&o_done[t], (nkv - 1) & 1, abort_flag);
         ok = __all_sync(0xffffffffu, ok);
-        if (SPLIT && ok) {
-            // the row sum: both threads of the row add the halves in the same order;
-            // the last P V has read the P tile, which carries the exchange
-            float *lx = reinterpret_cast<float *>(sP + t * TILE);
-            lx[hh * BM + row] = hh == 0 ? l0 : l1;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(xb);
-            ok = __all_sync(0xffffffffu, mbar_wait(xb, nkv & 1, abort_flag));
-            const float other = lx[(1 - hh) * BM + row];
-            if (hh == 0) l1 = other;
-            else l0 = other;
-        }
         if (ok) {
             tc_fence_after();
-            const float inv = 1.0f / (l0 + l1);
+            float lsum = l[0];   // the groups' running sums, in group order
+#pragma unroll
+            for (int g = 1; g < SUM_GROUPS; ++g) lsum += l[g];
+            const float inv = 1.0f / lsum;
             const uint32_t out_tile = smem_u32(sQ + t * TILE);  // Q tile is free once the last PV landed
 #pragma unroll 1
-            for (int cc = hh * (NC / 32); cc < (hh + 1) * (NC / 32); ++cc) {
+            for (int cc = 0; cc < 4; ++cc) {
                 uint32_t o[32];
                 tmem_ld32(o_addr + cc * 32, o);
                 tmem_ld_wait();
@@ -569,39 +541,26 @@ __device__ __forceinline__ void fa_cta(const CUtensorMap &tq, const CUtensorMap 
                                  pack_bf16x2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
                 }
             }
-            // the tile's threads have staged it: SPLIT waits on an mbarrier (bounded),
-            // the one-thread-per-row form on a named barrier
-            constexpr int GT = SPLIT ? 256 : 128;           // threads of the tile
-            const int gid = hh * BM + row;                  // index among them
-            auto tile_staged = [&]() -> bool {
-                if (!SPLIT) {
-                    named_bar_sync(1 + t, 128);
-                    return true;
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&e_bar[t]);
-                return __all_sync(0xffffffffu, mbar_wait(&e_bar[t], 0, abort_flag));
-            };
             if (p.ndst > 0) {
-                // row stores to each row's owner: 16 threads per 256-byte row, GT/16 rows
-                // per pass (two whole rows per warp instruction)
-                if (tile_staged()) {
-                    const int cq = gid & 15;
-                    const uint32_t tile = out_tile + (uint32_t)(cq >> 3) * HALF;
+                // row stores to each row's owner: 16 threads per 256-byte row, 8 rows
+                // per pass of the warpgroup (two whole rows per warp instruction)
+                named_bar_sync(1 + t, 128);
+                const int c = row & 15;
+                const uint32_t tile = out_tile + (uint32_t)(c >> 3) * HALF;
 #pragma unroll 4
-                    for (int k = 0; k < BM / (GT / 16); ++k) {
-                        const int rr = (gid >> 4) + (GT / 16) * k;
-                        const int g = q0 + t * BM + rr;
-                        if (g >= p.Sq) break;   // rows grow with k
-                        const int dq = g / p.rows_per_dst;
-                        const int tl = g - dq * p.rows_per_dst;
-                        const uint4 v = ld_shared_v4(tile + swz(rr, cq & 7));
-                        st_global_v4(p.dst[dq] + (int64_t)tl * p.d_row + (int64_t)h * p.d_head + 8 * cq, v);
-                    }
+                for (int k = 0; k < BM / 8; ++k) {
+                    const int rr = (row >> 4) + 8 * k;
+                    const int g = q0 + t * BM + rr;
+                    if (g >= p.Sq) break;   // rows grow with k
+                    const int dq = g / p.rows_per_dst;
+                    const int tl = g - dq * p.rows_per_dst;
+                    const uint4 v = ld_shared_v4(tile + swz(rr, c & 7));
+                    st_global_v4(p.dst[dq] + (int64_t)tl * p.d_row + (int64_t)h * p.d_head + 8 * c, v);
                 }
             } else {
                 fence_proxy_async_smem();
-                if (tile_staged() && gid == 0 && q0 + t * BM < p.Sq) {
+                named_bar_sync(1 + t, 128);
+                if (row == 0 && q0 + t * BM < p.Sq) {
                     tma_store_4d(&to, sQ + t * TILE, 0, q0 + t * BM, h, b);
                     tma_store_4d(&to, sQ + t * TILE + HALF, 64, q0 + t * BM, h, b);
                     tma_store_commit();
@@ -641,33 +600,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     tile0 += (pair - hb * p.pairs) * NQ;
     const int left = p.tiles - tile0;   // Q tiles of this head from tile0 on
     if (left <= 0) return;              // second half of a split pair past Sq (uniform over the CTA)
-    if (!single && left >= NQ) fa_cta<NQ, false>(tq, tk, tv, to, p, h, b, tile0 * BM);
-    else fa_cta<1, false>(tq, tk, tv, to, p, h, b, tile0 * BM);
-}
-
-// The same mapping for the 640-thread form.
-__global__ void __launch_bounds__(THREADS_SPLIT, 1)
-    fa_fwd_split_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                        const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap to, Params p) {
-    extern __shared__ uint8_t smem_raw[];
-    if (smem_u32(smem_raw) & 1023u) {   // no slack to align within: report, do nothing
-        if (threadIdx.x == 0) atomicOr(&g_h3_device_error, 1u);
-        return;
-    }
-    const int cta = (int)blockIdx.x;
-    const bool single = cta >= p.split_from;
-    int pair = cta, tile0 = 0;
-    if (single) {
-        pair = p.split_from + ((cta - p.split_from) >> 1);
-        tile0 = (cta - p.split_from) & 1;
-    }
-    const int hb = pair / p.pairs;
-    const int h = hb % p.H, b = hb / p.H;
-    tile0 += (pair - hb * p.pairs) * NQ;
-    const int left = p.tiles - tile0;
-    if (left <= 0) return;
-    if (!single && left >= NQ) fa_cta<NQ, true>(tq, tk, tv, to, p, h, b, tile0 * BM);
-    else fa_cta<1, true>(tq, tk, tv, to, p, h, b, tile0 * BM);
+    if (!single && left >= NQ) fa_cta<NQ>(tq, tk, tv, to, p, h, b, tile0 * BM);
+    else fa_cta<1>(tq, tk, tv, to, p, h, b, tile0 * BM);
 }
 
 }  // namespace attn
@@ -703,13 +637,6 @@ int check_attn_operand(const h3_tensor *t) {
 
 namespace {
 
-// Which form the attention launches use: 0 chosen per launch, 1 one softmax thread
-// per row (384 threads), 2 two softmax threads per row (640 threads); both give the
-// same bits (h3_attention_variant).
-std::atomic<int> g_attn_variant{0};
-
-bool attn_use_split() { return g_attn_variant.load() == 2; }
-
 // Shared launcher: `out` is the output view, or null with p.ndst > 0 (scatter).
 int launch_mha(const h3_tensor *out, const h3_tensor *q, const h3_tensor *k, const h3_tensor *v, float scale,
                attn::Params &p, cudaStream_t stream) {
@@ -737,18 +664,22 @@ int launch_mha(const h3_tensor *out, const h3_tensor *q, const h3_tensor *k, con
     p.B = B;
     p.nkv = (Sk + attn::BN - 1) / attn::BN;
     p.scale_log2 = scale * 1.4426950408889634f;
-    const bool split_rows = attn_use_split();
-    auto kernel = split_rows ? attn::fa_fwd_split_kernel : attn::fa_fwd_kernel;
-    const int smem = split_rows ? attn::Lay<true>::SMEM : attn::SMEM_BYTES;
-    const int threads = split_rows ? attn::THREADS_SPLIT : attn::THREADS;
-    static std::atomic<bool> attr_set[2][64];
+    static std::atomic<bool> attr_set[64];
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return H3_ERR_UNSUPPORTED;
-    if (!attr_set[split_rows][dev].load()) {
-        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    if (!attr_set[dev].load()) {
+        if (attn::SOFTMAX_REGS > 0) {
+            // the register split must fit in what the CTA is launched with
+            cudaFuncAttributes fa{};
+            if (cudaFuncGetAttributes(&fa, attn::fa_fwd_kernel) != cudaSuccess) return H3_ERR_LAUNCH;
+            if ((int64_t)fa.numRegs * attn::THREADS < attn::CTRL_REGS * 128 + 2 * attn::SOFTMAX_REGS * 128)
+                return H3_ERR_UNSUPPORTED;
+        }
+        if (cudaFuncSetAttribute(attn::fa_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 attn::SMEM_BYTES) != cudaSuccess)
             return H3_ERR_LAUNCH;
-        attr_set[split_rows][dev].store(true);
+        attr_set[dev].store(true);
     }
     const int sms = num_sms();
     p.tiles = (Sq + attn::BM - 1) / attn::BM;
@@ -761,7 +692,7 @@ int launch_mha(const h3_tensor *out, const h3_tensor *q, const h3_tensor *k, con
     const int64_t ctas = npairs + split;
     if (ctas > (int64_t)0x7fffffff) return H3_ERR_UNSUPPORTED;
     p.split_from = (int)(npairs - split);
-    kernel<<<(unsigned)ctas, threads, smem, stream>>>(tq, tk, tv, to, p);
+    attn::fa_fwd_kernel<<<(unsigned)ctas, attn::THREADS, attn::SMEM_BYTES, stream>>>(tq, tk, tv, to, p);
     return launch_status();
 }
 
@@ -799,11 +730,6 @@ extern "C" int h3_mha_scatter(const h3_tensor *dsts, int32_t ndst, const h3_tens
     p.d_row = d0->strides[0];
     p.d_head = d0->strides[1];
     return launch_mha(nullptr, q, k, v, scale, p, (cudaStream_t)stream);
-}
-
-extern "C" int h3_attention_variant(int variant) {
-    if (variant < 0 || variant > 2) return -1;
-    return g_attn_variant.exchange(variant);
 }
 
 // device error word of this translation unit (bounded waits in the attention kernel)

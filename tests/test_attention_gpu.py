@@ -148,52 +148,3 @@ def test_one_tile_ctas_equal_pairs(h3):
     out3 = h3.mha(q3, k, v)
     assert torch.equal(out3, out[:, :129])
     assert h3.load().h3_device_error() == 0
-
-
-class _variant:
-    """Run the attention launches in one form (0 per launch, 1 one softmax thread
-    per row, 2 two softmax threads per row)."""
-
-    def __init__(self, h3, v):
-        self.lib, self.v = h3.load(), v
-
-    def __enter__(self):
-        self.prev = self.lib.h3_attention_variant(self.v)
-        assert self.prev in (0, 1, 2)
-
-    def __exit__(self, *exc):
-        self.lib.h3_attention_variant(self.prev)
-
-
-@pytest.mark.parametrize("B,Sq,Sk,H", [(1, 128, 128, 1), (1, 200, 136, 3), (2, 333, 333, 2), (1, 1000, 777, 2),
-                                       (1, 130, 40, 2), (1, 64, 100, 1), (1, 300, 64, 1), (1, 256, 1000, 158),
-                                       (1, 4736, 4736, 5), (1, 18944, 18944, 2)])
-def test_split_rows_equal_one_thread_per_row(h3, B, Sq, Sk, H):
-    """Two softmax threads per query row (each on half the keys and O columns,
-    agreeing on the row max through shared memory) give the same bits as one
-    thread per row: key counts that leave a half empty, one-tile tail CTAs (158
-    heads), several heads and batches."""
-    torch.manual_seed(B * 7 + Sq + Sk + H)
-    q = torch.randn(B, Sq, H, 128, dtype=torch.bfloat16, device=DEV)
-    k = torch.randn(B, Sk, H, 128, dtype=torch.bfloat16, device=DEV)
-    v = torch.randn(B, Sk, H, 128, dtype=torch.bfloat16, device=DEV)
-    with _variant(h3, 1):
-        one = h3.mha(q, k, v)
-        torch.cuda.synchronize()
-    with _variant(h3, 2):
-        two = h3.mha(q, k, v)
-        torch.cuda.synchronize()
-    assert torch.equal(one, two)
-    rows = torch.linspace(0, Sq - 1, min(Sq, 64), device=DEV).long()
-    _check(two, q, k, v, rows=rows, mean_err=1e-3)
-    assert h3.load().h3_device_error() == 0
-
-
-def test_attention_variant_rejects_bad_value(h3):
-    lib = h3.load()
-    prev = lib.h3_attention_variant(0)
-    try:
-        assert lib.h3_attention_variant(3) == -1
-        assert lib.h3_attention_variant(0) == 0
-    finally:
-        lib.h3_attention_variant(prev)
