@@ -115,6 +115,14 @@ constexpr int GROUP_PAIRS = BN / 2 / SUM_GROUPS;
 #ifndef H3_ATTN_MAX_BF16
 #define H3_ATTN_MAX_BF16 0
 #endif
+// Measured equal within the pool's run-to-run spread at [1,40,18432,128] (1267-1311
+// TFLOP/s for all four combinations in one call), so the defaults are kept:
+#ifndef H3_ATTN_MAX_ACC
+#define H3_ATTN_MAX_ACC 4      // independent max chains over a row of S (4 or 8)
+#endif
+#ifndef H3_ATTN_EARLY_P
+#define H3_ATTN_EARLY_P 0      // store each row-sum group's P chunks as soon as they are ready
+#endif
 // Register split (setmaxnreg): the load / MMA warpgroup gives registers to the two
 // softmax warpgroups.  0 = off.  CTRL_REGS * 128 + 2 * SOFTMAX_REGS * 128 may not
 // exceed the registers the CTA is launched with (its per-thread count x 384); the
@@ -437,18 +445,24 @@ __device__ __forceinline__ void fa_cta(const CUtensorMap &tq, const CUtensorMap 
                 for (int i = 0; i < BN; ++i)
                     if (i >= valid) s[i] = __float_as_uint(-INFINITY);
             }
-            float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+            // the row max (exact in any order): H3_ATTN_MAX_ACC independent chains
+            constexpr int MA = H3_ATTN_MAX_ACC;
+            float mx[MA];
 #pragma unroll
-            for (int i = 0; i < BN; i += 8) {
-                mx0 = max3f(mx0, __uint_as_float(s[i]), __uint_as_float(s[i + 1]));
-                mx1 = max3f(mx1, __uint_as_float(s[i + 2]), __uint_as_float(s[i + 3]));
-                mx2 = max3f(mx2, __uint_as_float(s[i + 4]), __uint_as_float(s[i + 5]));
-                mx3 = max3f(mx3, __uint_as_float(s[i + 6]), __uint_as_float(s[i + 7]));
-            }
+            for (int k = 0; k < MA; ++k) mx[k] = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < BN; i += 2 * MA)
+#pragma unroll
+                for (int k = 0; k < MA; ++k)
+                    mx[k] = max3f(mx[k], __uint_as_float(s[i + 2 * k]), __uint_as_float(s[i + 2 * k + 1]));
+#pragma unroll
+            for (int w2 = MA / 2; w2 > 0; w2 /= 2)
+#pragma unroll
+                for (int k = 0; k < w2; ++k) mx[k] = fmaxf(mx[k], mx[k + w2]);
 #if H3_ATTN_MAX_BF16
-            const float mnew = bf16_round_up(fmaxf(max3f(mx0, mx1, mx2), mx3)) * c;
+            const float mnew = bf16_round_up(mx[0]) * c;
 #else
-            const float mnew = fmaxf(max3f(mx0, mx1, mx2), mx3) * c;
+            const float mnew = mx[0] * c;
 #endif
             float alpha = 1.f;
             bool rescale = false;
@@ -462,6 +476,33 @@ __device__ __forceinline__ void fa_cta(const CUtensorMap &tq, const CUtensorMap 
             const float neg_m = -m;
             const uint64_t c2 = pk2(c, c), nm2 = pk2(neg_m, neg_m);
             uint32_t w[BN / 2];
+            // P_t(j-1) V_{j-1} must have read the P tile (and landed in O_t) before P_t(j)
+            // overwrites it or O_t is rescaled
+            auto release_p_tile = [&]() -> bool {
+                if (j > 0 && !__all_sync(0xffffffffu, mbar_wait(&o_done[t], (j - 1) & 1, abort_flag))) return false;
+                // tcgen05.ld/st are warp-collective: rescale the whole warp's rows if any needs it
+                if (__any_sync(0xffffffffu, rescale)) {
+                    tc_fence_after();
+#pragma unroll 1
+                    for (int cc = 0; cc < 4; ++cc) {
+                        uint32_t o[32];
+                        tmem_ld32(o_addr + cc * 32, o);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                        tmem_st32(o_addr + cc * 32, o);
+                    }
+                    tmem_st_wait();
+                }
+                return true;
+            };
+            // P_t(j): this thread's row, keys [64 hf + 8 q, +8) in 16-byte chunk q of half hf
+            auto store_p = [&](int hf) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                    st_shared_v4(p_tile + hf * HALF + swz(row, q), w[32 * hf + 4 * q], w[32 * hf + 4 * q + 1],
+                                 w[32 * hf + 4 * q + 2], w[32 * hf + 4 * q + 3]);
+            };
 #pragma unroll
             for (int g = 0; g < SUM_GROUPS; ++g) {
                 uint64_t rs0 = pk2(0.f, 0.f), rs1 = pk2(0.f, 0.f);
@@ -485,34 +526,19 @@ __device__ __forceinline__ void fa_cta(const CUtensorMap &tq, const CUtensorMap 
                 up2(rs0, r0, r1);
                 up2(rs1, r2, r3);
                 l[g] = l[g] * alpha + ((r0 + r1) + (r2 + r3));
+#if H3_ATTN_EARLY_P
+                static_assert(SUM_GROUPS == 2, "early P stores go by 64-key halves");
+                if (g == 0 && !(ok = release_p_tile())) break;
+                store_p(g);
+#endif
             }
-            // P_t(j-1) V_{j-1} must have read the P tile (and landed in O_t) before P_t(j)
-            // overwrites it or O_t is rescaled
-            if (j > 0) {
-                ok = __all_sync(0xffffffffu, mbar_wait(&o_done[t], (j - 1) & 1, abort_flag));
-                if (!ok) break;
-            }
-            // tcgen05.ld/st are warp-collective: rescale the whole warp's rows if any needs it
-            if (__any_sync(0xffffffffu, rescale)) {
-                tc_fence_after();
-#pragma unroll 1
-                for (int cc = 0; cc < 4; ++cc) {
-                    uint32_t o[32];
-                    tmem_ld32(o_addr + cc * 32, o);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                    tmem_st32(o_addr + cc * 32, o);
-                }
-                tmem_st_wait();
-            }
-            // P_t(j): this thread's row, keys [64 hf + 8 q, +8) in 16-byte chunk q of half hf
-#pragma unroll
-            for (int hf = 0; hf < 2; ++hf)
-#pragma unroll
-                for (int q = 0; q < 8; ++q)
-                    st_shared_v4(p_tile + hf * HALF + swz(row, q), w[32 * hf + 4 * q], w[32 * hf + 4 * q + 1],
-                                 w[32 * hf + 4 * q + 2], w[32 * hf + 4 * q + 3]);
+            if (!ok) break;
+#if !H3_ATTN_EARLY_P
+            ok = release_p_tile();
+            if (!ok) break;
+            store_p(0);
+            store_p(1);
+#endif
             fence_proxy_async_smem();
             tc_fence_before();
             mbar_arrive(&p_ready[t]);
