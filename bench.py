@@ -364,6 +364,13 @@ def run_ours(args, rank, world, local_rank, group):
     else:
         gemm = _sp_gemms(ops, ws, w0, t, bc, time_call, step.cos, step.sin)
         norms = _sp_norms(ops, ws, w0, t, bc, time_call)
+    # the HBM reference in the same power state: a 1 GiB device copy timed the same
+    # way right after the step (the measured copy peak is a full-clock burst)
+    copy_src = torch.empty(1 << 29, dtype=torch.bfloat16, device=device)
+    copy_dst = torch.empty_like(copy_src)
+    copy_ms = time_call(lambda: copy_dst.copy_(copy_src))
+    copy_gbs_in_step = 2 * copy_src.numel() * 2 / (copy_ms * 1e-3) / 1e9
+    del copy_src, copy_dst
 
     # device time of one eager step split by phase (every rank runs it; the
     # exchange waits show how long a rank stands waiting for its slowest peer)
@@ -420,11 +427,17 @@ def run_ours(args, rank, world, local_rank, group):
         breakdown[k] = {"ms": round(ms, 3), "tflops": round(fl / (ms * 1e-3) / 1e12, 1),
                         "launches_per_step": args.blocks}
     hbm = pk.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+    from h3b200 import block as _block
+    per_pass = 1 if len(step.segments) <= _block.MAX_SEGMENTS else len(step.segments)   # launches per norm pass
     for k, (ms, nbytes) in norms.items():
         gbs = nbytes / (ms * 1e-3) / 1e9
         breakdown[k] = {"ms": round(ms, 3), "gbs": round(gbs, 1), "frac_of_hbm": round(gbs / hbm, 3),
+                        "frac_of_copy_in_step": round(gbs / copy_gbs_in_step, 3),
                         "bytes_per_launch": int(nbytes),
-                        "launches_per_step": len(step.segments) * (2 * args.blocks - 1 if k == "rms_modulate_sq" else 1)}
+                        "launches_per_step": per_pass * (2 * args.blocks - 1 if k == "rms_modulate_sq" else 1)}
+    breakdown["hbm_copy_in_step"] = {"gbs": round(copy_gbs_in_step, 1), "frac_of_hbm": round(copy_gbs_in_step / hbm, 3),
+                                     "note": "1 GiB device copy (read + write bytes) timed right after the step, "
+                                             "in its power state: the HBM reference for the norm passes beside them"}
     per_block = args.blocks
     phase_line = {n: {"rank0_ms_per_step": round(m, 3), "rank0_ms_per_block": round(m / per_block, 3),
                       "max_ms_per_block": round(x / per_block, 3)}
