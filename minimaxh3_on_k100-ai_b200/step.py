@@ -234,6 +234,11 @@ class DiTStep:
         self.timestep = torch.full((1,), cfg.timestep, dtype=torch.float32, device=self.device)
         self.x_dev = torch.empty(self.local, bc.hidden, dtype=torch.bfloat16, device=self.device)
         self.graph, self.graph_out, self.graph_marks = None, None, []
+        # __call__ copies the host tokens in on a side stream; the step waits for that
+        # copy only where it first reads them (after the AdaLN modulations, which do not),
+        # so the copy overlaps the modulations -- in the captured graph an event wait node
+        self.copy_stream = torch.cuda.Stream(self.device) if self.device.type == "cuda" else None
+        self.tokens_in = torch.cuda.Event(external=True) if self.device.type == "cuda" else None
 
     def modulations(self, timestep: torch.Tensor) -> list[torch.Tensor]:
         """Every block's modulation rows [timesteps*modalities, 6*Hd], computed up
@@ -242,7 +247,10 @@ class DiTStep:
 
     def forward(self, x: torch.Tensor, timestep: torch.Tensor | None = None) -> torch.Tensor:
         ts = self.timestep if timestep is None else timestep
-        return self.stack.run(x, self.modulations(ts), self.segments, self.cos, self.sin, self.cfg.tokens)
+        mods = self.modulations(ts)
+        if self.tokens_in is not None:
+            self.tokens_in.wait(torch.cuda.current_stream(self.device))   # the tokens' copy (if any)
+        return self.stack.run(x, mods, self.segments, self.cos, self.sin, self.cfg.tokens)
 
     def capture(self) -> None:
         """Record ``forward(self.x_dev)`` -- every kernel of the step and, under
@@ -289,7 +297,15 @@ class DiTStep:
 
     def __call__(self, x_host: torch.Tensor, out_host: torch.Tensor | None = None) -> torch.Tensor:
         """End to end: host (pinned) tokens in, host tokens out."""
-        self.x_dev.copy_(x_host, non_blocking=True)
+        if self.copy_stream is not None:
+            # on a side stream, after everything before this call on the step's stream
+            # (the previous step has finished with x_dev); the step waits at first use
+            self.copy_stream.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(self.copy_stream):
+                self.x_dev.copy_(x_host, non_blocking=True)
+                self.tokens_in.record(self.copy_stream)
+        else:
+            self.x_dev.copy_(x_host, non_blocking=True)
         y = self.run()
         if out_host is None:
             out_host = torch.empty(y.shape, dtype=y.dtype, pin_memory=True)
