@@ -97,6 +97,27 @@ def test_step_short_stack(h3):
     assert h3.load().h3_device_error() == 0
 
 
+def test_step_end_to_end_equals_forward(h3):
+    """DiTStep(x_host): the host tokens are copied in on a side stream while the AdaLN
+    modulations run, and the step waits for that copy where it first reads them.  Each
+    call with new host tokens returns exactly forward() of those tokens, eagerly and
+    replayed from the captured graph (whose event wait node carries the ordering)."""
+    from h3b200.block import BlockConfig
+    from h3b200.step import DiTStep, StepConfig
+    cfg = StepConfig(blocks=2, video_grid=(2, 8, 16), cond_tokens=64, block=BlockConfig(hidden=512, heads=4, ffn=1536))
+    step = DiTStep(cfg, DEV, seed=6)
+    torch.manual_seed(1)
+    xs = [torch.randn(cfg.tokens, 512).bfloat16().pin_memory() for _ in range(3)]
+    refs = [step.forward(x.to(DEV)).clone().cpu() for x in xs]
+    for captured in (False, True):
+        if captured:
+            step.capture()
+        for x, ref in zip(xs + xs[::-1], refs + refs[::-1]):
+            assert torch.equal(step(x), ref), f"captured={captured}"
+    step.release_graph()
+    assert h3.load().h3_device_error() == 0
+
+
 def test_graft_entry_smoke():
     """The smoke entry point the driver runs (one small block vs the CPU oracle)."""
     import __graft_entry__
