@@ -52,11 +52,15 @@ constexpr int QKV_STAGE_WARP = 32 * 256;
 // Shared-memory layout of one CTA.  PAIR: a CTA pair (cluster of 2, tcgen05
 // cta_group::2) owns a 256 x 256 output tile; each CTA loads its own 128 A rows
 // and half (128) of the tile's 256 W rows per K step -- 32 KB instead of 48 KB
-// per CTA, which leaves room for 6 ring slots -- and keeps its 128 output rows
-// in its own TMEM.
-template <bool PAIR>
+// per CTA, which leaves room for 6 ring slots (H3_GEMM_PAIR_STAGES without the QKV
+// epilogue's staging rows; 7 measured the same) -- and keeps its 128 output rows in
+// its own TMEM.
+#ifndef H3_GEMM_PAIR_STAGES
+#define H3_GEMM_PAIR_STAGES 6
+#endif
+template <bool PAIR, bool QKV = false>
 struct Cfg {
-    static constexpr int STAGES = PAIR ? 6 : 4;
+    static constexpr int STAGES = PAIR ? (QKV ? 6 : H3_GEMM_PAIR_STAGES) : 4;
     static constexpr int B_ROWS = PAIR ? BN / 2 : BN;   // W rows this CTA loads per K step
     static constexpr int STAGE_BYTES = A_BYTES + B_ROWS * BK * 2;
     static constexpr int ROWS = PAIR ? 2 * BM : BM;     // output rows per tile
@@ -65,11 +69,12 @@ struct Cfg {
     static constexpr int SMEM = OFF_BAR + NUM_BARS * 8 + 16 + 1024;
     static constexpr int OFF_QKV_STAGE = (OFF_BAR + NUM_BARS * 8 + 16 + 127) / 128 * 128;
     static constexpr int SMEM_QKV = OFF_QKV_STAGE + 4 * QKV_STAGE_WARP + 1024;
-    static_assert(SMEM_QKV <= 232448, "shared memory over the sm_100 per-block limit");
+    static_assert((QKV ? SMEM_QKV : SMEM) <= 232448, "shared memory over the sm_100 per-block limit");
 };
+__host__ __device__ constexpr bool is_qkv(int epi) { return epi == 3 || epi == 5; }
 template <bool PAIR>
 __host__ __device__ constexpr int smem_bytes(int epi) {
-    return (epi == 3 || epi == 5) ? Cfg<PAIR>::SMEM_QKV : Cfg<PAIR>::SMEM;
+    return is_qkv(epi) ? Cfg<PAIR, true>::SMEM_QKV : Cfg<PAIR, false>::SMEM;
 }
 
 // EPI_GATED_RES_SQ: EPI_GATED_RES, plus the tile's share of the output row's sum
@@ -136,7 +141,7 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 template <int EPI, bool PAIR>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, Params p) {
-    using C = Cfg<PAIR>;
+    using C = Cfg<PAIR, is_qkv(EPI)>;
     constexpr int STAGES = C::STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
