@@ -384,6 +384,27 @@ def run_ours(args, rank, world, local_rank, group):
     if world > 1:
         torch.distributed.all_reduce(most, op=torch.distributed.ReduceOp.MAX, group=group)
 
+    # the same split inside a graph-replayed step (no host launch gaps): a second
+    # capture of the step with an event record node at every phase mark, replayed
+    # twice; every rank captures and replays it, and it is dropped right after
+    graph_split = None
+    if step.graph is not None:
+        g2 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g2):
+            with _phases.capturing() as g2_marks:
+                step.forward(step.x_dev)
+        sync_all()
+        for _ in range(2):
+            g2.replay()
+        sync_all()
+        g_ms = _phases.totals(g2_marks)
+        del g2
+        g_mine = torch.tensor([g_ms.get(n, 0.0) for n in names], dtype=torch.float64, device=device)
+        g_most = g_mine.clone()
+        if world > 1:
+            torch.distributed.all_reduce(g_most, op=torch.distributed.ReduceOp.MAX, group=group)
+        graph_split = (g_mine.tolist(), g_most.tolist())
+
     # max over ranks
     vals = torch.tensor([dev_s, e2e_s, attn_ms, in_step_attn_ms], dtype=torch.float64, device=device)
     if world > 1:
@@ -442,6 +463,12 @@ def run_ours(args, rank, world, local_rank, group):
     phase_line = {n: {"rank0_ms_per_step": round(m, 3), "rank0_ms_per_block": round(m / per_block, 3),
                       "max_ms_per_block": round(x / per_block, 3)}
                   for n, m, x in zip(names, mine.tolist(), most.tolist())}
+    graph_line = None
+    if graph_split is not None:
+        graph_line = {"note": "one graph-replayed step captured with an event record node at every phase "
+                              "mark: device time between marks, per block, without host launch gaps",
+                      **{n: {"rank0_ms_per_block": round(m / per_block, 3), "max_ms_per_block": round(x / per_block, 3)}
+                         for n, m, x in zip(names, *graph_split)}}
     # model FLOPs of the step: all heads' attention over the joint sequence plus the
     # block GEMMs on all tokens (AdaLN GEMVs excluded)
     attn_total = 4.0 * cfg.tokens * cfg.tokens * bc.head_dim * bc.heads
@@ -467,6 +494,7 @@ def run_ours(args, rank, world, local_rank, group):
         "phases_eager": {"note": "one eager (not graph-replayed) step, device time between phase marks, "
                                  "per block; wait_* = a rank waiting for its peers' exchange flags",
                          **phase_line},
+        "phases_graph": graph_line,
         "cuda_graph": graph_note,
         "clocks": clocks,
     }

@@ -59,12 +59,13 @@ def record(fn: Callable[[], object]) -> dict[str, float]:
 
 
 @contextlib.contextmanager
-def capturing(only: Iterable[str]):
-    """Inside CUDA-graph capture: time the phases named in ``only``.  Yields the
-    list that collects the marks (pass it to ``totals`` after a replay)."""
+def capturing(only: Iterable[str] | None = None):
+    """Inside CUDA-graph capture: time the phases named in ``only`` (None: every
+    phase).  Yields the list that collects the marks (pass it to ``totals`` after
+    a replay)."""
     global _MARKS, _ONLY, _EXTERNAL
     marks: list = []
-    _MARKS, _ONLY, _EXTERNAL = marks, frozenset(only), True
+    _MARKS, _ONLY, _EXTERNAL = marks, (None if only is None else frozenset(only)), True
     try:
         yield marks
         mark("end")

@@ -56,3 +56,11 @@ def test_record_charges_every_phase(fake_events, monkeypatch):
         for name in ("a", "b", "a"):
             phases.mark(name)
     assert phases.record(step) == {"a": 2.0, "b": 1.0}
+
+
+def test_capturing_every_phase(fake_events):
+    with phases.capturing() as marks:
+        for name in ("norm1", "attention", "norm1", "down"):
+            phases.mark(name)
+    assert [n for n, _ in marks] == ["norm1", "attention", "norm1", "down", "end"]
+    assert phases.totals(marks) == {"norm1": 2.0, "attention": 1.0, "down": 1.0}
