@@ -213,7 +213,9 @@ class H3Transformer:
         cos, sin = table[:, :half], table[:, half:]
 
         h = hidden[start:start + local]
-        mods = self.stack.modulations(temb)
+        # the modulation rows any token of the sequence reads (the same set on every rank)
+        used = sorted(set((3 * timestep_indices.cpu() + token_tags.cpu()).tolist()))
+        mods = self.stack.modulations(temb, rows=used)
         h = self.stack.run(h, mods, segments_from_indices(adaln_idx.tolist()), cos, sin, seq)
         normalized = self.output_norm(h, temb, segments_from_indices(ts_idx.tolist()))
         video_all = ops.linear_f32(normalized, w.proj_out_w, w.proj_out_b)

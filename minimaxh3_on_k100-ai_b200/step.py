@@ -145,16 +145,47 @@ class BlockStack:
                                              self.cfg.heads, self.cfg.head_dim, self.device)
         return self._sp[key]
 
-    def modulations(self, temb: torch.Tensor) -> list[torch.Tensor]:
+    def _project_rows(self, activated: torch.Tensor, rows) -> torch.Tensor | None:
+        """This rank's columns of every block's AdaLN projection [blocks, t, n], only
+        the modalities that ``rows`` (rows of the [t*modalities, 6*Hd] table the
+        segments read) name -- the others are left unwritten and never read.  None
+        when every modality is needed or the weight-streaming kernel does not apply."""
+        bc = self.cfg
+        t, mods, width = activated.shape[0], bc.modalities, 6 * bc.hidden
+        if rows is None or t > ops.ADALN_MAX_ROWS:
+            return None
+        needed = sorted({int(r) % mods for r in rows})
+        if len(needed) == mods:
+            return None
+        n = self.weights[0].w_adaln.shape[0]          # this rank's columns: [c0, c0 + n)
+        c0 = self.rank * n if self.world > 1 else 0
+        spans = []
+        for m in needed:
+            a, b = max(m * width, c0), min((m + 1) * width, c0 + n)
+            if a < b:
+                spans.append((a - c0, b - c0))
+        local = torch.empty(len(self.weights), t, n, dtype=torch.bfloat16, device=activated.device)
+        for i, w in enumerate(self.weights):
+            for a, b in spans:
+                ops.adaln_projection(activated, w.w_adaln[a:b], w.b_adaln[a:b], out=local[i, :, a:b])
+        return local
+
+    def modulations(self, temb: torch.Tensor, rows=None) -> list[torch.Tensor]:
         """Every block's modulation rows [timesteps*modalities, 6*Hd], computed up
-        front (the reference's batched AdaLN, patches/InfiniLM.patch:1718-1761)."""
+        front (the reference's batched AdaLN, patches/InfiniLM.patch:1718-1761).
+        ``rows``: the table rows the segments will read (the reference computes every
+        modality's rows; a modality no token uses is skipped -- its rows stay unwritten)."""
         bc = self.cfg
         mark("adaln_modulations")
-        if self.world == 1:
-            return [adaln_modulation(temb, w, bc) for w in self.weights]
-        import torch.distributed as dist
         activated = ops.silu(temb, dtype=torch.bfloat16)
-        local = torch.stack([adaln_project(activated, w.w_adaln, w.b_adaln) for w in self.weights])
+        local = self._project_rows(activated, rows)
+        if self.world == 1:
+            if local is None:
+                return [adaln_modulation(temb, w, bc) for w in self.weights]
+            return [local[i].view(temb.shape[0] * bc.modalities, 6 * bc.hidden) for i in range(local.shape[0])]
+        import torch.distributed as dist
+        if local is None:
+            local = torch.stack([adaln_project(activated, w.w_adaln, w.b_adaln) for w in self.weights])
         gathered = torch.empty((self.world,) + tuple(local.shape), dtype=local.dtype, device=local.device)
         if local.is_cuda and torch.cuda.is_current_stream_capturing():
             dist.all_gather_into_tensor(gathered, local, group=self.group)   # recorded into the graph
@@ -229,6 +260,8 @@ class DiTStep:
         table = ops.h3_rope_cache(pos[idx].to(self.device), power)
         self.cos, self.sin = table[:, :48], table[:, 48:]
         self.segments: list[Segment] = segments_from_indices((3 * 0 + tags[idx]).tolist())
+        # the modulation rows any rank's tokens read (the same set on every rank)
+        self.mod_rows = sorted(set((3 * 0 + tags).tolist()))
         self.ws = self.stack.workspace(self.local)
         self.sp = self.stack.sequence_parallel(cfg.tokens, self.local)
         self.timestep = torch.full((1,), cfg.timestep, dtype=torch.float32, device=self.device)
@@ -243,7 +276,7 @@ class DiTStep:
     def modulations(self, timestep: torch.Tensor) -> list[torch.Tensor]:
         """Every block's modulation rows [timesteps*modalities, 6*Hd], computed up
         front (the reference's batched AdaLN)."""
-        return self.stack.modulations(time_embedding(timestep, self.time))
+        return self.stack.modulations(time_embedding(timestep, self.time), rows=self.mod_rows)
 
     def forward(self, x: torch.Tensor, timestep: torch.Tensor | None = None) -> torch.Tensor:
         ts = self.timestep if timestep is None else timestep

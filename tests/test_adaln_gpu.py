@@ -68,3 +68,21 @@ def test_adaln_projection_rejects(ops):
         ops.adaln_projection(x, w)          # more rows than the kernel serves
     with pytest.raises((RuntimeError, ValueError)):
         ops.adaln_projection(x[:2, :60], w[:, :60])   # K not a multiple of 8
+
+
+@pytest.mark.parametrize("rows", [[0, 1], [1], [2], [0, 3, 4]])
+def test_modulations_of_used_rows_only(ops, rows):
+    """The step's batched AdaLN computes only the modalities its segments read: those
+    rows equal the rows of the full computation bit for bit (t = 2 timesteps)."""
+    from h3b200.block import BlockConfig
+    from h3b200.step import BlockStack
+    bc = BlockConfig(hidden=256, heads=2, ffn=512)
+    stack = BlockStack(bc, 3, DEV, seed=3)
+    temb = torch.randn(2, 256, device=DEV)
+    full = stack.modulations(temb)
+    part = stack.modulations(temb, rows=rows)
+    for f, q in zip(full, part):
+        for r in rows:
+            m = r % bc.modalities
+            for i in range(2):                  # every timestep row of a needed modality
+                assert torch.equal(f[i * bc.modalities + m], q[i * bc.modalities + m])
