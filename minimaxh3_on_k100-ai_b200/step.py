@@ -162,7 +162,11 @@ class BlockStack:
         spans = []
         for m in needed:
             a, b = max(m * width, c0), min((m + 1) * width, c0 + n)
-            if a < b:
+            if a >= b:
+                continue
+            if spans and spans[-1][1] == a - c0:
+                spans[-1] = (spans[-1][0], b - c0)        # adjacent modalities: one launch
+            else:
                 spans.append((a - c0, b - c0))
         local = torch.empty(len(self.weights), t, n, dtype=torch.bfloat16, device=activated.device)
         for i, w in enumerate(self.weights):
